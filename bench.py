@@ -1,0 +1,544 @@
+#!/usr/bin/env python
+"""Benchmark of the FP8/FP4 hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload fp4_decode|fp8_roundtrip|scaled_mm|scaled_mm_rowwise]
+                    [--size S] [--shape I]
+
+Default workload (the one the headline metric is quoted on): FP4 decode of a
+16384x8192 float4_e2m1fn_x2 tensor (uniform bytes, arange(256) prefix) to a
+16384x16384 bf16 tensor times a per-tensor fp32 scale 0.37. One step = one
+decode of the whole tensor. Inputs (128 MiB) plus outputs (512 MiB) exceed the
+126 MB L2, so no flush is needed between steps.
+
+Other workloads (one JSON line each, same keys):
+  fp8_roundtrip      4096x4096 f32 -> e4m3 -> f32 (two kernels per step), four
+                     rotating buffer sets so the 144 MB working set of one
+                     step is not served from L2
+  scaled_mm          torch._scaled_mm e4m3 x e4m3, per-tensor scales, bf16
+                     out, M=N=K=--size (default 8192)
+  scaled_mm_rowwise  rowwise scales, LLM shape --shape 0|1|2 of
+                     (16384,4096,4096), (16384,14336,4096), (16384,4096,14336)
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own full-size
+workload (weak scaling, no collective on the data path); the time is the max
+over ranks of the device-timed region.
+
+`value` is device-resident throughput summed over ranks; `e2e` is the same
+metric through the package's public API with pinned host buffers (host to
+device copy, kernel, device to host copy inside the timed region, pipelined
+over chunks on three streams for the converters).
+
+`--impl reference` times the CPU implementation of the path on the host cores
+with all threads, on rank 0 only: the reference's own kernels are Metal
+compute for Apple GPUs and cannot run here, so the CPU oracle (a C
+restatement of the same conversions) stands in for the converters and a
+float32 dequantise-and-matmul stands in for the GEMM.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(ROOT, "mps-fp8-for-torch-and-comfyui-python-package_b200")
+for _p in (ROOT, PKG_ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------- environment
+def rank_info():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch from an ncu capture summarised in
+    profiles/<name>.md (a line `dram_bytes_per_launch: <int>`), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                try:
+                    return int(float(line.split(":", 1)[1].strip().split()[0]))
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu, self.proc, self.path, self.err = gpu_index, None, None, None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.PIPE, text=True)
+            time.sleep(0.3)
+        except OSError as e:
+            self.proc, self.err = None, str(e)
+
+    def stop(self):
+        if self.proc is None:
+            return {"error": self.err or "nvidia-smi unavailable"}
+        self.proc.terminate()
+        try:
+            _, err = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            err = ""
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 7:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"error": (err or "no samples").strip()[:200]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[0]) for r in rows if num(r[0]) is not None]
+        mx = [num(r[1]) for r in rows if num(r[1]) is not None]
+        reasons = sorted({self.NAMES[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def timed_region(step, steps: int, stream, dist_on: bool):
+    """`steps` steps between barrier + synchronize; device ms, max over ranks."""
+    import torch.distributed as dist
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if dist_on:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return ms
+
+
+def chunked_e2e(chunks, streams, body):
+    """Run body(i, stream_index) for every chunk on rotating streams, joined
+    to the current stream (so events on it bracket the whole pipeline)."""
+    cur = torch.cuda.current_stream()
+    ev = torch.cuda.Event()
+    ev.record(cur)
+    for s in streams:
+        s.wait_event(ev)
+    for i in range(chunks):
+        j = i % len(streams)
+        with torch.cuda.stream(streams[j]):
+            body(i, j)
+    for s in streams:
+        cur.wait_stream(s)
+
+
+# ---------------------------------------------------------------- workloads
+class Fp4Decode:
+    name = "fp4_decode"
+    metric = "fp4_decode_GBps"
+    unit, bound, kernels_per_step = "GB/s", "hbm", 1
+    profile = "fp4_decode_16384x8192_bf16"
+    dtype = "u8->bf16"
+
+    def __init__(self, rank, args):
+        from fp4_fp8_for_torch_mps import _lib as L
+        from fp4_fp8_for_torch_mps import fp8_mps_native as nat
+        from fp4_fp8_for_torch_mps.workloads import FP4_DECODE_SCALE, fp4_decode_input
+        self.L, self.nat, self.scale_v = L, nat, FP4_DECODE_SCALE
+        self.x_host = fp4_decode_input(seed=rank)
+        rows, cols = self.x_host.shape
+        self.rows, self.cols = rows, cols
+        self.x = self.x_host.cuda()
+        self.out = torch.empty(rows, 2 * cols, dtype=torch.bfloat16, device="cuda")
+        self.scale = torch.tensor([FP4_DECODE_SCALE], dtype=torch.float32, device="cuda")
+        self.work = self.x.numel() * 5            # bytes read + written per step
+        self.h2d, self.d2h = self.x.numel(), self.x.numel() * 4
+        self.config = {"workload": "fp4_decode", "shape": [rows, cols], "out": f"bf16[{rows},{2 * cols}]",
+                       "scale": FP4_DECODE_SCALE, "l2": "640 MiB per step > L2, no flush"}
+        self.stream = torch.cuda.current_stream()
+        self.lib = L.lib()
+        # end-to-end buffers: pinned host in/out, 16 row chunks on 3 streams
+        self.h_in = self.x_host.pin_memory()
+        self.h_out = torch.empty(rows, 2 * cols, dtype=torch.bfloat16).pin_memory()
+        self.chunks = 16
+        self.crow = rows // self.chunks
+        self.streams = [torch.cuda.Stream() for _ in range(3)]
+        self.d_in = [torch.empty(self.crow, cols, dtype=torch.uint8, device="cuda") for _ in self.streams]
+        self.d_out = [torch.empty(self.crow, 2 * cols, dtype=torch.bfloat16, device="cuda") for _ in self.streams]
+
+    def step(self):
+        rc = self.lib.fp8b200_decode_fp4(self.x.data_ptr(), self.x.numel(), self.out.data_ptr(), self.L.BF16,
+                                         self.scale.data_ptr(), self.L.SCALE_F32, self.stream.cuda_stream)
+        if rc:
+            self.L.check(rc, "fp4 decode")
+
+    def e2e_step(self):
+        c = self.crow
+
+        def body(i, j):
+            self.d_in[j].copy_(self.h_in[i * c:(i + 1) * c], non_blocking=True)
+            self.nat.fp4_decode(self.d_in[j].view(torch.float4_e2m1fn_x2), torch.bfloat16,
+                                scale=self.scale, out=self.d_out[j])
+            self.h_out[i * c:(i + 1) * c].copy_(self.d_out[j], non_blocking=True)
+        chunked_e2e(self.chunks, self.streams, body)
+
+    def check(self):
+        import numpy as np
+        from oracle import oracle as O
+        ref = O.fp4_decode(self.x_host[-64:].numpy(), 1, self.scale_v)
+        return bool(np.array_equal(ref, self.h_out[-64:].view(torch.int16).numpy().view(np.uint16)))
+
+    @staticmethod
+    def cpu_run(rows=16384, reps=3):
+        from oracle import oracle as O
+        from fp4_fp8_for_torch_mps.workloads import FP4_DECODE_SCALE, fp4_decode_input
+        x = fp4_decode_input(seed=0, rows=rows).numpy()
+        threads = os.cpu_count() or 1
+        O.fp4_decode(x, 1, FP4_DECODE_SCALE, threads=threads)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            O.fp4_decode(x, 1, FP4_DECODE_SCALE, threads=threads)
+        dt = (time.perf_counter() - t0) / reps
+        return x.size * 5 / dt / 1e9, threads, f"{rows}x{x.shape[1]} bytes -> bf16 x 0.37 per pass (oracle, C)"
+
+
+class Fp8RoundTrip:
+    name = "fp8_roundtrip"
+    metric = "fp8_roundtrip_GBps"
+    unit, bound, kernels_per_step = "GB/s", "hbm", 2
+    profile = "fp8_encode_decode_4096x4096"
+    dtype = "f32->e4m3->f32"
+    SETS = 4
+
+    def __init__(self, rank, args):
+        from fp4_fp8_for_torch_mps import _lib as L
+        from fp4_fp8_for_torch_mps import fp8_mps_native as nat
+        from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
+        self.L, self.nat = L, nat
+        self.x_host = fp8_roundtrip_input(seed=rank)
+        n = self.x_host.numel()
+        self.xs = [self.x_host.cuda() for _ in range(self.SETS)]
+        self.codes = [torch.empty(n, dtype=torch.uint8, device="cuda") for _ in range(self.SETS)]
+        self.back = [torch.empty(n, dtype=torch.float32, device="cuda") for _ in range(self.SETS)]
+        self.i = 0
+        self.work = n * 10                       # encode 5 B/elt + decode 5 B/elt
+        self.h2d, self.d2h = n * 4, n * 4
+        self.config = {"workload": "fp8_roundtrip", "shape": list(self.x_host.shape), "fp8": "e4m3fn",
+                       "l2": f"{self.SETS} rotating buffer sets (576 MiB) > L2"}
+        self.stream = torch.cuda.current_stream()
+        self.lib = L.lib()
+        self.h_in = self.x_host.pin_memory()
+        self.h_out = torch.empty_like(self.x_host).pin_memory()
+        self.chunks = 8
+        self.streams = [torch.cuda.Stream() for _ in range(3)]
+        cn = n // self.chunks
+        self.cn = cn
+        self.d_in = [torch.empty(cn, dtype=torch.float32, device="cuda") for _ in self.streams]
+        self.d_mid = [torch.empty(cn, dtype=torch.uint8, device="cuda") for _ in self.streams]
+        self.d_out = [torch.empty(cn, dtype=torch.float32, device="cuda") for _ in self.streams]
+
+    def step(self):
+        k = self.i % self.SETS
+        self.i += 1
+        s = self.stream.cuda_stream
+        n = self.codes[k].numel()
+        rc = self.lib.fp8b200_encode_fp8(self.xs[k].data_ptr(), self.L.F32, self.codes[k].data_ptr(),
+                                         self.L.E4M3, n, None, s)
+        rc = rc or self.lib.fp8b200_decode_fp8(self.codes[k].data_ptr(), self.L.E4M3, self.back[k].data_ptr(),
+                                               self.L.F32, n, None, 0, s)
+        if rc:
+            self.L.check(rc, "fp8 round trip")
+
+    def e2e_step(self):
+        c = self.cn
+        hin, hout = self.h_in.view(-1), self.h_out.view(-1)
+
+        def body(i, j):
+            self.d_in[j].copy_(hin[i * c:(i + 1) * c], non_blocking=True)
+            self.nat.encode_fp8(self.d_in[j], torch.float8_e4m3fn, out=self.d_mid[j])
+            self.nat.decode_fp8(self.d_mid[j], torch.float8_e4m3fn, torch.float32, out=self.d_out[j])
+            hout[i * c:(i + 1) * c].copy_(self.d_out[j], non_blocking=True)
+        chunked_e2e(self.chunks, self.streams, body)
+
+    def check(self):
+        import numpy as np
+        from oracle import oracle as O
+        xb = self.x_host.view(-1)[:1 << 16].view(torch.int32).numpy().view(np.uint32)
+        ref = O.decode_fp8(O.encode_fp8(xb, 0, 0), 0, 0)
+        got = self.h_out.view(-1)[:1 << 16].view(torch.int32).numpy().view(np.uint32)
+        return bool(np.array_equal(ref, got))
+
+    @staticmethod
+    def cpu_run(rows=4096, reps=3):
+        import numpy as np
+        from oracle import oracle as O
+        from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
+        xb = fp8_roundtrip_input(0).view(torch.int32).numpy().view(np.uint32).reshape(-1)
+        xb = xb[: rows * 4096]
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            O.decode_fp8(O.encode_fp8(xb, 0, 0, threads=threads), 0, 0, threads=threads)
+        dt = (time.perf_counter() - t0) / reps
+        return xb.size * 10 / dt / 1e9, threads, f"{rows}x4096 f32 encode+decode per pass (oracle, C)"
+
+
+class ScaledMM:
+    name = "scaled_mm"
+    unit, bound, kernels_per_step = "TFLOP/s", "tensor", 1
+    dtype = "e4m3xe4m3->bf16 (f32 acc)"
+
+    def __init__(self, rank, args, rowwise=False):
+        from fp4_fp8_for_torch_mps import _lib as L
+        from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands, scaled_mm_operands
+        self.L = L
+        if rowwise:
+            M, N, K = ROWWISE_SHAPES[args.shape]
+            aq, bq, sa, sb = rowwise_operands(M, N, K, seed=rank)
+            self.name, self.metric = "scaled_mm_rowwise", "scaled_mm_rowwise_TFLOPS"
+        else:
+            M = N = K = args.size
+            aq, bq, sa, sb = scaled_mm_operands(M, N, K, seed=rank)
+            self.name, self.metric = "scaled_mm", "scaled_mm_TFLOPS"
+        self.M, self.N, self.K = M, N, K
+        self.profile = f"{self.name}_{M}x{N}x{K}"
+        self.a_host, self.b_host, self.sa_host, self.sb_host = aq, bq, sa, sb
+        self.a, self.b = aq.cuda(), bq.cuda()
+        self.sa, self.sb = sa.cuda(), sb.cuda()
+        self.out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        self.work = 2.0 * M * N * K
+        self.h2d = M * K + N * K
+        self.d2h = M * N * 2
+        l2 = "A+B+D {:.0f} MiB".format((M * K + N * K + 2 * M * N) / 2**20)
+        self.config = {"workload": self.name, "M": M, "N": N, "K": K,
+                       "scales": "rowwise" if rowwise else "tensorwise", "out": "bf16",
+                       "l2": l2 + (" > L2, no flush" if (M * K + N * K + 2 * M * N) > 126e6 else
+                                   " (one GEMM reads each operand tile from L2 repeatedly by design)")}
+        self.stream = torch.cuda.current_stream()
+        self.lib = L.lib()
+        self.la = L.SCALE_ROWWISE if rowwise else L.SCALE_TENSOR
+        self.h_a, self.h_b = aq.view(torch.uint8).pin_memory(), bq.view(torch.uint8).pin_memory()
+        self.h_out = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.d_a = torch.empty_like(self.a.view(torch.uint8))
+        self.d_b = torch.empty_like(self.b.view(torch.uint8))
+
+    def step(self):
+        L = self.L
+        rc = self.lib.fp8b200_scaled_mm(self.a.data_ptr(), L.E4M3, self.K, self.b.data_ptr(), L.E4M3, self.K,
+                                        self.M, self.N, self.K, self.sa.data_ptr(), self.la, self.sb.data_ptr(),
+                                        self.la, None, 0, None, self.out.data_ptr(), L.BF16, self.N,
+                                        self.stream.cuda_stream)
+        if rc:
+            L.check(rc, "scaled_mm")
+
+    def e2e_step(self):
+        # public API: torch._scaled_mm on operands copied from pinned host memory
+        self.d_a.copy_(self.h_a, non_blocking=True)
+        self.d_b.copy_(self.h_b, non_blocking=True)
+        r = torch._scaled_mm(self.d_a.view(torch.float8_e4m3fn), self.d_b.view(torch.float8_e4m3fn).t(),
+                             self.sa, self.sb, out_dtype=torch.bfloat16)
+        self.h_out.copy_(r, non_blocking=True)
+
+    def check(self):
+        import numpy as np
+        from oracle import oracle as O
+        rows = np.arange(0, self.M, max(1, self.M // 16))[:16]
+        ref, S = O.scaled_mm_ref(self.a_host.view(torch.uint8).numpy(), self.b_host.view(torch.uint8).numpy(),
+                                 self.sa_host.numpy().reshape(-1), self.sb_host.numpy().reshape(-1), rows=rows)
+        got = self.h_out[torch.from_numpy(rows)].float().double().numpy()
+        return bool(np.all(np.abs(got - ref) <= O.bf16_ulp(ref) + 2.0 ** -20 * S))
+
+    def cpu_run(self, reps=1):
+        """float32 dequantise-and-matmul on the host (the CPU path for this
+        GEMM; CPU torch._scaled_mm is per-tensor only and ~0.1 GFLOP/s), on a
+        256-row slice of A."""
+        threads = torch.get_num_threads()
+        rows = 256
+        A = self.a_host[:rows].float() * self.sa_host.reshape(-1, 1)[:rows] if self.sa_host.numel() > 1 \
+            else self.a_host[:rows].float() * self.sa_host
+        B = self.b_host.float() * (self.sb_host.reshape(-1, 1) if self.sb_host.numel() > 1 else self.sb_host)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            (A @ B.t()).to(torch.bfloat16)
+        dt = (time.perf_counter() - t0) / reps
+        return 2.0 * rows * self.N * self.K / dt / 1e12, threads, \
+            f"{rows}x{self.N}x{self.K} f32 dequantised matmul (CPU torch, {threads} threads)"
+
+
+WORKLOADS = {"fp4_decode": Fp4Decode, "fp8_roundtrip": Fp8RoundTrip,
+             "scaled_mm": lambda r, a: ScaledMM(r, a, False),
+             "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True)}
+
+
+# ---------------------------------------------------------------- reference arm
+def reference_line(args):
+    if args.workload == "fp4_decode":
+        vals = [Fp4Decode.cpu_run(rows=16384, reps=1) for _ in range(max(args.steps, 1))]
+        unit, metric = "GB/s", "fp4_decode_GBps"
+        config = {"workload": "fp4_decode", "shape": [16384, 8192], "out": "bf16", "scale": 0.37}
+    elif args.workload == "fp8_roundtrip":
+        vals = [Fp8RoundTrip.cpu_run(rows=4096, reps=1) for _ in range(max(args.steps, 1))]
+        unit, metric = "GB/s", "fp8_roundtrip_GBps"
+        config = {"workload": "fp8_roundtrip", "shape": [4096, 4096], "fp8": "e4m3fn"}
+    else:
+        w = ScaledMM.__new__(ScaledMM)
+        from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands, scaled_mm_operands
+        rowwise = args.workload == "scaled_mm_rowwise"
+        M, N, K = ROWWISE_SHAPES[args.shape] if rowwise else (args.size,) * 3
+        # a 256-row slice of A is all the CPU path runs
+        ops = (rowwise_operands if rowwise else scaled_mm_operands)(256, N, K)
+        w.a_host, w.b_host, w.sa_host, w.sb_host = ops
+        w.M, w.N, w.K = 256, N, K
+        vals = [w.cpu_run() for _ in range(max(args.steps, 1))]
+        unit, metric = "TFLOP/s", ("scaled_mm_rowwise_TFLOPS" if rowwise else "scaled_mm_TFLOPS")
+        config = {"workload": args.workload, "M": M, "N": N, "K": K, "out": "bf16"}
+    v = statistics.median(x[0] for x in vals)
+    return {"metric": metric, "value": round(v, 4), "unit": unit, "config": config,
+            "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": vals[0][1], "kind": "port",
+                             "sample": vals[0][2]},
+            "dtype": "cpu"}
+
+
+# ---------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="fp4_decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--size", type=int, default=8192)
+    ap.add_argument("--shape", type=int, default=0, choices=[0, 1, 2])
+    args = ap.parse_args()
+    rank, local, ws = rank_info()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        line = reference_line(args)
+        line.update({"impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                     "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic",
+                     "e2e": {"value": line["value"], "unit": line["unit"],
+                             "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        print(json.dumps(line))
+        return 0
+
+    dist_on = ws > 1
+    torch.cuda.set_device(local)
+    if dist_on:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import fp4_fp8_for_torch_mps  # noqa: F401  (registers the overrides used by e2e)
+    from fp4_fp8_for_torch_mps import _lib as L
+
+    w = WORKLOADS[args.workload](rank, args)
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        w.step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    n0 = L.launch_count()
+    ms = timed_region(w.step, args.steps, w.stream, dist_on)
+    launches = L.launch_count() - n0
+    clocks = sampler.stop()
+
+    for _ in range(2):
+        w.e2e_step()
+    torch.cuda.synchronize()
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_ms = timed_region(w.e2e_step, e2e_steps, torch.cuda.current_stream(), dist_on)
+    ok = w.check()
+
+    pk, pk_kind = peaks()
+    per_step_s = ms / args.steps * 1e-3
+    scale = 1e9 if w.unit == "GB/s" else 1e12
+    value = w.work * ws / per_step_s / scale
+    e2e_value = w.work * ws / (e2e_ms / e2e_steps * 1e-3) / scale
+    achieved = w.work / per_step_s / scale  # per GPU, per launch-averaged step
+    if w.bound == "hbm":
+        peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
+    else:
+        peak, punit = 2.0 * pk["bf16_tflops"], "TFLOP/s"
+        psrc = f"2 x {pk_kind} bf16_tflops (dense fp8 issue rate is twice bf16 on tcgen05)"
+    cpu = None
+    if rank == 0:
+        v, cores, sample = w.cpu_run() if hasattr(w, "cpu_run") else (None, None, None)
+        cpu = {"value": round(v, 4), "unit": w.unit, "cores": cores, "kind": "port", "sample": sample}
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": w.metric, "value": round(value, 3), "unit": w.unit, "n_gpus": ws, "steps": args.steps,
+        "warmup": warm, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+        "config": dict(w.config, parallelism=f"replicas{ws}" if ws > 1 else "single"),
+        "e2e": {"value": round(e2e_value, 3), "unit": w.unit, "h2d_bytes_per_step": int(w.h2d),
+                "d2h_bytes_per_step": int(w.d2h)},
+        "roofline": {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
+                     "frac": round(achieved / peak, 4), "peak_source": psrc,
+                     "traffic": profile_traffic(w.profile)},
+        "cpu_baseline": cpu,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "result_check": ok,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,174 @@
+/*
+ * fp8_b200.h — C ABI of the B200 (sm_100a) FP8/FP4 conversion and scaled-GEMM
+ * library (libfp8_b200.so).
+ *
+ * This is the boundary the Python plugin (package fp4_fp8_for_torch_mps)
+ * binds with ctypes. It replaces the reference plugin's kernel boundary: the
+ * Metal library compiled by torch.mps.compile_shader and dispatched as
+ * `lib.<kernel>(..., threads=, group_size=)` from fp8_mps_native.py. Each
+ * entry point below cites the reference kernel and launcher it replaces.
+ *
+ * Conventions
+ *  - All data pointers are device pointers on the current CUDA device, owned
+ *    by the caller; the library never allocates or frees. `stream` is a
+ *    cudaStream_t (NULL = legacy default stream).
+ *  - Scales are device pointers to float32 so that no host synchronisation is
+ *    needed (the reference reads amax with .item(), fp8_mps_native.py:107).
+ *  - Every function returns 0 on success or a negative FP8B200_E* status;
+ *    fp8b200_last_error() gives a message for the calling thread.
+ *  - n == 0 is valid and launches nothing.
+ */
+#ifndef FP8_B200_H_
+#define FP8_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define FP8B200_OK 0
+#define FP8B200_EINVAL (-1)   /* bad argument (dtype, size, alignment, stride) */
+#define FP8B200_ELAUNCH (-2)  /* CUDA launch or runtime error */
+#define FP8B200_EDEVICE (-3)  /* current device is not sm_100 (B200) */
+#define FP8B200_ETIMEOUT (-4) /* a bounded device-side wait gave up */
+
+/* dtype codes */
+#define FP8B200_F32 0
+#define FP8B200_BF16 1
+#define FP8B200_F16 2
+#define FP8B200_E4M3 3 /* torch.float8_e4m3fn */
+#define FP8B200_E5M2 4 /* torch.float8_e5m2 */
+
+/* scale modes for the decoders */
+#define FP8B200_SCALE_NONE 0     /* exact conversion, scale ignored */
+#define FP8B200_SCALE_F32 1      /* out = round_out(round_f32(value * scale)) */
+#define FP8B200_SCALE_F16_REF 2  /* out = f16(f16(value) * f16(scale)), the
+                                    reference dequantize semantics (f16 out only) */
+
+/* scale layouts for fp8b200_scaled_mm */
+#define FP8B200_SCALE_TENSOR 0   /* one float */
+#define FP8B200_SCALE_ROWWISE 1  /* scale_a: M floats; scale_b: N floats */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fp8b200_version(void);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+const char *fp8b200_last_error(void);
+
+/*
+ * float32/bfloat16/float16 -> float8 (e4m3fn or e5m2) encode of n contiguous
+ * elements: round to nearest even; e4m3fn: |x| rounding past 448, inf and NaN
+ * give 0x7F|sign; e5m2: rounding past 57344 and inf give 0x7C|sign, NaN
+ * 0x7F|sign. If `scale` is non-NULL each element is first multiplied by
+ * *scale in float32.
+ * Replaces float_to_fp8_kernel (shaders/fp8_matmul.metal:240-248, encoder
+ * :105-142) launched by fp8_encode (fp8_mps_native.py:85-98).
+ */
+int fp8b200_encode_fp8(const void *src, int src_dtype, void *dst, int fp8_dtype,
+                       int64_t n, const float *scale, void *stream);
+
+/*
+ * float8 -> float32/bfloat16/float16 decode of n contiguous codes, bit-exact
+ * with CPU PyTorch (NaN payloads included), optionally scaled (scale_mode).
+ * Replaces fp8_to_half_kernel (shaders/fp8_matmul.metal:229-237) plus the
+ * scale and cast passes of fp8_dequantize (fp8_mps_native.py:65-82) and
+ * ops.py:113-120.
+ */
+int fp8b200_decode_fp8(const void *src, int fp8_dtype, void *dst, int out_dtype,
+                       int64_t n, const float *scale, int scale_mode, void *stream);
+
+/*
+ * float4_e2m1fn_x2 -> float decode: each of `nbytes` packed bytes gives two
+ * outputs, low nibble first (element 2i), optionally scaled (scale_mode).
+ * Replaces fp4x2_to_half_kernel (shaders/fp8_matmul.metal:251-261) plus the
+ * scale and cast passes of fp4_dequantize (fp8_mps_native.py:162-179) and
+ * ops.py:104-111.
+ */
+int fp8b200_decode_fp4(const void *src, int64_t nbytes, void *dst, int out_dtype,
+                       const float *scale, int scale_mode, void *stream);
+
+/*
+ * Per-tensor dynamic quantisation to float8: amax = max|x|, scale =
+ * 448/amax (57344/amax for e5m2; 1 if amax is 0 or NaN), dst = encode(x *
+ * scale), scale_out[0] = scale, scale_out[1] = 1/scale (the value the
+ * reference returns). `amax_scratch` is one caller-provided device uint32
+ * used as the reduction accumulator; it is cleared by this call.
+ * Replaces fp8_quantize (fp8_mps_native.py:101-120) without its .item() sync.
+ */
+int fp8b200_quantize_fp8(const void *src, int src_dtype, void *dst, int fp8_dtype,
+                         int64_t n, float *scale_out, uint32_t *amax_scratch,
+                         void *stream);
+
+/*
+ * float -> float4_e2m1fn_x2 encode of n (even) contiguous elements into n/2
+ * packed bytes, element 2i in the low nibble, with the reference's
+ * nearest-of-8 thresholds (not round-to-nearest-even at ties; NaN -> +6).
+ * If `scale` is non-NULL each element is first multiplied by *scale.
+ * Replaces float_to_fp4x2_kernel (shaders/fp8_matmul.metal:264-274, encoder
+ * :88-102) launched by fp4_encode (fp8_mps_native.py:182-197).
+ */
+int fp8b200_encode_fp4(const void *src, int src_dtype, void *dst, int64_t n,
+                       const float *scale, void *stream);
+
+/*
+ * Per-tensor FP4 quantisation: scale = 6/amax (1 if amax is 0 or NaN),
+ * dst = encode_fp4(x * scale), scale_out = {scale, 1/scale}; `amax_scratch`
+ * as for fp8b200_quantize_fp8.
+ * Replaces fp4_quantize (fp8_mps_native.py:200-221) without its .item() sync.
+ */
+int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, int64_t n,
+                         float *scale_out, uint32_t *amax_scratch, void *stream);
+
+/*
+ * D = (A * scale_a) @ (B * scale_b)^T [+ bias] [* scale_result] -> out_dtype.
+ * A: M x K float8 codes, row-major with row stride lda (bytes).
+ * B: N x K float8 codes, row-major with row stride ldb (bytes): the bytes of
+ *    torch._scaled_mm's column-major mat2 (K x N).
+ * scale_a / scale_b: float32 device pointers, layout FP8B200_SCALE_TENSOR or
+ *    FP8B200_SCALE_ROWWISE (M values for A, N values for B).
+ * bias: N values of bias_dtype (F32/BF16/F16) or NULL; scale_result: one
+ *    float32 or NULL. D: M x N of out_dtype (F32/BF16/F16/E4M3/E5M2), row
+ *    stride ldd elements. K must be a positive multiple of 16; lda/ldb
+ *    multiples of 16; A and B 16-byte aligned.
+ * Accumulation is float32 on the tcgen05 tensor cores.
+ * Replaces the reference's _scaled_mm override (ops.py:33-49) and the GEMM
+ * kernels behind it: fp8_scaled_matmul_kernel (shaders/fp8_matmul.metal:
+ * 145-180), fp8_scaled_vecmat_kernel (:183-226) and the decode+fp16-matmul
+ * fast path (fp8_mps_native.py:129-159).
+ */
+int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda,
+                      const void *B, int b_dtype, int64_t ldb,
+                      int64_t M, int64_t N, int64_t K,
+                      const float *scale_a, int scale_a_layout,
+                      const float *scale_b, int scale_b_layout,
+                      const void *bias, int bias_dtype,
+                      const float *scale_result,
+                      void *D, int out_dtype, int64_t ldd,
+                      void *stream);
+
+/*
+ * Device-side status of the scaled GEMM on the current device: 0 if no
+ * bounded wait has timed out, else FP8B200_ETIMEOUT with *status_out holding
+ * the site code. Synchronises the device. `reset` clears the word.
+ * (Failure reporting for the GEMM's bounded waits; the reference has none.)
+ */
+int fp8b200_gemm_status(uint32_t *status_out, int reset);
+
+/*
+ * Test hook for the GEMM's bounded waits: skip_first_load != 0 makes the
+ * producer never fill the first pipeline stage, so the consumer's wait runs
+ * out after wait_timeout_ns (0 = the default of 2 s) and the kernel returns
+ * with the status word set. Not for production use.
+ */
+int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
+
+/* Number of kernels this library launched since load (all devices). */
+uint64_t fp8b200_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP8_B200_H_ */

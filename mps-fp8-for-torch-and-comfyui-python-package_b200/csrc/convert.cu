@@ -1,0 +1,706 @@
+// FP8 / FP4 conversion kernels for B200 (sm_100a).
+//
+// All of these are HBM-bound byte streams. Design:
+//  * Every thread moves one "unit" per step: the input bytes that produce
+//    exactly 32 output bytes (decoders) or 16 output bytes (encoders). The
+//    unit index is `thread + j * total_threads`, so each warp-wide load and
+//    store covers one contiguous span (a full 1 KiB for 32-byte stores):
+//    every DRAM sector is written whole by a single instruction.
+//  * 256-bit global accesses (ld/st .v8.u32, new on sm_100) halve the number
+//    of memory instructions against 16-byte vectors; four units per thread
+//    per step keep four independent loads in flight.
+//  * Grid-stride over at most (blocks per SM) x (SM count) CTAs.
+//  * Encode (float -> fp8): PTX cvt.rn.satfinite.{e4m3,e5m2}x2.f32 converts
+//    two elements per instruction; the only cases where that instruction and
+//    CPU PyTorch disagree (magnitudes that round past the largest finite
+//    value, inf, NaN) are found with one integer max per 16 elements and
+//    patched on a rare slow path.
+//  * Decode (fp8 -> float, fp4 -> float): a per-block table in shared memory
+//    maps each code (or each packed fp4 byte) to its output bit pattern, with
+//    the scale already applied. The table is replicated 32 times, one copy per
+//    lane, so lane L always reads bank L: every lookup is a single
+//    conflict-free shared-memory wavefront.
+//
+// Semantics (bit-exact with CPU PyTorch on x86, NaN payloads included):
+//   e4m3fn encode: RNE; |x| rounding past 448, inf, NaN -> 0x7F | sign
+//   e5m2 encode:   RNE; rounding past 57344, inf -> 0x7C | sign; NaN -> 0x7F | sign
+//   decode to f32: exact; e4m3fn NaN -> sign|0x7FF00000; e5m2 NaN quieted
+//   decode to bf16: exact; every NaN -> 0x7FC0
+//   decode to f16: exact; NaN -> sign|0x7E00|payload>>13
+// The reference kernels these replace: shaders/fp8_matmul.metal:105-142 and
+// :240-248 (encode), :229-237 (decode), :251-261 (fp4 decode), :88-102 and
+// :264-274 (fp4 encode).
+#include "common.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <type_traits>
+
+namespace fp8b200 {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kUnroll = 4;  // units per thread per step
+
+// ------------------------------------------------------------------ loads/stores
+struct U8x32 { uint32_t w[8]; };
+
+__device__ __forceinline__ uint32_t ld_u32(const void *p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_u64(const void *p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_u128(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ U8x32 ld_u256(const void *p) {
+  U8x32 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                 "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_u128(void *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void st_u256(void *p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+inline bool aligned32(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
+
+// ------------------------------------------------------------------ element semantics
+// fp8 code -> float32 bit pattern (CPU PyTorch semantics).
+__device__ __forceinline__ uint32_t fp8_to_f32_bits(uint32_t c, int fmt) {
+  const uint32_t s = (c & 0x80u) << 24, mag = c & 0x7Fu;
+  if (fmt == FP8B200_E4M3) {
+    if (mag == 0x7Fu) return s | 0x7FF00000u;
+    const uint32_t ef = mag >> 3, mf = mag & 7u;
+    if (ef == 0) return s | f2u(__uint2float_rn(mf) * 0x1p-9f);  // exact
+    return s | ((ef + 120u) << 23) | (mf << 20);
+  }
+  const uint32_t ef = mag >> 2, mf = mag & 3u;
+  if (ef == 31u) return mf ? (s | 0x7FC00000u | (mf << 21)) : (s | 0x7F800000u);
+  if (ef == 0) return s | f2u(__uint2float_rn(mf) * 0x1p-16f);  // exact
+  return s | ((ef + 112u) << 23) | (mf << 21);
+}
+
+__device__ __forceinline__ bool is_nan_bits(uint32_t b) { return (b & 0x7FFFFFFFu) > 0x7F800000u; }
+
+// float32 bits -> output dtype bits (f32 unchanged; bf16/f16 round to nearest even).
+__device__ __forceinline__ uint32_t f32_to_out_bits(uint32_t b, int odt) {
+  if (odt == FP8B200_F32) return b;
+  const bool nan = is_nan_bits(b);
+  if (odt == FP8B200_BF16)
+    return nan ? 0x7FC0u : (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(u2f(b)));
+  if (nan) return ((b >> 16) & 0x8000u) | 0x7E00u | ((b & 0x7FFFFFu) >> 13);
+  return (uint32_t)__half_as_ushort(__float2half_rn(u2f(b)));
+}
+
+// value bits (f32) x scale according to scale_mode, result as out-dtype bits.
+__device__ __forceinline__ uint32_t apply_scale(uint32_t vb, int odt, float scale, int mode) {
+  if (mode == FP8B200_SCALE_F32) {
+    if (!is_nan_bits(vb)) vb = f2u(__fmul_rn(u2f(vb), scale));
+    return f32_to_out_bits(vb, odt);
+  }
+  if (mode == FP8B200_SCALE_F16_REF) {
+    // f16(value) * f16(scale) rounded to f16 (output dtype is f16 here)
+    const uint32_t h = f32_to_out_bits(vb, FP8B200_F16);
+    if (is_nan_bits(vb)) return h;
+    const float s16 = __half2float(__float2half_rn(scale));
+    const float v16 = __half2float(__ushort_as_half((unsigned short)h));
+    return f32_to_out_bits(f2u(__fmul_rn(v16, s16)), FP8B200_F16);
+  }
+  return f32_to_out_bits(vb, odt);
+}
+
+__device__ __forceinline__ float load_scale(const float *scale, int mode) {
+  return (mode != FP8B200_SCALE_NONE && scale != nullptr) ? __ldg(scale) : 1.0f;
+}
+
+__constant__ float kFp4Values[16] = {
+    0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+    -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f,
+};
+
+// ------------------------------------------------------------------ lookup tables
+// Entry type: u32 for one fp8 output (any dtype) and for an fp4 pair of
+// 16-bit outputs; u64 (uint2) for an fp4 pair of f32 outputs.
+template <bool FP4, int OUT_BYTES>
+struct Lut {
+  using T = typename std::conditional<FP4 && OUT_BYTES == 4, uint2, uint32_t>::type;
+  static constexpr int kBytes = 256 * 32 * (int)sizeof(T);
+};
+
+// Builds the 32-way replicated table: 256 distinct entries, then copies.
+template <bool FP4, int OUT_BYTES>
+__device__ __forceinline__ void build_lut(typename Lut<FP4, OUT_BYTES>::T *lut, int fmt, int odt, float s, int mode) {
+  using T = typename Lut<FP4, OUT_BYTES>::T;
+  __shared__ T distinct[256];
+  for (int c = threadIdx.x; c < 256; c += blockDim.x) {
+    if constexpr (!FP4) {
+      distinct[c] = apply_scale(fp8_to_f32_bits((uint32_t)c, fmt), odt, s, mode);
+    } else {
+      const uint32_t lo = apply_scale(f2u(kFp4Values[c & 15]), odt, s, mode);
+      const uint32_t hi = apply_scale(f2u(kFp4Values[c >> 4]), odt, s, mode);
+      if constexpr (OUT_BYTES == 4) distinct[c] = make_uint2(lo, hi);
+      else distinct[c] = lo | (hi << 16);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) lut[i] = distinct[i >> 5];
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------ decoders
+// One unit = the input bytes that give 32 output bytes:
+//   fp8 -> 16-bit: 16 codes;  fp8 -> f32: 8 codes;
+//   fp4 -> 16-bit: 8 bytes;   fp4 -> f32: 4 bytes.
+template <bool FP4, int OUT_BYTES>
+struct DecodeUnit {
+  static constexpr int kOutPerByte = FP4 ? 2 : 1;
+  static constexpr int kInBytes = 32 / (OUT_BYTES * kOutPerByte);
+};
+
+template <bool FP4, int OUT_BYTES>
+__device__ __forceinline__ void decode_unit(const uint8_t *in, uint8_t *out,
+                                            const typename Lut<FP4, OUT_BYTES>::T *tab) {
+  constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
+  uint32_t x[4];
+  if constexpr (IB == 16) { uint4 v = ld_u128(in); x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w; }
+  else if constexpr (IB == 8) { uint2 v = ld_u64(in); x[0] = v.x; x[1] = v.y; }
+  else { x[0] = ld_u32(in); }
+  uint32_t w[8];
+  // tab[c << 5] is this lane's copy of entry c
+#pragma unroll
+  for (int q = 0; q < IB / 4; q++) {
+    const uint32_t c0 = x[q] & 0xFFu, c1 = (x[q] >> 8) & 0xFFu, c2 = (x[q] >> 16) & 0xFFu, c3 = x[q] >> 24;
+    if constexpr (!FP4 && OUT_BYTES == 2) {        // 4 codes -> 4 halves -> 2 words
+      w[2 * q] = tab[c0 << 5] | (tab[c1 << 5] << 16);
+      w[2 * q + 1] = tab[c2 << 5] | (tab[c3 << 5] << 16);
+    } else if constexpr (!FP4) {                    // 4 codes -> 4 words
+      w[4 * q] = tab[c0 << 5]; w[4 * q + 1] = tab[c1 << 5];
+      w[4 * q + 2] = tab[c2 << 5]; w[4 * q + 3] = tab[c3 << 5];
+    } else if constexpr (OUT_BYTES == 2) {          // 4 bytes -> 8 halves -> 4 words
+      w[4 * q] = tab[c0 << 5]; w[4 * q + 1] = tab[c1 << 5];
+      w[4 * q + 2] = tab[c2 << 5]; w[4 * q + 3] = tab[c3 << 5];
+    } else {                                        // 4 bytes -> 8 f32 words
+      const uint2 p0 = tab[c0 << 5], p1 = tab[c1 << 5], p2 = tab[c2 << 5], p3 = tab[c3 << 5];
+      w[0] = p0.x; w[1] = p0.y; w[2] = p1.x; w[3] = p1.y;
+      w[4] = p2.x; w[5] = p2.y; w[6] = p3.x; w[7] = p3.y;
+    }
+  }
+  st_u256(out, w);
+}
+
+// in/out must be 32-byte aligned for the unit loop; the ragged tail (fewer
+// bytes than one unit per ... ) is decoded element-wise by block 0.
+template <bool FP4, int OUT_BYTES>
+__global__ void __launch_bounds__(kThreads)
+decode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t nbytes, int fmt, int odt,
+              const float *__restrict__ scale, int mode) {
+  using T = typename Lut<FP4, OUT_BYTES>::T;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T *lut = reinterpret_cast<T *>(smem_raw);
+  build_lut<FP4, OUT_BYTES>(lut, fmt, odt, load_scale(scale, mode), mode);
+  const T *tab = lut + (threadIdx.x & 31u);
+
+  constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
+  const int64_t nunits = nbytes / IB;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; u + (kUnroll - 1) * nthreads < nunits; u += kUnroll * nthreads) {
+#pragma unroll
+    for (int j = 0; j < kUnroll; j++) {
+      const int64_t v = u + j * nthreads;
+      decode_unit<FP4, OUT_BYTES>(src + v * IB, dst + v * 32, tab);
+    }
+  }
+  for (; u < nunits; u += nthreads) decode_unit<FP4, OUT_BYTES>(src + u * IB, dst + u * 32, tab);
+
+  if (blockIdx.x == 0) {
+    for (int64_t i = nunits * IB + threadIdx.x; i < nbytes; i += blockDim.x) {
+      const T e = tab[(uint32_t)src[i] << 5];
+      if constexpr (!FP4) {
+        if (OUT_BYTES == 4) reinterpret_cast<uint32_t *>(dst)[i] = e;
+        else reinterpret_cast<uint16_t *>(dst)[i] = (uint16_t)e;
+      } else {
+        reinterpret_cast<T *>(dst)[i] = e;
+      }
+    }
+  }
+}
+
+// Unaligned buffers: one input byte per thread, same semantics, no table.
+__global__ void __launch_bounds__(kThreads)
+decode_scalar_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t nbytes, int fp4, int fmt,
+                     int odt, const float *__restrict__ scale, int mode) {
+  const float s = load_scale(scale, mode);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t b = src[i];
+    if (!fp4) {
+      const uint32_t r = apply_scale(fp8_to_f32_bits(b, fmt), odt, s, mode);
+      if (odt == FP8B200_F32) reinterpret_cast<uint32_t *>(dst)[i] = r;
+      else reinterpret_cast<uint16_t *>(dst)[i] = (uint16_t)r;
+    } else {
+      const uint32_t lo = apply_scale(f2u(kFp4Values[b & 15u]), odt, s, mode);
+      const uint32_t hi = apply_scale(f2u(kFp4Values[b >> 4]), odt, s, mode);
+      if (odt == FP8B200_F32) {
+        reinterpret_cast<uint32_t *>(dst)[2 * i] = lo;
+        reinterpret_cast<uint32_t *>(dst)[2 * i + 1] = hi;
+      } else {
+        reinterpret_cast<uint16_t *>(dst)[2 * i] = (uint16_t)lo;
+        reinterpret_cast<uint16_t *>(dst)[2 * i + 1] = (uint16_t)hi;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ encode
+// Widen one source element to float (exact); `sign` receives the source sign
+// bit (kept separately because NaN sign is not preserved by every widening).
+template <int SRC>
+__device__ __forceinline__ float widen(uint32_t raw, uint32_t &sign) {
+  if constexpr (SRC == FP8B200_F32) { sign = raw & 0x80000000u; return u2f(raw); }
+  else if constexpr (SRC == FP8B200_BF16) { sign = (raw & 0x8000u) << 16; return u2f(raw << 16); }
+  else { sign = (raw & 0x8000u) << 16; return __half2float(__ushort_as_half((unsigned short)raw)); }
+}
+
+// x86 multiply NaN rule (what CPU torch's `x * scale` yields): a NaN operand x
+// is kept (sign included); a NaN created from non-NaN operands is negative.
+__device__ __forceinline__ float mul_scale(float x, uint32_t &sign, float s) {
+  const float r = __fmul_rn(x, s);
+  if (is_nan_bits(f2u(r)) && !is_nan_bits(f2u(x)))
+    sign = is_nan_bits(f2u(s)) ? (f2u(s) & 0x80000000u) : 0x80000000u;
+  else if (!is_nan_bits(f2u(r)))
+    sign = f2u(r) & 0x80000000u;
+  return r;
+}
+
+template <int FMT>
+__device__ __forceinline__ uint32_t cvt_pair(float lo, float hi) {
+  uint16_t r;  // PTX puts the first source operand in the upper byte
+  if constexpr (FMT == FP8B200_E4M3)
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// magnitude bits above which cvt.satfinite differs from CPU torch
+template <int FMT> constexpr uint32_t special_threshold() {
+  return FMT == FP8B200_E4M3 ? 0x43E80000u /* 464 */ : 0x476FFFFFu /* just below 61440 */;
+}
+
+template <int FMT>
+__device__ __forceinline__ uint32_t special_code(uint32_t absb, uint32_t sign) {
+  const uint32_t s = sign >> 24;
+  if constexpr (FMT == FP8B200_E4M3) return s | 0x7Fu;
+  else return s | (absb > 0x7F800000u ? 0x7Fu : 0x7Cu);
+}
+
+template <int SRC, int FMT>
+__device__ __forceinline__ uint32_t encode_one(uint32_t raw, bool scaled, float s) {
+  uint32_t sign;
+  float x = widen<SRC>(raw, sign);
+  if (scaled) x = mul_scale(x, sign, s);
+  const uint32_t absb = f2u(x) & 0x7FFFFFFFu;
+  if (absb > special_threshold<FMT>()) return special_code<FMT>(absb, sign);
+  return cvt_pair<FMT>(x, 0.0f) & 0xFFu;
+}
+
+template <int SRC>
+__device__ __forceinline__ uint32_t load_raw(const void *src, int64_t i) {
+  if constexpr (SRC == FP8B200_F32) return reinterpret_cast<const uint32_t *>(src)[i];
+  else return reinterpret_cast<const uint16_t *>(src)[i];
+}
+
+// One unit = 16 elements (64 or 32 input bytes) -> 16 output bytes.
+template <int SRC, int FMT>
+__device__ __forceinline__ void encode_unit(const uint8_t *in, uint8_t *out, bool scaled, float s) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  uint32_t raw[16];
+  if constexpr (EB == 4) {
+    const U8x32 a = ld_u256(in), b = ld_u256(in + 32);
+#pragma unroll
+    for (int j = 0; j < 8; j++) { raw[j] = a.w[j]; raw[8 + j] = b.w[j]; }
+  } else {
+    const U8x32 a = ld_u256(in);
+#pragma unroll
+    for (int j = 0; j < 8; j++) { raw[2 * j] = a.w[j] & 0xFFFFu; raw[2 * j + 1] = a.w[j] >> 16; }
+  }
+  float x[16];
+  uint32_t amax = 0;
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    uint32_t sg;
+    x[i] = widen<SRC>(raw[i], sg);
+    if (scaled) x[i] = __fmul_rn(x[i], s);
+    amax = max(amax, f2u(x[i]) & 0x7FFFFFFFu);
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++)
+    o[q] = cvt_pair<FMT>(x[4 * q], x[4 * q + 1]) | (cvt_pair<FMT>(x[4 * q + 2], x[4 * q + 3]) << 16);
+  if (amax > special_threshold<FMT>()) {  // rare: overflow, inf or NaN present
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const uint32_t c = encode_one<SRC, FMT>(raw[i], scaled, s);
+      o[i >> 2] = (o[i >> 2] & ~(0xFFu << (8 * (i & 3)))) | (c << (8 * (i & 3)));
+    }
+  }
+  st_u128(out, o[0], o[1], o[2], o[3]);
+}
+
+// vec: source 32-byte and destination 16-byte aligned; otherwise every
+// element goes through the scalar loop (still on the GPU).
+template <int SRC, int FMT>
+__global__ void __launch_bounds__(kThreads)
+encode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t n, int64_t nunits,
+              const float *__restrict__ scale) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  const bool scaled = scale != nullptr;
+  const float s = scaled ? __ldg(scale) : 1.0f;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; u + (kUnroll - 1) * nthreads < nunits; u += kUnroll * nthreads) {
+#pragma unroll
+    for (int j = 0; j < kUnroll; j++) {
+      const int64_t v = u + j * nthreads;
+      encode_unit<SRC, FMT>(src + v * 16 * EB, dst + v * 16, scaled, s);
+    }
+  }
+  for (; u < nunits; u += nthreads) encode_unit<SRC, FMT>(src + u * 16 * EB, dst + u * 16, scaled, s);
+  for (int64_t i = nunits * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nthreads)
+    dst[i] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(src, i), scaled, s);
+}
+
+// ------------------------------------------------------------------ fp4 encode
+// The reference's nearest-of-8 threshold encoder (shaders/fp8_matmul.metal:
+// 88-102): not round-to-nearest-even at ties (0.25 -> 0.5, 1.25 -> 1.5), NaN
+// -> +6, -0.0 -> +0. Element 2i goes to the low nibble (:271-273).
+__device__ __forceinline__ uint32_t fp4_code(float v) {
+  uint32_t sign = 0;
+  if (v < 0.0f) { sign = 8u; v = -v; }
+  const uint32_t c = (v < 0.25f) ? 0u : (v < 0.75f) ? 1u : (v < 1.25f) ? 2u : (v < 1.75f) ? 3u
+                   : (v < 2.5f) ? 4u : (v < 3.5f) ? 5u : (v < 5.0f) ? 6u : 7u;
+  return sign | c;
+}
+
+template <int SRC>
+__device__ __forceinline__ float load_elem(const void *src, int64_t i) {
+  uint32_t sg;
+  return widen<SRC>(load_raw<SRC>(src, i), sg);
+}
+
+// One unit = 32 elements -> 16 packed bytes; vec units need a 32-byte
+// aligned source and a 16-byte aligned destination.
+template <int SRC>
+__global__ void __launch_bounds__(kThreads)
+fp4_encode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t npairs, int64_t nunits,
+                  const float *__restrict__ scale) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  const bool scaled = scale != nullptr;
+  const float s = scaled ? __ldg(scale) : 1.0f;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < nunits; u += nthreads) {
+    const uint8_t *in = src + u * 32 * EB;
+    uint32_t o[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int h = 0; h < EB; h++) {  // 32-byte chunks: 8 (f32) or 16 (16-bit) elements each
+      const U8x32 a = ld_u256(in + 32 * h);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        uint32_t sg;
+        if constexpr (EB == 4) {
+          float x = widen<SRC>(a.w[j], sg);
+          if (scaled) x = __fmul_rn(x, s);
+          const int e = 8 * h + j;
+          o[e >> 3] |= fp4_code(x) << (4 * (e & 7));
+        } else {
+          float x0 = widen<SRC>(a.w[j] & 0xFFFFu, sg), x1 = widen<SRC>(a.w[j] >> 16, sg);
+          if (scaled) { x0 = __fmul_rn(x0, s); x1 = __fmul_rn(x1, s); }
+          const int e = 16 * h + 2 * j;
+          o[e >> 3] |= (fp4_code(x0) | (fp4_code(x1) << 4)) << (4 * (e & 7));
+        }
+      }
+    }
+    st_u128(dst + u * 16, o[0], o[1], o[2], o[3]);
+  }
+  for (int64_t p = nunits * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < npairs; p += nthreads) {
+    float lo = load_elem<SRC>(src, 2 * p), hi = load_elem<SRC>(src, 2 * p + 1);
+    if (scaled) { lo = __fmul_rn(lo, s); hi = __fmul_rn(hi, s); }
+    dst[p] = (uint8_t)(fp4_code(lo) | (fp4_code(hi) << 4));
+  }
+}
+
+// ------------------------------------------------------------------ amax / quantize
+// max |x| as float bits (NaN sorts above inf, so a NaN anywhere wins).
+// nunits: 32-byte chunks read vectorised (0 for an unaligned source); the
+// remaining elements go through the scalar loop.
+template <int SRC>
+__global__ void __launch_bounds__(kThreads)
+amax_kernel(const uint8_t *__restrict__ src, int64_t n, int64_t nunits, uint32_t *__restrict__ amax_out) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  constexpr int PER = 32 / EB;
+  uint32_t m = 0, sg;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < nunits; u += nthreads) {
+    const U8x32 a = ld_u256(src + u * 32);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      if constexpr (EB == 4) m = max(m, f2u(widen<SRC>(a.w[j], sg)) & 0x7FFFFFFFu);
+      else {
+        m = max(m, f2u(widen<SRC>(a.w[j] & 0xFFFFu, sg)) & 0x7FFFFFFFu);
+        m = max(m, f2u(widen<SRC>(a.w[j] >> 16, sg)) & 0x7FFFFFFFu);
+      }
+    }
+  }
+  for (int64_t i = nunits * PER + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nthreads)
+    m = max(m, f2u(load_elem<SRC>(src, i)) & 0x7FFFFFFFu);
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t warp_max[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t r = threadIdx.x < blockDim.x / 32 ? warp_max[threadIdx.x] : 0u;
+    r = __reduce_max_sync(0xFFFFFFFFu, r);
+    if (threadIdx.x == 0 && r) atomicMax(amax_out, r);
+  }
+}
+
+// scale = fmax/amax (1 if amax is 0 or NaN), computed in double as the
+// reference does on the host (fp8_mps_native.py:107-108, :119).
+__global__ void quant_scale_kernel(const uint32_t *__restrict__ amax_bits, float fmax, float *__restrict__ scale_out) {
+  const double a = (double)u2f(*amax_bits);
+  const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+  scale_out[0] = (float)sd;
+  scale_out[1] = (float)(1.0 / sd);
+}
+
+// ------------------------------------------------------------------ launch helpers
+// Resident CTAs per SM for `kernel` (queried once per kernel and device),
+// after raising its dynamic shared-memory limit when it needs more than 48 KiB.
+template <typename K>
+int resident_per_sm(K kernel, int smem_bytes) {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 1;
+  if (!cached[dev]) {
+    if (smem_bytes > 48 * 1024)
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem_bytes) != cudaSuccess || n < 1) n = 1;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <bool FP4, int OUT_BYTES>
+void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt, const float *scale, int mode,
+                   cudaStream_t st, int dev) {
+  constexpr int smem = Lut<FP4, OUT_BYTES>::kBytes;
+  constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
+  const int per_sm = resident_per_sm(decode_kernel<FP4, OUT_BYTES>, smem);
+  const int g = grid_for(std::max<int64_t>(nbytes / IB, 1), kThreads, per_sm);
+  decode_kernel<FP4, OUT_BYTES><<<g, kThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, fmt, odt,
+                                                           scale, mode);
+}
+
+template <int SRC, int FMT>
+void launch_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+  const bool vec = aligned32(src) && aligned16(dst);
+  const int64_t nunits = vec ? n / 16 : 0;
+  const int g = grid_for(std::max<int64_t>(vec ? nunits : n, 1), kThreads,
+                         resident_per_sm(encode_kernel<SRC, FMT>, 0));
+  encode_kernel<SRC, FMT><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, nunits, scale);
+}
+
+void launch_encode_any(int sdt, int fmt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+  if (fmt == FP8B200_E4M3) {
+    if (sdt == FP8B200_F32) launch_encode<FP8B200_F32, FP8B200_E4M3>(src, dst, n, scale, st);
+    else if (sdt == FP8B200_BF16) launch_encode<FP8B200_BF16, FP8B200_E4M3>(src, dst, n, scale, st);
+    else launch_encode<FP8B200_F16, FP8B200_E4M3>(src, dst, n, scale, st);
+  } else {
+    if (sdt == FP8B200_F32) launch_encode<FP8B200_F32, FP8B200_E5M2>(src, dst, n, scale, st);
+    else if (sdt == FP8B200_BF16) launch_encode<FP8B200_BF16, FP8B200_E5M2>(src, dst, n, scale, st);
+    else launch_encode<FP8B200_F16, FP8B200_E5M2>(src, dst, n, scale, st);
+  }
+}
+
+template <int SRC>
+void launch_fp4_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+  const int64_t npairs = n / 2;
+  const int64_t nunits = (aligned32(src) && aligned16(dst)) ? n / 32 : 0;
+  const int g = grid_for(std::max<int64_t>(nunits ? nunits : npairs, 1), kThreads,
+                         resident_per_sm(fp4_encode_kernel<SRC>, 0));
+  fp4_encode_kernel<SRC><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, npairs, nunits, scale);
+}
+
+void launch_fp4_encode_any(int sdt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+  if (sdt == FP8B200_F32) launch_fp4_encode<FP8B200_F32>(src, dst, n, scale, st);
+  else if (sdt == FP8B200_BF16) launch_fp4_encode<FP8B200_BF16>(src, dst, n, scale, st);
+  else launch_fp4_encode<FP8B200_F16>(src, dst, n, scale, st);
+}
+
+bool is_float_dtype(int dt) { return dt == FP8B200_F32 || dt == FP8B200_BF16 || dt == FP8B200_F16; }
+bool is_fp8_dtype(int dt) { return dt == FP8B200_E4M3 || dt == FP8B200_E5M2; }
+
+int check_scale_mode(int mode, const float *scale, int odt) {
+  if (mode < FP8B200_SCALE_NONE || mode > FP8B200_SCALE_F16_REF)
+    return set_error(FP8B200_EINVAL, "unknown scale_mode %d", mode);
+  if (mode != FP8B200_SCALE_NONE && scale == nullptr)
+    return set_error(FP8B200_EINVAL, "scale_mode %d needs a scale pointer", mode);
+  if (mode == FP8B200_SCALE_F16_REF && odt != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "the f16 reference scale semantics produce float16 output only");
+  return FP8B200_OK;
+}
+
+int launch_amax_and_scale(const void *src, int src_dtype, int64_t n, float fmax, float *scale_out,
+                          uint32_t *amax_scratch, cudaStream_t st) {
+  if (cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t), st) != cudaSuccess)
+    return check_launch("quantize amax clear");
+  if (n > 0) {
+    const int eb = src_dtype == FP8B200_F32 ? 4 : 2;
+    const int64_t nunits = aligned32(src) ? (n * eb) / 32 : 0;
+    const int g = grid_for(std::max<int64_t>(nunits ? nunits : n, 1), kThreads, 4);
+    const uint8_t *s = (const uint8_t *)src;
+    if (src_dtype == FP8B200_F32) amax_kernel<FP8B200_F32><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
+    else if (src_dtype == FP8B200_BF16) amax_kernel<FP8B200_BF16><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
+    else amax_kernel<FP8B200_F16><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
+    count_launch();
+    if (int rc = check_launch("quantize amax")) return rc;
+  }
+  quant_scale_kernel<<<1, 1, 0, st>>>(amax_scratch, fmax, scale_out);
+  count_launch();
+  return check_launch("quantize scale");
+}
+
+}  // namespace
+}  // namespace fp8b200
+
+using namespace fp8b200;
+
+extern "C" int fp8b200_encode_fp8(const void *src, int src_dtype, void *dst, int fp8_dtype, int64_t n,
+                                  const float *scale, void *stream) {
+  if (n < 0) return set_error(FP8B200_EINVAL, "negative element count");
+  if (!is_float_dtype(src_dtype)) return set_error(FP8B200_EINVAL, "encode: source dtype %d is not f32/bf16/f16", src_dtype);
+  if (!is_fp8_dtype(fp8_dtype)) return set_error(FP8B200_EINVAL, "encode: target dtype %d is not e4m3fn/e5m2", fp8_dtype);
+  if (n == 0) return FP8B200_OK;
+  if (!src || !dst) return set_error(FP8B200_EINVAL, "encode: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  launch_encode_any(src_dtype, fp8_dtype, src, dst, n, scale, (cudaStream_t)stream);
+  count_launch();
+  return check_launch("fp8 encode");
+}
+
+extern "C" int fp8b200_decode_fp8(const void *src, int fp8_dtype, void *dst, int out_dtype, int64_t n,
+                                  const float *scale, int scale_mode, void *stream) {
+  if (n < 0) return set_error(FP8B200_EINVAL, "negative element count");
+  if (!is_fp8_dtype(fp8_dtype)) return set_error(FP8B200_EINVAL, "decode: source dtype %d is not e4m3fn/e5m2", fp8_dtype);
+  if (!is_float_dtype(out_dtype)) return set_error(FP8B200_EINVAL, "decode: output dtype %d is not f32/bf16/f16", out_dtype);
+  if (int rc = check_scale_mode(scale_mode, scale, out_dtype)) return rc;
+  if (n == 0) return FP8B200_OK;
+  if (!src || !dst) return set_error(FP8B200_EINVAL, "decode: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (aligned32(src) && aligned32(dst)) {
+    if (out_dtype == FP8B200_F32) launch_decode<false, 4>(src, dst, n, fp8_dtype, out_dtype, scale, scale_mode, st, dev);
+    else launch_decode<false, 2>(src, dst, n, fp8_dtype, out_dtype, scale, scale_mode, st, dev);
+  } else {
+    const int g = grid_for(n, kThreads, 4);
+    decode_scalar_kernel<<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, 0, fp8_dtype, out_dtype,
+                                                 scale, scale_mode);
+  }
+  count_launch();
+  return check_launch("fp8 decode");
+}
+
+extern "C" int fp8b200_decode_fp4(const void *src, int64_t nbytes, void *dst, int out_dtype, const float *scale,
+                                  int scale_mode, void *stream) {
+  if (nbytes < 0) return set_error(FP8B200_EINVAL, "negative byte count");
+  if (!is_float_dtype(out_dtype)) return set_error(FP8B200_EINVAL, "fp4 decode: output dtype %d is not f32/bf16/f16", out_dtype);
+  if (int rc = check_scale_mode(scale_mode, scale, out_dtype)) return rc;
+  if (nbytes == 0) return FP8B200_OK;
+  if (!src || !dst) return set_error(FP8B200_EINVAL, "fp4 decode: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (aligned32(src) && aligned32(dst)) {
+    if (out_dtype == FP8B200_F32) launch_decode<true, 4>(src, dst, nbytes, 0, out_dtype, scale, scale_mode, st, dev);
+    else launch_decode<true, 2>(src, dst, nbytes, 0, out_dtype, scale, scale_mode, st, dev);
+  } else {
+    const int g = grid_for(nbytes, kThreads, 4);
+    decode_scalar_kernel<<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, 1, 0, out_dtype,
+                                                 scale, scale_mode);
+  }
+  count_launch();
+  return check_launch("fp4 decode");
+}
+
+extern "C" int fp8b200_quantize_fp8(const void *src, int src_dtype, void *dst, int fp8_dtype, int64_t n,
+                                    float *scale_out, uint32_t *amax_scratch, void *stream) {
+  if (n < 0) return set_error(FP8B200_EINVAL, "negative element count");
+  if (!is_float_dtype(src_dtype)) return set_error(FP8B200_EINVAL, "quantize: source dtype %d is not f32/bf16/f16", src_dtype);
+  if (!is_fp8_dtype(fp8_dtype)) return set_error(FP8B200_EINVAL, "quantize: target dtype %d is not e4m3fn/e5m2", fp8_dtype);
+  if (!scale_out || !amax_scratch) return set_error(FP8B200_EINVAL, "quantize: null scale/scratch pointer");
+  if (n > 0 && (!src || !dst)) return set_error(FP8B200_EINVAL, "quantize: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
+  if (int rc = launch_amax_and_scale(src, src_dtype, n, fmax, scale_out, amax_scratch, st)) return rc;
+  if (n > 0) {
+    launch_encode_any(src_dtype, fp8_dtype, src, dst, n, scale_out, st);
+    count_launch();
+    return check_launch("quantize encode");
+  }
+  return FP8B200_OK;
+}
+
+extern "C" int fp8b200_encode_fp4(const void *src, int src_dtype, void *dst, int64_t n, const float *scale,
+                                  void *stream) {
+  if (n < 0 || (n & 1)) return set_error(FP8B200_EINVAL, "fp4 encode: element count must be even and non-negative");
+  if (!is_float_dtype(src_dtype)) return set_error(FP8B200_EINVAL, "fp4 encode: source dtype %d is not f32/bf16/f16", src_dtype);
+  if (n == 0) return FP8B200_OK;
+  if (!src || !dst) return set_error(FP8B200_EINVAL, "fp4 encode: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  launch_fp4_encode_any(src_dtype, src, dst, n, scale, (cudaStream_t)stream);
+  count_launch();
+  return check_launch("fp4 encode");
+}
+
+extern "C" int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, int64_t n, float *scale_out,
+                                    uint32_t *amax_scratch, void *stream) {
+  if (n < 0 || (n & 1)) return set_error(FP8B200_EINVAL, "fp4 quantize: element count must be even and non-negative");
+  if (!is_float_dtype(src_dtype)) return set_error(FP8B200_EINVAL, "fp4 quantize: source dtype %d is not f32/bf16/f16", src_dtype);
+  if (!scale_out || !amax_scratch) return set_error(FP8B200_EINVAL, "fp4 quantize: null scale/scratch pointer");
+  if (n > 0 && (!src || !dst)) return set_error(FP8B200_EINVAL, "fp4 quantize: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int rc = launch_amax_and_scale(src, src_dtype, n, 6.0f, scale_out, amax_scratch, st)) return rc;
+  if (n > 0) {
+    launch_fp4_encode_any(src_dtype, src, dst, n, scale_out, st);
+    count_launch();
+    return check_launch("fp4 quantize encode");
+  }
+  return FP8B200_OK;
+}

@@ -1,0 +1,541 @@
+// FP8 scaled GEMM for B200 on the 5th-generation tensor cores (tcgen05).
+//
+//   D[M,N] = (A[M,K] * sa) @ (B[N,K] * sb)^T  [+ bias[N]]  [* scale_result]
+//
+// A and B are float8 (e4m3fn or e5m2) codes with K contiguous ("K-major"), the
+// layout torch._scaled_mm requires (self row-major, mat2 column-major). The
+// accumulation is float32 in tensor memory (TMEM).
+//
+// Kernel structure (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: 128x128-byte A tiles and 256x128-byte B tiles,
+//               128-byte swizzled, into a 4-stage shared-memory ring
+//               (cp.async.bulk.tensor, no multicast; L2 gives the reuse).
+//   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::f8f6f4
+//               (M=128, N=256, K=32) into one of two TMEM accumulators
+//               (2 x 256 fp32 columns), commits to mbarriers.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp its own
+//               32-lane quarter), scale, bias, convert, store to global. The
+//               double-buffered accumulator lets the epilogue of tile i
+//               overlap the MMAs of tile i+1.
+// Every mbarrier wait is bounded (globaltimer): on timeout the kernel records
+// a status word, stops issuing, releases TMEM and returns; the host reads the
+// status with fp8b200_gemm_status().
+//
+// Replaces fp8_scaled_matmul_kernel / fp8_scaled_vecmat_kernel
+// (shaders/fp8_matmul.metal:145-226) and the decode + fp16 matmul path
+// (fp8_mps_native.py:129-159).
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace fp8b200 {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;           // bytes = fp8 elements per k-block (one 128B swizzle row)
+constexpr int STAGES = 4;
+constexpr int UMMA_K = 32;        // K per tcgen05.mma for 8-bit operands
+constexpr int A_BYTES = BM * BK;  // 16 KiB
+constexpr int B_BYTES = BN * BK;  // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;    // two 256-column fp32 accumulators
+constexpr int GROUP_M = 16;       // tile raster: 16 M-tiles per group for L2 reuse
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+struct Params {
+  int M, N, K, num_kb, tiles_m, tiles_n, num_tiles;
+  const float *sa, *sb;
+  int sa_rowwise, sb_rowwise;
+  const void *bias;
+  int bias_dtype;
+  const float *scale_result;
+  void *D;
+  long long ldd;
+  int out_dtype;
+  int vec_store;
+  uint32_t idesc;
+  unsigned long long timeout_ns;
+  int debug_skip_first_load;
+};
+
+// Status word: 0 = ok, otherwise (1 << 31) | site of the first wait that timed out.
+__device__ uint32_t g_status;
+
+// ------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on phase `parity` of `bar`; false on timeout or if another
+// role already recorded a failure.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long timeout_ns, uint32_t site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 31u) == 0) {
+      if (*reinterpret_cast<volatile uint32_t *>(&g_status) != 0) return false;
+      if (globaltimer() - t0 > timeout_ns) {
+        atomicCAS(&g_status, 0u, 0x80000000u | site);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+__device__ __forceinline__ void umma_f8f6f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive fp32 columns: thread t receives lane t's 32 values.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc_sw128_kmajor(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address, 16-byte units
+  d |= (uint64_t)1 << 16;                    // leading byte offset (unused for SW128 K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                    // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;                    // layout: SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void tile_coords(const Params &p, int tile, int &tm, int &tn) {
+  const int per_group = GROUP_M * p.tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsize = min(p.tiles_m - first_m, GROUP_M);
+  const int r = tile - group * per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+// ------------------------------------------------------------------ epilogue conversion
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+// fp8 encode with CPU PyTorch semantics (as in convert.cu): cvt.satfinite
+// plus the overflow / inf / NaN fix-up.
+template <int FMT>
+__device__ __forceinline__ uint32_t enc8(float x) {
+  const uint32_t b = __float_as_uint(x), a = b & 0x7FFFFFFFu, s = (b >> 24) & 0x80u;
+  uint16_t r;
+  if constexpr (FMT == FP8B200_E4M3) {
+    if (a > 0x43E80000u) return s | 0x7Fu;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
+  } else {
+    if (a > 0x7F800000u) return s | 0x7Fu;
+    if (a > 0x476FFFFFu) return s | 0x7Cu;
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
+  }
+  return r & 0xFFu;
+}
+
+__device__ __forceinline__ float load_bias(const void *bias, int dt, int col) {
+  if (dt == FP8B200_F32) return reinterpret_cast<const float *>(bias)[col];
+  if (dt == FP8B200_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(bias)[col]);
+  return __half2float(reinterpret_cast<const __half *>(bias)[col]);
+}
+
+// Scale, bias and store 32 consecutive columns of one output row.
+__device__ __forceinline__ void store_row_chunk(const Params &p, int row, int col0, const uint32_t (&acc)[32],
+                                                float row_scale, float tensor_scale_b, float sr) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    const int col = col0 + j;
+    float sbv = tensor_scale_b;
+    if (p.sb_rowwise) sbv = (col < p.N) ? __ldg(p.sb + col) : 0.0f;
+    float x = __uint_as_float(acc[j]) * (row_scale * sbv);
+    if (p.bias != nullptr && col < p.N) x += load_bias(p.bias, p.bias_dtype, col);
+    v[j] = x * sr;
+  }
+  const bool full = p.vec_store && (col0 + 32 <= p.N);
+  char *base = reinterpret_cast<char *>(p.D);
+  switch (p.out_dtype) {
+    case FP8B200_BF16:
+    case FP8B200_F16: {
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        w[j] = p.out_dtype == FP8B200_BF16 ? pack_bf16(v[2 * j], v[2 * j + 1]) : pack_f16(v[2 * j], v[2 * j + 1]);
+      uint16_t *rowp = reinterpret_cast<uint16_t *>(base) + (long long)row * p.ldd;
+      if (full) {
+        uint4 *dst = reinterpret_cast<uint4 *>(rowp + col0);
+#pragma unroll
+        for (int q = 0; q < 4; q++) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (col0 + j < p.N) rowp[col0 + j] = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+      }
+      break;
+    }
+    case FP8B200_F32: {
+      float *rowp = reinterpret_cast<float *>(base) + (long long)row * p.ldd;
+      if (full) {
+        float4 *dst = reinterpret_cast<float4 *>(rowp + col0);
+#pragma unroll
+        for (int q = 0; q < 8; q++) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (col0 + j < p.N) rowp[col0 + j] = v[j];
+      }
+      break;
+    }
+    default: {  // fp8 output
+      uint32_t w[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        uint32_t c[4];
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+          c[t] = p.out_dtype == FP8B200_E4M3 ? enc8<FP8B200_E4M3>(v[4 * q + t]) : enc8<FP8B200_E5M2>(v[4 * q + t]);
+        w[q] = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+      }
+      uint8_t *rowp = reinterpret_cast<uint8_t *>(base) + (long long)row * p.ldd;
+      if (full) {
+        uint4 *dst = reinterpret_cast<uint4 *>(rowp + col0);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (col0 + j < p.N) rowp[col0 + j] = (uint8_t)(w[j >> 2] >> (8 * (j & 3)));
+      }
+      break;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(THREADS, 1)
+scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled tiles
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const uint32_t sA = base;                     // STAGES x 16 KiB
+  const uint32_t sB = base + STAGES * A_BYTES;  // STAGES x 32 KiB
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  // barriers: full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], then the TMEM address slot
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 4);  // one arrival per epilogue warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (p.debug_skip_first_load) { ok = false; break; }  // test hook: never fill stage 0
+          mbar_expect_tx(full_bar(stage), STAGE_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmap_a, full_bar(stage), kb * BK, tm * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tmap_b, full_bar(stage), kb * BK, tn * BN);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128_kmajor(sA + stage * A_BYTES);
+          const uint64_t bdesc = sdesc_sw128_kmajor(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; k++) {
+            // advance along K inside the 128-byte swizzled row: +32 bytes
+            umma_f8f6f4(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
+                        p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));  // frees the smem stage once these MMAs finish
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, TMEM lane quarter = warp % 4
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
+    const float sb_t = p.sb_rowwise ? 0.0f : __ldg(p.sb);
+    const float sr = p.scale_result ? __ldg(p.scale_result) : 1.0f;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      // warp-uniform bounded wait
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = tm * BM + quarter * 32 + lane;
+      const float rs = p.sa_rowwise ? ((row < p.M) ? __ldg(p.sa + row) : 0.0f) : sa_t;
+      const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        const int col0 = tn * BN + c * 32;
+        if (row < p.M && col0 < p.N) store_row_chunk(p, row, col0, r, rs, sb_t, sr);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FP8B200_EINVAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FP8B200_OK;
+}
+
+unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
+int g_debug_skip_first_load = 0;
+
+}  // namespace gemm
+}  // namespace fp8b200
+
+using namespace fp8b200;
+using namespace fp8b200::gemm;
+
+extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const void *B, int b_dtype, int64_t ldb,
+                                 int64_t M, int64_t N, int64_t K, const float *scale_a, int scale_a_layout,
+                                 const float *scale_b, int scale_b_layout, const void *bias, int bias_dtype,
+                                 const float *scale_result, void *D, int out_dtype, int64_t ldd, void *stream) {
+  auto fp8 = [](int d) { return d == FP8B200_E4M3 || d == FP8B200_E5M2; };
+  if (!fp8(a_dtype) || !fp8(b_dtype)) return set_error(FP8B200_EINVAL, "scaled_mm: operands must be e4m3fn/e5m2");
+  if (out_dtype != FP8B200_F32 && out_dtype != FP8B200_BF16 && out_dtype != FP8B200_F16 && !fp8(out_dtype))
+    return set_error(FP8B200_EINVAL, "scaled_mm: unsupported output dtype %d", out_dtype);
+  if (M < 0 || N < 0 || K < 0) return set_error(FP8B200_EINVAL, "scaled_mm: negative size");
+  if (M == 0 || N == 0) return FP8B200_OK;
+  if (K == 0) return set_error(FP8B200_EINVAL, "scaled_mm: K must be positive");
+  if (K % 16) return set_error(FP8B200_EINVAL, "scaled_mm: K=%lld must be a multiple of 16", (long long)K);
+  if (M > 0x7FFFFFFFLL || N > 0x7FFFFFFFLL || K > 0x7FFFFFFFLL)
+    return set_error(FP8B200_EINVAL, "scaled_mm: dimension too large");
+  if (lda < K || ldb < K || (lda % 16) || (ldb % 16))
+    return set_error(FP8B200_EINVAL, "scaled_mm: row strides must be >= K and multiples of 16 bytes");
+  if (ldd < N) return set_error(FP8B200_EINVAL, "scaled_mm: output row stride < N");
+  if (!A || !B || !D || !scale_a || !scale_b) return set_error(FP8B200_EINVAL, "scaled_mm: null pointer");
+  if (!aligned16(A) || !aligned16(B)) return set_error(FP8B200_EINVAL, "scaled_mm: operands must be 16-byte aligned");
+  if ((scale_a_layout != FP8B200_SCALE_TENSOR && scale_a_layout != FP8B200_SCALE_ROWWISE) ||
+      (scale_b_layout != FP8B200_SCALE_TENSOR && scale_b_layout != FP8B200_SCALE_ROWWISE))
+    return set_error(FP8B200_EINVAL, "scaled_mm: unknown scale layout");
+  if (bias && bias_dtype != FP8B200_F32 && bias_dtype != FP8B200_BF16 && bias_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "scaled_mm: bias must be f32/bf16/f16");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+
+  CUtensorMap ma, mb;
+  if (int rc = make_kmajor_map(&ma, A, M, K, lda, BM)) return rc;
+  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, BN)) return rc;
+
+  Params p;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.sa = scale_a; p.sb = scale_b;
+  p.sa_rowwise = scale_a_layout == FP8B200_SCALE_ROWWISE;
+  p.sb_rowwise = scale_b_layout == FP8B200_SCALE_ROWWISE;
+  p.bias = bias; p.bias_dtype = bias_dtype;
+  p.scale_result = scale_result;
+  p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
+  const int esz = dtype_size(out_dtype);
+  p.vec_store = aligned16(D) && ((ldd * esz) % 16 == 0);
+  const uint32_t afmt = a_dtype == FP8B200_E5M2 ? 1u : 0u, bfmt = b_dtype == FP8B200_E5M2 ? 1u : 0u;
+  // instruction descriptor: f32 accumulate, A/B formats, both K-major, N>>3, M>>4
+  p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  p.timeout_ns = g_timeout_ns;
+  p.debug_skip_first_load = g_debug_skip_first_load;
+
+  static bool attr_done[64] = {};
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(scaled_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  const int grid = std::min(p.num_tiles, current_sm_count());
+  scaled_mm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
+  count_launch();
+  return check_launch("scaled_mm");
+}
+
+extern "C" int fp8b200_gemm_status(uint32_t *status_out, int reset) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+  if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "gemm status read: %s", cudaGetErrorString(e));
+  if (status_out) *status_out = v;
+  if (reset) {
+    const uint32_t z = 0;
+    e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
+    if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "gemm status reset: %s", cudaGetErrorString(e));
+  }
+  return v ? FP8B200_ETIMEOUT : FP8B200_OK;
+}
+
+extern "C" int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns) {
+  g_debug_skip_first_load = skip_first_load ? 1 : 0;
+  g_timeout_ns = wait_timeout_ns ? wait_timeout_ns : 2000000000ull;
+  return FP8B200_OK;
+}

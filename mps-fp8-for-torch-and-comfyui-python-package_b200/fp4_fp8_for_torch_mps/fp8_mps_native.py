@@ -1,0 +1,303 @@
+"""Host launchers for the B200 FP8/FP4 kernels.
+
+Same function names, argument meaning and return conventions as the
+reference's launcher module (fp8_mps_native.py:26-221), so code and tests
+written against the reference keep working; the Metal dispatch
+(`lib.<kernel>(..., threads=, group_size=)`) becomes a call into the C ABI of
+libfp8_b200.so (include/fp8_b200.h) on the tensor's device and current CUDA
+stream. Outputs are allocated here with torch.empty (the C ABI never
+allocates). There is no CPU fallback: inputs on the CPU are moved to the
+current CUDA device, as the reference moves them to "mps".
+
+Additions beyond the reference (used by the aten overrides in ops.py):
+`encode_fp8` / `decode_fp8` for both fp8 formats and any float dtype,
+`quantize_fp8`, `fp4_decode` (shape-preserving, any float dtype, f32
+scale), and `scaled_mm` with torch._scaled_mm's full argument set.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+_FP8 = (torch.float8_e4m3fn, torch.float8_e5m2)
+_FLOAT = (torch.float32, torch.bfloat16, torch.float16)
+_scratch: dict[int, torch.Tensor] = {}
+
+
+# ----------------------------------------------------------------- helpers
+def _on_cuda(t: torch.Tensor) -> torch.Tensor:
+    if t.device.type != "cuda":
+        t = t.to("cuda")
+    return t
+
+
+def _as_float_src(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous f32/bf16/f16 CUDA tensor (other dtypes are cast to f32 first,
+    as the reference does with `.to(dtype=torch.float32)`)."""
+    t = _on_cuda(t)
+    if t.dtype not in _FLOAT:
+        t = t.to(torch.float32)
+    return t.contiguous()
+
+
+def _scale_f32(scale, device) -> torch.Tensor:
+    if not isinstance(scale, torch.Tensor):
+        scale = torch.tensor([float(scale)], dtype=torch.float32)
+    return scale.to(device=device, dtype=torch.float32).reshape(-1)[:1].contiguous()
+
+
+def _amax_scratch(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _scratch.get(idx)
+    if t is None:
+        t = torch.empty(1, dtype=torch.int32, device=device)
+        _scratch[idx] = t
+    return t
+
+
+def _check_out(out, dtype, numel, device, what):
+    if (out.dtype != dtype or out.numel() != numel or not out.is_contiguous()
+            or out.device != device):
+        raise RuntimeError(f"{what}: `out` must be a contiguous {dtype} tensor of {numel} elements "
+                           f"on {device}")
+
+
+# ----------------------------------------------------------------- fp8 encode / decode
+def encode_fp8(x: torch.Tensor, fp8_dtype: torch.dtype = torch.float8_e4m3fn,
+               out: torch.Tensor | None = None, scale: torch.Tensor | None = None) -> torch.Tensor:
+    """x (f32/bf16/f16, any shape) -> uint8 codes of `fp8_dtype`, bit-exact with
+    CPU `x.to(fp8_dtype)`. `out` (contiguous 1-byte tensor, same numel) is
+    written in place when given."""
+    if fp8_dtype not in _FP8:
+        raise RuntimeError(f"encode_fp8: {fp8_dtype} is not an fp8 dtype")
+    src = _as_float_src(x)
+    if out is None:
+        out = torch.empty(src.shape, dtype=torch.uint8, device=src.device)
+    if out.numel() != src.numel() or not out.is_contiguous() or out.element_size() != 1:
+        raise RuntimeError("encode_fp8: `out` must be a contiguous 1-byte tensor with x's numel")
+    if out.device != src.device:
+        raise RuntimeError("encode_fp8: `out` is on another device")
+    sc = None if scale is None else _scale_f32(scale, src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_encode_fp8(src.data_ptr(), L.dtype_code(src.dtype), out.data_ptr(),
+                                           L.dtype_code(fp8_dtype), src.numel(), L.ptr(sc),
+                                           L.stream_of(src)), "fp8 encode")
+    return out
+
+
+def decode_fp8(codes: torch.Tensor, fp8_dtype: torch.dtype, out_dtype: torch.dtype,
+               scale=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp8 codes (uint8 or fp8 tensor) -> out_dtype, same shape, bit-exact with
+    CPU `codes.view(fp8_dtype).to(out_dtype)` (times `scale` in f32 when
+    given: one f32 product, one rounding to out_dtype). `out` (contiguous,
+    out_dtype, same numel) is written in place when given."""
+    if fp8_dtype not in _FP8 or out_dtype not in _FLOAT:
+        raise RuntimeError(f"decode_fp8: unsupported {fp8_dtype} -> {out_dtype}")
+    src = _on_cuda(codes)
+    if src.element_size() != 1:
+        raise RuntimeError("decode_fp8: input must hold 1-byte codes")
+    src = src.contiguous()
+    if out is None:
+        out = torch.empty(src.shape, dtype=out_dtype, device=src.device)
+    else:
+        _check_out(out, out_dtype, src.numel(), src.device, "decode_fp8")
+    sc = None if scale is None else _scale_f32(scale, src.device)
+    mode = L.SCALE_NONE if sc is None else L.SCALE_F32
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_decode_fp8(src.data_ptr(), L.dtype_code(fp8_dtype), out.data_ptr(),
+                                           L.dtype_code(out_dtype), src.numel(), L.ptr(sc), mode,
+                                           L.stream_of(src)), "fp8 decode")
+    return out
+
+
+def fp8_encode(input):
+    """float -> float8_e4m3fn codes as uint8, same shape (fp8_mps_native.py:85-98)."""
+    return encode_fp8(input, torch.float8_e4m3fn)
+
+
+def fp8_dequantize(input, scale):
+    """e4m3 codes -> f16, same shape, times scale with the reference's f16
+    arithmetic (fp8_mps_native.py:65-82)."""
+    src = _on_cuda(input)
+    if src.element_size() != 1:
+        raise RuntimeError("fp8_dequantize: input must hold 1-byte codes")
+    src = src.contiguous()
+    out = torch.empty(src.shape, dtype=torch.float16, device=src.device)
+    sc = _scale_f32(scale, src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_decode_fp8(src.data_ptr(), L.E4M3, out.data_ptr(), L.F16,
+                                           src.numel(), sc.data_ptr(), L.SCALE_F16_REF,
+                                           L.stream_of(src)), "fp8 dequantize")
+    return out
+
+
+def quantize_fp8(input, fp8_dtype: torch.dtype = torch.float8_e4m3fn):
+    """Per-tensor dynamic quantisation on the device, no host sync:
+    returns (codes uint8 same shape, f32[2] = [scale, 1/scale])."""
+    if fp8_dtype not in _FP8:
+        raise RuntimeError(f"quantize_fp8: {fp8_dtype} is not an fp8 dtype")
+    src = _as_float_src(input)
+    out = torch.empty(src.shape, dtype=torch.uint8, device=src.device)
+    scales = torch.empty(2, dtype=torch.float32, device=src.device)
+    scratch = _amax_scratch(src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_quantize_fp8(src.data_ptr(), L.dtype_code(src.dtype), out.data_ptr(),
+                                             L.dtype_code(fp8_dtype), src.numel(), scales.data_ptr(),
+                                             scratch.data_ptr(), L.stream_of(src)), "fp8 quantize")
+    return out, scales
+
+
+def fp8_quantize(input):
+    """amax-scaled e4m3 encode; returns (codes, inv_scale f32[1])
+    (fp8_mps_native.py:101-120), with the scale computed on the device."""
+    out, scales = quantize_fp8(input, torch.float8_e4m3fn)
+    return out, scales[1:2]
+
+
+# ----------------------------------------------------------------- fp4
+def fp4_decode(packed: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+               scale=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed e2m1 pairs (uint8 or float4_e2m1fn_x2, shape (..., B)) ->
+    out_dtype of shape (..., 2B), low nibble first, times `scale` in f32.
+    `out` (contiguous, out_dtype, 2x the input's numel) is written in place
+    when given."""
+    if out_dtype not in _FLOAT:
+        raise RuntimeError(f"fp4_decode: unsupported output dtype {out_dtype}")
+    src = _on_cuda(packed)
+    if src.element_size() != 1:
+        raise RuntimeError("fp4_decode: input must hold packed bytes")
+    src = src.contiguous()
+    shape = tuple(src.shape[:-1]) + (src.shape[-1] * 2,) if src.dim() else (2,)
+    if out is None:
+        out = torch.empty(shape, dtype=out_dtype, device=src.device)
+    else:
+        _check_out(out, out_dtype, 2 * src.numel(), src.device, "fp4_decode")
+    sc = None if scale is None else _scale_f32(scale, src.device)
+    mode = L.SCALE_NONE if sc is None else L.SCALE_F32
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_decode_fp4(src.data_ptr(), src.numel(), out.data_ptr(),
+                                           L.dtype_code(out_dtype), L.ptr(sc), mode,
+                                           L.stream_of(src)), "fp4 decode")
+    return out
+
+
+def fp4_dequantize(input, scale):
+    """Packed bytes -> 1-D f16 of 2*numel values times scale, with the
+    reference's f16 arithmetic (fp8_mps_native.py:162-179)."""
+    src = _on_cuda(input)
+    if src.element_size() != 1:
+        raise RuntimeError("fp4_dequantize: input must hold packed bytes")
+    src = src.contiguous()
+    out = torch.empty(src.numel() * 2, dtype=torch.float16, device=src.device)
+    sc = _scale_f32(scale, src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_decode_fp4(src.data_ptr(), src.numel(), out.data_ptr(), L.F16,
+                                           sc.data_ptr(), L.SCALE_F16_REF, L.stream_of(src)),
+                "fp4 dequantize")
+    return out
+
+
+def fp4_encode(input):
+    """float -> packed e2m1 pairs, 1-D uint8 [numel/2], the reference's
+    nearest-of-8 thresholds (fp8_mps_native.py:182-197)."""
+    src = _as_float_src(input)
+    if src.numel() % 2:
+        raise RuntimeError("FP4 x2 requires even number of elements")
+    out = torch.empty(src.numel() // 2, dtype=torch.uint8, device=src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_encode_fp4(src.data_ptr(), L.dtype_code(src.dtype), out.data_ptr(),
+                                           src.numel(), None, L.stream_of(src)), "fp4 encode")
+    return out
+
+
+def fp4_quantize(input):
+    """amax-scaled (6/amax) FP4 encode; returns (packed, inv_scale f32[1])
+    (fp8_mps_native.py:200-221)."""
+    src = _as_float_src(input)
+    if src.numel() % 2:
+        raise RuntimeError("FP4 x2 requires even number of elements")
+    out = torch.empty(src.numel() // 2, dtype=torch.uint8, device=src.device)
+    scales = torch.empty(2, dtype=torch.float32, device=src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_quantize_fp4(src.data_ptr(), L.dtype_code(src.dtype), out.data_ptr(),
+                                             src.numel(), scales.data_ptr(),
+                                             _amax_scratch(src.device).data_ptr(),
+                                             L.stream_of(src)), "fp4 quantize")
+    return out, scales[1:2]
+
+
+# ----------------------------------------------------------------- scaled GEMM
+def scaled_mm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+              bias: torch.Tensor | None = None, scale_result: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16,
+              a_dtype: torch.dtype = torch.float8_e4m3fn,
+              b_dtype: torch.dtype = torch.float8_e4m3fn,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """D = (A * scale_a) @ (B * scale_b)^T [+ bias] [* scale_result].
+
+    a: (M, K) fp8 codes, rows contiguous; b_nk: (N, K) fp8 codes, rows
+    contiguous (the bytes of torch._scaled_mm's column-major mat2).
+    scale_a: 1 value or M values; scale_b: 1 value or N values (float32).
+    """
+    if a.dim() != 2 or b_nk.dim() != 2:
+        raise RuntimeError("scaled_mm: inputs must be 2-D")
+    M, K = a.shape
+    N, Kb = b_nk.shape
+    if Kb != K:
+        raise RuntimeError(f"scaled_mm: K mismatch ({K} vs {Kb})")
+    dev = a.device
+    if b_nk.device != dev:
+        raise RuntimeError("scaled_mm: operands on different devices")
+    if a.stride(1) != 1 or b_nk.stride(1) != 1:
+        raise RuntimeError("scaled_mm: operand rows must be contiguous along K")
+    sa = scale_a.to(device=dev, dtype=torch.float32).contiguous()
+    sb = scale_b.to(device=dev, dtype=torch.float32).contiguous()
+    la = L.SCALE_TENSOR if sa.numel() == 1 else L.SCALE_ROWWISE
+    lb = L.SCALE_TENSOR if sb.numel() == 1 else L.SCALE_ROWWISE
+    if la == L.SCALE_ROWWISE and sa.numel() != M:
+        raise RuntimeError(f"scaled_mm: scale_a has {sa.numel()} values, expected 1 or {M}")
+    if lb == L.SCALE_ROWWISE and sb.numel() != N:
+        raise RuntimeError(f"scaled_mm: scale_b has {sb.numel()} values, expected 1 or {N}")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=dev)
+    elif out.dtype != out_dtype or tuple(out.shape) != (M, N) or out.stride(1) != 1 or out.device != dev:
+        raise RuntimeError("scaled_mm: `out` must be an (M, N) out_dtype tensor with contiguous rows")
+    if bias is not None:
+        bias = bias.to(dev).contiguous()
+        if bias.numel() != N or bias.dtype not in _FLOAT:
+            raise RuntimeError("scaled_mm: bias must hold N float values")
+    sr = None if scale_result is None else _scale_f32(scale_result, dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().fp8b200_scaled_mm(
+            a.data_ptr(), L.dtype_code(a_dtype), a.stride(0),
+            b_nk.data_ptr(), L.dtype_code(b_dtype), b_nk.stride(0),
+            M, N, K,
+            sa.data_ptr(), la, sb.data_ptr(), lb,
+            L.ptr(bias), L.dtype_code(bias.dtype) if bias is not None else 0,
+            L.ptr(sr), out.data_ptr(), L.dtype_code(out_dtype), out.stride(0),
+            L.stream_of(a)), "scaled_mm")
+    return out
+
+
+def fp8_scaled_mm(A, B, scale_a, scale_b):
+    """A (M,K) e4m3 bytes, B (N,K) e4m3 bytes -> f32 (M,N)
+    (fp8_mps_native.py:26-62; scales: one value or one per row/column)."""
+    if A.dtype != torch.uint8 or B.dtype != torch.uint8:
+        raise RuntimeError("fp8_scaled_mm expects uint8 operands")
+    if not (A.is_contiguous() and B.is_contiguous()):
+        raise RuntimeError("fp8_scaled_mm expects contiguous operands")
+    A = _on_cuda(A)
+    B = B.to(A.device)
+    return scaled_mm(A, B, scale_a, scale_b, out_dtype=torch.float32)
+
+
+def fp8_scaled_mm_auto(A, B, scale_a, scale_b):
+    """Shape-based kernel choice happens inside the library (fp8_mps_native.py:123-126)."""
+    return fp8_scaled_mm(A.contiguous(), B.contiguous(), scale_a, scale_b)
+
+
+def fp8_scaled_mm_fast(A, B, scale_a, scale_b):
+    """The reference's decode + fp16 matmul path (fp8_mps_native.py:129-159);
+    here the same tensor-core GEMM as every other size."""
+    return fp8_scaled_mm(A.contiguous(), B.contiguous(), scale_a, scale_b)
