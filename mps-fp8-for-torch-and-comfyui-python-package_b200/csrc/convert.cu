@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 namespace fp8b200 {
@@ -494,20 +495,23 @@ __global__ void quant_scale_kernel(const uint32_t *__restrict__ amax_bits, float
 // ------------------------------------------------------------------ launch helpers
 // Resident CTAs per SM for `kernel` (queried once per kernel and device),
 // after raising its dynamic shared-memory limit when it needs more than 48 KiB.
-template <typename K>
-int resident_per_sm(K kernel, int smem_bytes) {
-  static int cached[64] = {};
+// The cache is keyed by the kernel's address: many kernels share one type.
+int resident_per_sm(const void *kernel, int smem_bytes) {
+  struct Entry { const void *k; int dev; int n; };
+  static Entry cache[128];
+  static int used = 0;
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 1;
-  if (!cached[dev]) {
-    if (smem_bytes > 48 * 1024)
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem_bytes) != cudaSuccess || n < 1) n = 1;
-    cached[dev] = n;
-  }
-  return cached[dev];
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; i++)
+    if (cache[i].k == kernel && cache[i].dev == dev) return cache[i].n;
+  if (smem_bytes > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem_bytes) != cudaSuccess || n < 1) n = 1;
+  if (used < 128) cache[used++] = Entry{kernel, dev, n};
+  return n;
 }
 
 template <bool FP4, int OUT_BYTES>
@@ -515,7 +519,7 @@ void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt,
                    cudaStream_t st, int dev) {
   constexpr int smem = Lut<FP4, OUT_BYTES>::kBytes;
   constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
-  const int per_sm = resident_per_sm(decode_kernel<FP4, OUT_BYTES>, smem);
+  const int per_sm = resident_per_sm((const void *)decode_kernel<FP4, OUT_BYTES>, smem);
   const int g = grid_for(std::max<int64_t>(nbytes / IB, 1), kThreads, per_sm);
   decode_kernel<FP4, OUT_BYTES><<<g, kThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, fmt, odt,
                                                            scale, mode);
@@ -526,7 +530,7 @@ void launch_encode(const void *src, void *dst, int64_t n, const float *scale, cu
   const bool vec = aligned32(src) && aligned16(dst);
   const int64_t nunits = vec ? n / 16 : 0;
   const int g = grid_for(std::max<int64_t>(vec ? nunits : n, 1), kThreads,
-                         resident_per_sm(encode_kernel<SRC, FMT>, 0));
+                         resident_per_sm((const void *)encode_kernel<SRC, FMT>, 0));
   encode_kernel<SRC, FMT><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, nunits, scale);
 }
 
@@ -547,7 +551,7 @@ void launch_fp4_encode(const void *src, void *dst, int64_t n, const float *scale
   const int64_t npairs = n / 2;
   const int64_t nunits = (aligned32(src) && aligned16(dst)) ? n / 32 : 0;
   const int g = grid_for(std::max<int64_t>(nunits ? nunits : npairs, 1), kThreads,
-                         resident_per_sm(fp4_encode_kernel<SRC>, 0));
+                         resident_per_sm((const void *)fp4_encode_kernel<SRC>, 0));
   fp4_encode_kernel<SRC><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, npairs, nunits, scale);
 }
 

@@ -285,8 +285,10 @@ def _cuda_copy_(keyset, self, src, non_blocking=False):
     nat = _native()
     with torch.cuda.device(self.device):
         if route == COPY_RAW:
+            # 1-byte dtypes on both sides: byte views keep any strides, and a
+            # uint8 copy_ passes straight through this override
             torch.ops.aten.copy_.default.redispatch(
-                ks, self.view(torch.uint8), src.contiguous().view(torch.uint8), non_blocking)
+                ks, self.view(torch.uint8), src.view(torch.uint8), non_blocking)
             return self
         # move the source to the destination device first (it is the smaller
         # side for a decode)

@@ -1,0 +1,82 @@
+"""Row sharding across ranks (host logic): gloo process groups on CPU with
+world sizes 2 and 4. The conversion applied per shard is CPU PyTorch's own
+(the kernels need a GPU); what is tested is the partition and the
+replicated-output gather."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from fp4_fp8_for_torch_mps.parallel import gather_rows, shard_rows, sharded_rows_apply, sharded_scaled_mm
+
+
+@pytest.mark.parametrize("total,ws", [(0, 2), (1, 4), (7, 2), (16, 4), (1000, 8), (16384, 8)])
+def test_shard_rows_partition(total, ws):
+    blocks = [shard_rows(total, ws, r) for r in range(ws)]
+    assert blocks[0][0] == 0 and blocks[-1][1] == total
+    for (s0, e0), (s1, e1) in zip(blocks, blocks[1:]):
+        assert e0 == s1
+    sizes = [e - s for s, e in blocks]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_single_process_is_identity():
+    x = torch.randn(5, 3)
+    assert torch.equal(sharded_rows_apply(x, lambda t: t * 2), x * 2)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, ws, port, rows, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        _body(rank, ws, rows, q)
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _body(rank, ws, rows, q):
+    if True:
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(rows, 24, generator=g) * 50
+        enc = sharded_rows_apply(x, lambda t: t.to(torch.float8_e4m3fn), gather=True)
+        ok1 = torch.equal(enc.view(torch.uint8), x.to(torch.float8_e4m3fn).view(torch.uint8))
+        local = sharded_rows_apply(x, lambda t: t.to(torch.float8_e5m2))
+        s, e = shard_rows(rows, ws, rank)
+        ok2 = torch.equal(local.view(torch.uint8), x[s:e].to(torch.float8_e5m2).view(torch.uint8))
+        a = (torch.randn(rows, 32, generator=g) * 10).to(torch.float8_e4m3fn)
+        b = (torch.randn(16, 32, generator=g) * 10).to(torch.float8_e4m3fn)
+        sc = torch.tensor(0.5)
+        full = sharded_scaled_mm(a, b.t(), sc, sc, gather=True, out_dtype=torch.float32)
+        ok3 = torch.equal(full, torch._scaled_mm(a, b.t(), sc, sc, out_dtype=torch.float32))
+        back = gather_rows(local, rows)
+        ok4 = torch.equal(back.view(torch.uint8), x.to(torch.float8_e5m2).view(torch.uint8))
+        q.put((rank, ok1, ok2, ok3, ok4))
+
+
+@pytest.mark.parametrize("ws,rows", [(2, 37), (4, 64), (4, 3)])
+def test_gloo_sharded_convert_and_gather(ws, rows):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, rows, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(ws)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(len(r) == 5 and all(r[1:]) for r in res), res
