@@ -102,6 +102,24 @@ int fp8b200_quantize_fp8(const void *src, int src_dtype, void *dst, int fp8_dtyp
                          void *stream);
 
 /*
+ * Allocation-free fp8b200_quantize_fp8 (no counterpart in the reference; the
+ * reference has no device memory management of its own). Same inputs,
+ * outputs and results, but no amax_scratch argument: the scratch is a fixed
+ * 16 KiB array inside this library's device memory (one amax partial per
+ * 65536 elements), so a caller that cannot allocate device memory, such as a
+ * host runtime that only passes in the tensors to read and write, needs
+ * nothing beyond src, dst and scale_out.
+ * Limits: n <= FP8B200_NOALLOC_MAX_ELEMENTS, else FP8B200_EINVAL. The first
+ * call on each device looks up the array's device address (make that first
+ * call before any stream capture). Every call shares the array: calls that
+ * overlap on the GPU (other streams or threads) race and must be serialised.
+ * Each GPU that loads the library holds the array until the process exits.
+ */
+#define FP8B200_NOALLOC_MAX_ELEMENTS (4096LL * 65536LL)
+int fp8b200_quantize_fp8_noalloc(const void *src, int src_dtype, void *dst, int fp8_dtype,
+                                 int64_t n, float *scale_out, void *stream);
+
+/*
  * float -> float4_e2m1fn_x2 encode of n (even) contiguous elements into n/2
  * packed bytes, element 2i in the low nibble, with the reference's
  * nearest-of-8 thresholds (not round-to-nearest-even at ties; NaN -> +6).

@@ -1,0 +1,152 @@
+// Allocation-free per-tensor FP8 quantisation.
+//
+// fp8b200_quantize_fp8 needs one word of device scratch (the amax
+// accumulator) that its caller must allocate. Some callers cannot allocate
+// device memory at the point where they quantise: a host runtime or plugin
+// ABI that owns a fixed device arena and only hands this library the tensors
+// it should read and write, or code that must not enter the CUDA allocator on
+// that path. For them, fp8b200_quantize_fp8_noalloc keeps its scratch in a
+// fixed array in this library's own device memory instead.
+//
+// Scratch layout: one max-|x| partial per slice of kSliceElems input
+// elements, kSlices slots (16 KiB). Every slot a call reads was written
+// earlier in the same call, so nothing has to be cleared between calls; the
+// array keeps the last call's partials. Two calls that run at the same time
+// on the GPU (different streams, or different host threads) share the array
+// and race: serialise them.
+#include "common.cuh"
+
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+namespace fp8b200 {
+namespace noalloc {
+
+constexpr int64_t kSliceElems = 65536;
+constexpr int kSlices = 4096;
+constexpr int64_t kMaxElems = kSliceElems * kSlices;  // 2^28 elements
+constexpr int kThreads = 256;
+
+// The scratch. In host code this name is only a stand-in for the symbol: the
+// device address comes from cudaGetSymbolAddress (scratch_ptr below).
+static __device__ __align__(256) uint32_t g_amax_partials[kSlices];
+
+template <int SRC>
+__device__ __forceinline__ uint32_t abs_bits(const void *src, int64_t i) {
+  if constexpr (SRC == FP8B200_F32) {
+    return reinterpret_cast<const uint32_t *>(src)[i] & 0x7FFFFFFFu;
+  } else if constexpr (SRC == FP8B200_BF16) {
+    return ((uint32_t)reinterpret_cast<const uint16_t *>(src)[i] << 16) & 0x7FFFFFFFu;
+  } else {
+    const float f = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t *>(src)[i]));
+    return __float_as_uint(f) & 0x7FFFFFFFu;
+  }
+}
+
+// One block per slice: partials[b] = max |x| over slice b, as float bits
+// (NaN sorts above inf, so a NaN anywhere wins, as in the allocating path).
+template <int SRC>
+__global__ void __launch_bounds__(kThreads)
+slice_amax_kernel(const void *__restrict__ src, int64_t n, uint32_t *__restrict__ partials) {
+  const int64_t begin = (int64_t)blockIdx.x * kSliceElems;
+  const int64_t end = min(n, begin + kSliceElems);
+  uint32_t m = 0;
+  for (int64_t i = begin + threadIdx.x; i < end; i += kThreads) m = max(m, abs_bits<SRC>(src, i));
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t warp_max[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t r = threadIdx.x < kThreads / 32 ? warp_max[threadIdx.x] : 0u;
+    r = __reduce_max_sync(0xFFFFFFFFu, r);
+    if (threadIdx.x == 0) partials[blockIdx.x] = r;
+  }
+}
+
+// One block: amax over the first `nslices` partials, then scale = fmax/amax
+// (1 when amax is 0 or NaN) and its reciprocal, in double as the allocating
+// path computes them.
+__global__ void __launch_bounds__(1024)
+scale_from_partials_kernel(const uint32_t *__restrict__ partials, int nslices, float fmax,
+                           float *__restrict__ scale_out) {
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < nslices; i += blockDim.x) m = max(m, partials[i]);
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t warp_max[32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t r = threadIdx.x < blockDim.x / 32 ? warp_max[threadIdx.x] : 0u;
+    r = __reduce_max_sync(0xFFFFFFFFu, r);
+    if (threadIdx.x == 0) {
+      const double a = (double)__uint_as_float(r);
+      const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+      scale_out[0] = (float)sd;
+      scale_out[1] = (float)(1.0 / sd);
+    }
+  }
+}
+
+// Device address of the scratch array, looked up once per device with that
+// device current.
+constexpr int kMaxDevices = 64;
+std::once_flag g_once[kMaxDevices];
+uint32_t *g_ptr[kMaxDevices] = {};
+cudaError_t g_lookup_err[kMaxDevices] = {};
+
+int scratch_ptr(int dev, uint32_t **out) {
+  std::call_once(g_once[dev], [dev] {
+    void *p = nullptr;
+    g_lookup_err[dev] = cudaGetSymbolAddress(&p, g_amax_partials);
+    g_ptr[dev] = static_cast<uint32_t *>(p);
+  });
+  if (g_lookup_err[dev] != cudaSuccess || g_ptr[dev] == nullptr)
+    return set_error(FP8B200_ELAUNCH, "quantize_noalloc: cudaGetSymbolAddress failed: %s",
+                     cudaGetErrorString(g_lookup_err[dev]));
+  *out = g_ptr[dev];
+  return FP8B200_OK;
+}
+
+}  // namespace noalloc
+}  // namespace fp8b200
+
+using namespace fp8b200;
+
+extern "C" int fp8b200_quantize_fp8_noalloc(const void *src, int src_dtype, void *dst, int fp8_dtype, int64_t n,
+                                            float *scale_out, void *stream) {
+  using namespace fp8b200::noalloc;
+  if (n < 0) return set_error(FP8B200_EINVAL, "quantize_noalloc: negative element count");
+  if (n > kMaxElems)
+    return set_error(FP8B200_EINVAL,
+                     "quantize_noalloc: %lld elements exceed the limit of %lld (its fixed scratch holds %d "
+                     "partials of %lld elements); use fp8b200_quantize_fp8 with caller-provided scratch",
+                     (long long)n, (long long)kMaxElems, kSlices, (long long)kSliceElems);
+  if (src_dtype != FP8B200_F32 && src_dtype != FP8B200_BF16 && src_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "quantize_noalloc: source dtype %d is not f32/bf16/f16", src_dtype);
+  if (fp8_dtype != FP8B200_E4M3 && fp8_dtype != FP8B200_E5M2)
+    return set_error(FP8B200_EINVAL, "quantize_noalloc: target dtype %d is not e4m3fn/e5m2", fp8_dtype);
+  if (!scale_out) return set_error(FP8B200_EINVAL, "quantize_noalloc: null scale pointer");
+  if (n > 0 && (!src || !dst)) return set_error(FP8B200_EINVAL, "quantize_noalloc: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  if (dev >= kMaxDevices) return set_error(FP8B200_EDEVICE, "quantize_noalloc: device index %d too large", dev);
+  uint32_t *partials;
+  if (int rc = scratch_ptr(dev, &partials)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int nslices = (int)((n + kSliceElems - 1) / kSliceElems);
+  if (nslices > 0) {
+    if (src_dtype == FP8B200_F32) slice_amax_kernel<FP8B200_F32><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    else if (src_dtype == FP8B200_BF16) slice_amax_kernel<FP8B200_BF16><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    else slice_amax_kernel<FP8B200_F16><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    count_launch();
+    if (int rc = check_launch("quantize_noalloc amax")) return rc;
+  }
+  const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
+  scale_from_partials_kernel<<<1, 1024, 0, st>>>(partials, nslices, fmax, scale_out);
+  count_launch();
+  if (int rc = check_launch("quantize_noalloc scale")) return rc;
+  // the encode pass is the library's ordinary encoder, reading the scale the
+  // previous kernel wrote on the same stream
+  return fp8b200_encode_fp8(src, src_dtype, dst, fp8_dtype, n, scale_out, stream);
+}
