@@ -102,6 +102,19 @@ int fp8b200_quantize_fp8(const void *src, int src_dtype, void *dst, int fp8_dtyp
                          void *stream);
 
 /*
+ * Per-row (per-token) dynamic quantisation of a rows x cols matrix (row
+ * strides ld_src / ld_dst in elements): for each row r, amax_r = max|x_r|,
+ * scale_r = fmax/amax_r (1 if amax_r is 0 or NaN), dst_r = encode(x_r *
+ * scale_r), inv_scale[r] = 1/scale_r. One launch, no scratch, no host sync;
+ * inv_scale is the (M,1) scale_a of a rowwise fp8b200_scaled_mm.
+ * Generalises fp8_quantize (fp8_mps_native.py:101-120) from one scale per
+ * tensor to one scale per row.
+ */
+int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t rows, int64_t cols,
+                              int64_t ld_src, void *dst, int64_t ld_dst, int fp8_dtype,
+                              float *inv_scale, void *stream);
+
+/*
  * Allocation-free fp8b200_quantize_fp8 (no counterpart in the reference; the
  * reference has no device memory management of its own). Same inputs,
  * outputs and results, but no amax_scratch argument: the scratch is a fixed

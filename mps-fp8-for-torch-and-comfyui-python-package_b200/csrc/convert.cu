@@ -492,6 +492,64 @@ __global__ void quant_scale_kernel(const uint32_t *__restrict__ amax_bits, float
   scale_out[1] = (float)(1.0 / sd);
 }
 
+// ------------------------------------------------------------------ per-row quantize
+// One CTA per row (grid-stride over rows): pass 1 reduces max|x| over the
+// row, pass 2 re-reads the row (from L2: a row is at most a few tens of KiB)
+// and encodes x * scale_r with scale_r = fmax / amax_r computed in double,
+// exactly the reference's per-tensor quantize (fp8_mps_native.py:101-120)
+// applied to each row; inv_scale[r] = 1 / scale_r. Rows whose amax is 0 or
+// NaN use scale 1.
+constexpr int kRowThreads = 256;
+
+template <int SRC, int FMT>
+__global__ void __launch_bounds__(kRowThreads)
+quantize_rows_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *__restrict__ dst, int64_t ld_dst,
+                     int64_t rows, int64_t cols, int vec, float fmax, float *__restrict__ inv_scale) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  __shared__ uint32_t warp_max[kRowThreads / 32];
+  __shared__ float row_scale;
+  const int64_t nchunks = vec ? cols / 16 : 0;  // 16-element chunks read 32 bytes at a time
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint8_t *rs = src + r * ld_src * EB;
+    uint8_t *rd = dst + r * ld_dst;
+    uint32_t m = 0, sg;
+    for (int64_t c = threadIdx.x; c < nchunks; c += kRowThreads) {
+#pragma unroll
+      for (int h = 0; h < EB / 2; h++) {
+        const U8x32 a = ld_u256(rs + c * 16 * EB + 32 * h);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          if constexpr (EB == 4) m = max(m, f2u(widen<SRC>(a.w[j], sg)) & 0x7FFFFFFFu);
+          else {
+            m = max(m, f2u(widen<SRC>(a.w[j] & 0xFFFFu, sg)) & 0x7FFFFFFFu);
+            m = max(m, f2u(widen<SRC>(a.w[j] >> 16, sg)) & 0x7FFFFFFFu);
+          }
+        }
+      }
+    }
+    for (int64_t i = nchunks * 16 + threadIdx.x; i < cols; i += kRowThreads)
+      m = max(m, f2u(load_elem<SRC>(rs, i)) & 0x7FFFFFFFu);
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < kRowThreads / 32; w++) t = max(t, warp_max[w]);
+      const double a = (double)u2f(t);
+      const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+      row_scale = (float)sd;
+      inv_scale[r] = (float)(1.0 / sd);
+    }
+    __syncthreads();
+    const float s = row_scale;
+    for (int64_t c = threadIdx.x; c < nchunks; c += kRowThreads)
+      encode_unit<SRC, FMT>(rs + c * 16 * EB, rd + c * 16, true, s);
+    for (int64_t i = nchunks * 16 + threadIdx.x; i < cols; i += kRowThreads)
+      rd[i] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(rs, i), true, s);
+    __syncthreads();  // warp_max / row_scale are reused by the next row
+  }
+}
+
 // ------------------------------------------------------------------ launch helpers
 // Resident CTAs per SM for `kernel` (queried once per kernel and device),
 // after raising its dynamic shared-memory limit when it needs more than 48 KiB.
@@ -707,4 +765,37 @@ extern "C" int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, i
     return check_launch("fp4 quantize encode");
   }
   return FP8B200_OK;
+}
+
+extern "C" int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                                         void *dst, int64_t ld_dst, int fp8_dtype, float *inv_scale, void *stream) {
+  if (rows < 0 || cols < 0) return set_error(FP8B200_EINVAL, "quantize_rows: negative size");
+  if (!is_float_dtype(src_dtype)) return set_error(FP8B200_EINVAL, "quantize_rows: source dtype %d is not f32/bf16/f16", src_dtype);
+  if (!is_fp8_dtype(fp8_dtype)) return set_error(FP8B200_EINVAL, "quantize_rows: target dtype %d is not e4m3fn/e5m2", fp8_dtype);
+  if (ld_src < cols || ld_dst < cols) return set_error(FP8B200_EINVAL, "quantize_rows: row stride smaller than the row");
+  if (rows == 0) return FP8B200_OK;
+  if (!src || !dst || !inv_scale) return set_error(FP8B200_EINVAL, "quantize_rows: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  const int eb = src_dtype == FP8B200_F32 ? 4 : 2;
+  // 32-byte loads need every row start 32-byte aligned, 16-byte stores every output row 16-byte aligned
+  const int vec = aligned32(src) && (ld_src * eb) % 32 == 0 && aligned16(dst) && ld_dst % 16 == 0;
+  const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
+  const int g = (int)std::min<int64_t>(rows, (int64_t)current_sm_count() * 8);
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint8_t *s = (const uint8_t *)src;
+  uint8_t *d = (uint8_t *)dst;
+#define QR(SRC, FMT) quantize_rows_kernel<SRC, FMT><<<g, kRowThreads, 0, st>>>(s, ld_src, d, ld_dst, rows, cols, vec, fmax, inv_scale)
+  if (fp8_dtype == FP8B200_E4M3) {
+    if (src_dtype == FP8B200_F32) QR(FP8B200_F32, FP8B200_E4M3);
+    else if (src_dtype == FP8B200_BF16) QR(FP8B200_BF16, FP8B200_E4M3);
+    else QR(FP8B200_F16, FP8B200_E4M3);
+  } else {
+    if (src_dtype == FP8B200_F32) QR(FP8B200_F32, FP8B200_E5M2);
+    else if (src_dtype == FP8B200_BF16) QR(FP8B200_BF16, FP8B200_E5M2);
+    else QR(FP8B200_F16, FP8B200_E5M2);
+  }
+#undef QR
+  count_launch();
+  return check_launch("quantize_rows");
 }

@@ -148,6 +148,28 @@ def quantize_fp8(input, fp8_dtype: torch.dtype = torch.float8_e4m3fn):
     return out, scales
 
 
+def quantize_rows_fp8(x: torch.Tensor, fp8_dtype: torch.dtype = torch.float8_e4m3fn):
+    """Per-row (per-token) dynamic quantisation over the last dimension, one
+    fused launch, no host sync: each row r is encoded as x * (fmax / amax_r),
+    the reference's per-tensor quantize (fp8_mps_native.py:101-120) applied
+    row by row. Returns (codes as a `fp8_dtype` tensor of x's shape,
+    inv_scale float32 of shape (..., 1) = amax_r / fmax), ready to be
+    torch._scaled_mm's rowwise scale_a."""
+    if fp8_dtype not in _FP8:
+        raise RuntimeError(f"quantize_rows_fp8: {fp8_dtype} is not an fp8 dtype")
+    src = _as_float_src(x)
+    shape = tuple(src.shape)
+    cols = shape[-1] if shape else 1
+    rows = src.numel() // max(cols, 1) if cols else 0
+    out = torch.empty(shape, dtype=torch.uint8, device=src.device)
+    inv = torch.empty(shape[:-1] + (1,) if shape else (1,), dtype=torch.float32, device=src.device)
+    with torch.cuda.device(src.device):
+        L.check(L.lib().fp8b200_quantize_rows_fp8(src.data_ptr(), L.dtype_code(src.dtype), rows, cols, cols,
+                                                  out.data_ptr(), cols, L.dtype_code(fp8_dtype), inv.data_ptr(),
+                                                  L.stream_of(src)), "quantize_rows")
+    return out.view(fp8_dtype), inv
+
+
 def fp8_quantize(input):
     """amax-scaled e4m3 encode; returns (codes, inv_scale f32[1])
     (fp8_mps_native.py:101-120), with the scale computed on the device."""

@@ -272,3 +272,39 @@ def test_fp4_quantize_matches_reference_formula(nat):
     scale = 6.0 / amax
     assert np.array_equal(enc.cpu().numpy(), O.fp4_encode_ref(x.numpy(), scale))
     assert inv.item() == np.float32(1.0 / scale) and enc.shape == (2049,)
+
+
+# ---------------------------------------------------------------- per-row quantize
+@pytest.mark.parametrize("rows,cols", [(1, 16), (3, 17), (64, 4096), (37, 14336), (5, 1000), (2, 70000)])
+@pytest.mark.parametrize("sdt", [0, 1, 2])
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_quantize_rows(nat, rows, cols, sdt, fmt):
+    g = torch.Generator().manual_seed(rows * cols + sdt)
+    x = (torch.randn(rows, cols, generator=g) * torch.rand(rows, 1, generator=g) * 50).to(OUT[sdt])
+    if rows > 2:
+        x[1] = 0                                  # all-zero row -> scale 1
+        x[2, cols // 2] = float("nan")            # NaN row -> scale 1, NaN code
+    codes, inv = nat.quantize_rows_fp8(x.cuda(), FP8[fmt])
+    assert codes.dtype == FP8[fmt] and codes.shape == (rows, cols) and inv.shape == (rows, 1)
+    fmax = 448.0 if fmt == 0 else 57344.0
+    xf = x.float().numpy()
+    got = codes.view(torch.uint8).cpu().numpy()
+    gi = inv.cpu().numpy().reshape(-1)
+    for r in range(rows):
+        amax = np.float64(np.max(np.abs(xf[r])))
+        sd = fmax / amax if amax > 0 else 1.0
+        assert gi[r] == np.float32(1.0 / sd), r
+        assert np.array_equal(got[r], O.encode_fp8_scaled(xf[r], np.float32(sd), fmt)), r
+
+
+def test_quantize_rows_feeds_rowwise_scaled_mm(nat):
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(256, 512, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(384, 512, generator=g) * 0.02).cuda()
+    wq, ws = nat.quantize_fp8(w)
+    xq, xs = nat.quantize_rows_fp8(x)
+    y = torch._scaled_mm(xq, wq.view(torch.float8_e4m3fn).t(), xs, ws[1:2].expand(1, 384).contiguous(),
+                         out_dtype=torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    rel = (y.float() - ref).norm() / ref.norm()
+    assert rel < 0.05
