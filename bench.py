@@ -413,14 +413,118 @@ class ScaledMM:
             f"{rows}x{self.N}x{self.K} f32 dequantised matmul (CPU torch, {threads} threads)"
 
 
-WORKLOADS = {"fp4_decode": Fp4Decode, "fp8_roundtrip": Fp8RoundTrip,
+class LlamaFp8:
+    """32 Llama-3-8B-shaped layers, e4m3 weights, per-token e4m3 activations,
+    every linear through torch._scaled_mm; batch 8 x 2048 tokens split across
+    the ranks (strong scaling). Metric: tokens/s."""
+    name = "llama_fp8"
+    metric = "llama_fp8_tokens_per_s"
+    unit, bound, kernels_per_step = "tokens/s", "tensor", 1
+    profile = "scaled_mm_llama_fp8"
+    dtype = "e4m3 linears (f32 acc), bf16 attention/norms"
+    scaling = "strong"
+
+    def __init__(self, rank, args):
+        from fp4_fp8_for_torch_mps.workloads import LLAMA, Fp8LlamaStack, llama_input
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        total_batch, self.seq = 8, 2048
+        if total_batch % ws:
+            raise SystemExit(f"llama_fp8: batch {total_batch} does not split over {ws} ranks")
+        self.batch = total_batch // ws
+        self.layers = args.layers or LLAMA["layers"]
+        self.model = Fp8LlamaStack(torch.device("cuda"), layers=self.layers, seed=0)
+        x = llama_input(total_batch, self.seq, seed=0)
+        t = self.batch * self.seq
+        self.x_host = x[rank * t:(rank + 1) * t].contiguous()
+        self.x = self.x_host.cuda()
+        self.work = float(t)                       # tokens per step on this rank
+        self.h2d = self.d2h = self.x_host.numel() * 2
+        self.config = {"workload": "llama_fp8", "layers": self.layers, "hidden": 4096, "intermediate": 14336,
+                       "heads": 32, "kv_heads": 8, "global_batch": total_batch, "seq_len": self.seq,
+                       "tokens_per_rank": t, "l2": "activations and weights per step >> L2"}
+        self.stream = torch.cuda.current_stream()
+        self.h_in = self.x_host.pin_memory()
+        self.h_out = torch.empty_like(self.x_host).pin_memory()
+        self.gemm_flops = self.model.gemm_flops(t)
+
+    def step(self):
+        self.y = self.model.forward(self.x, self.batch, self.seq)
+
+    def e2e_step(self):
+        x = self.h_in.to("cuda", non_blocking=True)
+        y = self.model.forward(x, self.batch, self.seq)
+        self.h_out.copy_(y, non_blocking=True)
+
+    def gemm_roofline(self):
+        """Average achieved TFLOP/s of the _scaled_mm launches in one
+        instrumented step (CUDA events on the launching stream)."""
+        ev = []
+        for l in self.model.layers:
+            l.gemm_events = ev
+        torch.cuda.synchronize()
+        self.step()
+        torch.cuda.synchronize()
+        for l in self.model.layers:
+            l.gemm_events = None
+        ms = sum(a.elapsed_time(b) for a, b, _ in ev)
+        flops = sum(f for _, _, f in ev)
+        return flops / (ms * 1e-3) / 1e12, ms, len(ev)
+
+    def check(self):
+        y = self.h_out.float()
+        return bool(torch.isfinite(y).all().item()) and y.std().item() > 0
+
+    def cpu_run(self, reps=1):
+        return llama_cpu_tokens_per_s(self.layers, reps)
+
+
+def llama_cpu_tokens_per_s(layers: int, reps: int = 1, seq: int = 256):
+    """One Llama-shaped layer on the host in float32 with e4m3-dequantised
+    random weights over one `seq`-token sequence; tokens/s extrapolated to
+    `layers` layers."""
+    import torch.nn.functional as F
+    from fp4_fp8_for_torch_mps.workloads import LLAMA, _rope, quantize_per_tensor, rope_tables
+    c = LLAMA
+    h, f, hd, nkv = c["hidden"], c["intermediate"], c["head_dim"], c["kv_heads"]
+    g = torch.Generator().manual_seed(0)
+
+    def w(n, k):
+        q, sc = quantize_per_tensor(torch.randn(n, k, generator=g) * 0.02)
+        return q.float() * sc
+
+    wqkv, wo, wgu, wd = w(h + 2 * nkv * hd, h), w(h, h), w(2 * f, h), w(h, f)
+    x = torch.randn(seq, h, generator=g)
+    cos, sin = (t.float() for t in rope_tables(seq, "cpu"))
+    threads = torch.get_num_threads()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        r = F.rms_norm(x, (h,), None, c["eps"])
+        q, k, v = (r @ wqkv.t()).split([h, nkv * hd, nkv * hd], dim=1)
+        q = _rope(q.view(1, seq, 32, hd), cos, sin).transpose(1, 2)
+        k = _rope(k.view(1, seq, nkv, hd), cos, sin).transpose(1, 2)
+        v = v.view(1, seq, nkv, hd).transpose(1, 2)
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        y = x + a.transpose(1, 2).reshape(seq, h) @ wo.t()
+        gg, u = (F.rms_norm(y, (h,), None, c["eps"]) @ wgu.t()).chunk(2, dim=1)
+        y = y + (F.silu(gg) * u) @ wd.t()
+    dt = (time.perf_counter() - t0) / reps
+    return seq / (dt * layers), threads, \
+        f"one layer, 1x{seq} tokens, float32 e4m3-dequantised weights (CPU torch, {threads} threads), x{layers} layers"
+
+
+WORKLOADS = {"fp4_decode": Fp4Decode, "fp8_roundtrip": Fp8RoundTrip, "llama_fp8": LlamaFp8,
              "scaled_mm": lambda r, a: ScaledMM(r, a, False),
              "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True)}
 
 
 # ---------------------------------------------------------------- reference arm
 def reference_line(args):
-    if args.workload == "fp4_decode":
+    if args.workload == "llama_fp8":
+        layers = args.layers or 32
+        vals = [llama_cpu_tokens_per_s(layers) for _ in range(max(min(args.steps, 3), 1))]
+        unit, metric = "tokens/s", "llama_fp8_tokens_per_s"
+        config = {"workload": "llama_fp8", "layers": layers, "global_batch": 8, "seq_len": 2048}
+    elif args.workload == "fp4_decode":
         vals = [Fp4Decode.cpu_run(rows=16384, reps=1) for _ in range(max(args.steps, 1))]
         unit, metric = "GB/s", "fp4_decode_GBps"
         config = {"workload": "fp4_decode", "shape": [16384, 8192], "out": "bf16", "scale": 0.37}
@@ -457,6 +561,7 @@ def main():
     ap.add_argument("--workload", default="fp4_decode", choices=sorted(WORKLOADS))
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--shape", type=int, default=0, choices=[0, 1, 2])
+    ap.add_argument("--layers", type=int, default=0, help="llama_fp8: number of layers (default 32)")
     args = ap.parse_args()
     rank, local, ws = rank_info()
 
@@ -502,10 +607,15 @@ def main():
 
     pk, pk_kind = peaks()
     per_step_s = ms / args.steps * 1e-3
-    scale = 1e9 if w.unit == "GB/s" else 1e12
+    scale = {"GB/s": 1e9, "TFLOP/s": 1e12}.get(w.unit, 1.0)
     value = w.work * ws / per_step_s / scale
     e2e_value = w.work * ws / (e2e_ms / e2e_steps * 1e-3) / scale
     achieved = w.work / per_step_s / scale  # per GPU, per launch-averaged step
+    extra = {}
+    if hasattr(w, "gemm_roofline"):
+        achieved, gemm_ms, n_gemm = w.gemm_roofline()
+        extra = {"gemm_ms_per_step": round(gemm_ms, 3), "gemm_launches_per_step": n_gemm,
+                 "gemm_share": round(gemm_ms / (ms / args.steps), 4)}
     if w.bound == "hbm":
         peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
     else:
@@ -523,14 +633,15 @@ def main():
         return 0
     line = {
         "metric": w.metric, "value": round(value, 3), "unit": w.unit, "n_gpus": ws, "steps": args.steps,
-        "warmup": warm, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": warm, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+        "scaling": getattr(w, "scaling", "weak"),
         "config": dict(w.config, parallelism=f"replicas{ws}" if ws > 1 else "single"),
         "e2e": {"value": round(e2e_value, 3), "unit": w.unit, "h2d_bytes_per_step": int(w.h2d),
                 "d2h_bytes_per_step": int(w.d2h)},
         "roofline": {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
                      "frac": round(achieved / peak, 4), "peak_source": psrc,
-                     "traffic": profile_traffic(w.profile)},
+                     "traffic": profile_traffic(w.profile), **extra},
         "cpu_baseline": cpu,
         "gpu_launches": int(launches),
         "clocks": clocks,

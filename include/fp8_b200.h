@@ -195,6 +195,14 @@ int fp8b200_gemm_status(uint32_t *status_out, int reset);
  */
 int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
 
+/*
+ * Kernel choice for fp8b200_scaled_mm: 0 = by shape (the CTA-pair kernel with
+ * 256x256 tiles when M >= 256 and N >= 256, else the single-CTA kernel with
+ * 128x256 tiles), 1 = always single-CTA, 2 = always CTA-pair. Process-wide;
+ * for tests and tuning.
+ */
+int fp8b200_gemm_set_path(int path);
+
 /* Number of kernels this library launched since load (all devices). */
 uint64_t fp8b200_launch_count(void);
 

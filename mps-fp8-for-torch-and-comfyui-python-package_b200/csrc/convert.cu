@@ -176,19 +176,28 @@ struct DecodeUnit {
   static constexpr int kInBytes = 32 / (OUT_BYTES * kOutPerByte);
 };
 
+template <int IB>
+struct UnitIn { uint32_t x[IB / 4]; };
+
+template <int IB>
+__device__ __forceinline__ UnitIn<IB> load_unit(const uint8_t *in) {
+  UnitIn<IB> u;
+  if constexpr (IB == 16) { const uint4 v = ld_u128(in); u.x[0] = v.x; u.x[1] = v.y; u.x[2] = v.z; u.x[3] = v.w; }
+  else if constexpr (IB == 8) { const uint2 v = ld_u64(in); u.x[0] = v.x; u.x[1] = v.y; }
+  else { u.x[0] = ld_u32(in); }
+  return u;
+}
+
 template <bool FP4, int OUT_BYTES>
-__device__ __forceinline__ void decode_unit(const uint8_t *in, uint8_t *out,
+__device__ __forceinline__ void decode_unit(const UnitIn<DecodeUnit<FP4, OUT_BYTES>::kInBytes> &in, uint8_t *out,
                                             const typename Lut<FP4, OUT_BYTES>::T *tab) {
   constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
-  uint32_t x[4];
-  if constexpr (IB == 16) { uint4 v = ld_u128(in); x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w; }
-  else if constexpr (IB == 8) { uint2 v = ld_u64(in); x[0] = v.x; x[1] = v.y; }
-  else { x[0] = ld_u32(in); }
   uint32_t w[8];
   // tab[c << 5] is this lane's copy of entry c
 #pragma unroll
   for (int q = 0; q < IB / 4; q++) {
-    const uint32_t c0 = x[q] & 0xFFu, c1 = (x[q] >> 8) & 0xFFu, c2 = (x[q] >> 16) & 0xFFu, c3 = x[q] >> 24;
+    const uint32_t x = in.x[q];
+    const uint32_t c0 = x & 0xFFu, c1 = (x >> 8) & 0xFFu, c2 = (x >> 16) & 0xFFu, c3 = x >> 24;
     if constexpr (!FP4 && OUT_BYTES == 2) {        // 4 codes -> 4 halves -> 2 words
       w[2 * q] = tab[c0 << 5] | (tab[c1 << 5] << 16);
       w[2 * q + 1] = tab[c2 << 5] | (tab[c3 << 5] << 16);
@@ -224,13 +233,14 @@ decode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (; u + (kUnroll - 1) * nthreads < nunits; u += kUnroll * nthreads) {
+    // all loads of the step first: several independent loads in flight per thread
+    UnitIn<IB> in[kUnroll];
 #pragma unroll
-    for (int j = 0; j < kUnroll; j++) {
-      const int64_t v = u + j * nthreads;
-      decode_unit<FP4, OUT_BYTES>(src + v * IB, dst + v * 32, tab);
-    }
+    for (int j = 0; j < kUnroll; j++) in[j] = load_unit<IB>(src + (u + j * nthreads) * IB);
+#pragma unroll
+    for (int j = 0; j < kUnroll; j++) decode_unit<FP4, OUT_BYTES>(in[j], dst + (u + j * nthreads) * 32, tab);
   }
-  for (; u < nunits; u += nthreads) decode_unit<FP4, OUT_BYTES>(src + u * IB, dst + u * 32, tab);
+  for (; u < nunits; u += nthreads) decode_unit<FP4, OUT_BYTES>(load_unit<IB>(src + u * IB), dst + u * 32, tab);
 
   if (blockIdx.x == 0) {
     for (int64_t i = nunits * IB + threadIdx.x; i < nbytes; i += blockDim.x) {
@@ -330,18 +340,27 @@ __device__ __forceinline__ uint32_t load_raw(const void *src, int64_t i) {
 }
 
 // One unit = 16 elements (64 or 32 input bytes) -> 16 output bytes.
+template <int SRC>
+struct EncIn { U8x32 a[SRC == FP8B200_F32 ? 2 : 1]; };
+
+template <int SRC>
+__device__ __forceinline__ EncIn<SRC> load_enc(const uint8_t *in) {
+  EncIn<SRC> e;
+  e.a[0] = ld_u256(in);
+  if constexpr (SRC == FP8B200_F32) e.a[1] = ld_u256(in + 32);
+  return e;
+}
+
 template <int SRC, int FMT>
-__device__ __forceinline__ void encode_unit(const uint8_t *in, uint8_t *out, bool scaled, float s) {
+__device__ __forceinline__ void encode_unit(const EncIn<SRC> &e, uint8_t *out, bool scaled, float s) {
   constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
   uint32_t raw[16];
   if constexpr (EB == 4) {
-    const U8x32 a = ld_u256(in), b = ld_u256(in + 32);
 #pragma unroll
-    for (int j = 0; j < 8; j++) { raw[j] = a.w[j]; raw[8 + j] = b.w[j]; }
+    for (int j = 0; j < 8; j++) { raw[j] = e.a[0].w[j]; raw[8 + j] = e.a[1].w[j]; }
   } else {
-    const U8x32 a = ld_u256(in);
 #pragma unroll
-    for (int j = 0; j < 8; j++) { raw[2 * j] = a.w[j] & 0xFFFFu; raw[2 * j + 1] = a.w[j] >> 16; }
+    for (int j = 0; j < 8; j++) { raw[2 * j] = e.a[0].w[j] & 0xFFFFu; raw[2 * j + 1] = e.a[0].w[j] >> 16; }
   }
   float x[16];
   uint32_t amax = 0;
@@ -377,14 +396,15 @@ encode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_
   const float s = scaled ? __ldg(scale) : 1.0f;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (; u + (kUnroll - 1) * nthreads < nunits; u += kUnroll * nthreads) {
+  constexpr int U = SRC == FP8B200_F32 ? 2 : kUnroll;  // 32 or 64 KiB of loads in flight per CTA step
+  for (; u + (U - 1) * nthreads < nunits; u += U * nthreads) {
+    EncIn<SRC> in[U];
 #pragma unroll
-    for (int j = 0; j < kUnroll; j++) {
-      const int64_t v = u + j * nthreads;
-      encode_unit<SRC, FMT>(src + v * 16 * EB, dst + v * 16, scaled, s);
-    }
+    for (int j = 0; j < U; j++) in[j] = load_enc<SRC>(src + (u + j * nthreads) * 16 * EB);
+#pragma unroll
+    for (int j = 0; j < U; j++) encode_unit<SRC, FMT>(in[j], dst + (u + j * nthreads) * 16, scaled, s);
   }
-  for (; u < nunits; u += nthreads) encode_unit<SRC, FMT>(src + u * 16 * EB, dst + u * 16, scaled, s);
+  for (; u < nunits; u += nthreads) encode_unit<SRC, FMT>(load_enc<SRC>(src + u * 16 * EB), dst + u * 16, scaled, s);
   for (int64_t i = nunits * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nthreads)
     dst[i] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(src, i), scaled, s);
 }
@@ -543,7 +563,7 @@ quantize_rows_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *_
     __syncthreads();
     const float s = row_scale;
     for (int64_t c = threadIdx.x; c < nchunks; c += kRowThreads)
-      encode_unit<SRC, FMT>(rs + c * 16 * EB, rd + c * 16, true, s);
+      encode_unit<SRC, FMT>(load_enc<SRC>(rs + c * 16 * EB), rd + c * 16, true, s);
     for (int64_t i = nchunks * 16 + threadIdx.x; i < cols; i += kRowThreads)
       rd[i] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(rs, i), true, s);
     __syncthreads();  // warp_max / row_scale are reused by the next row

@@ -47,7 +47,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;    // two 256-column fp32 accumulators
 constexpr int GROUP_M = 16;       // tile raster: 16 M-tiles per group for L2 reuse
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2 * BN * 4 /*column tables*/ + 256 /*barriers*/;
 
 struct Params {
   int M, N, K, num_kb, tiles_m, tiles_n, num_tiles;
@@ -205,19 +205,15 @@ __device__ __forceinline__ float load_bias(const void *bias, int dt, int col) {
   return __half2float(reinterpret_cast<const __half *>(bias)[col]);
 }
 
-// Scale, bias and store 32 consecutive columns of one output row.
+// Scale, bias and store 32 consecutive columns of one output row. col_scale /
+// col_bias point at this chunk's 32 entries of the tile's column tables in
+// shared memory (every lane reads the same address: broadcast).
 __device__ __forceinline__ void store_row_chunk(const Params &p, int row, int col0, const uint32_t (&acc)[32],
-                                                float row_scale, float tensor_scale_b, float sr) {
+                                                float row_scale, const float *col_scale, const float *col_bias,
+                                                float sr) {
   float v[32];
 #pragma unroll
-  for (int j = 0; j < 32; j++) {
-    const int col = col0 + j;
-    float sbv = tensor_scale_b;
-    if (p.sb_rowwise) sbv = (col < p.N) ? __ldg(p.sb + col) : 0.0f;
-    float x = __uint_as_float(acc[j]) * (row_scale * sbv);
-    if (p.bias != nullptr && col < p.N) x += load_bias(p.bias, p.bias_dtype, col);
-    v[j] = x * sr;
-  }
+  for (int j = 0; j < 32; j++) v[j] = (__uint_as_float(acc[j]) * (row_scale * col_scale[j]) + col_bias[j]) * sr;
   const bool full = p.vec_store && (col0 + 32 <= p.N);
   char *base = reinterpret_cast<char *>(p.D);
   switch (p.out_dtype) {
@@ -277,7 +273,40 @@ __device__ __forceinline__ void store_row_chunk(const Params &p, int row, int co
   }
 }
 
-// ------------------------------------------------------------------ the kernel
+// Named barrier among the four epilogue warps (128 threads).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// The tile's per-column factors (tensorwise or rowwise scale_b; bias or 0),
+// loaded once per tile by the 128 epilogue threads into shared memory.
+__device__ __forceinline__ void stage_columns(const Params &p, int n0, float sb_t, float *s_scale, float *s_bias,
+                                              int etid) {
+  for (int j = etid; j < BN; j += 128) {
+    const int col = n0 + j;
+    const bool in = col < p.N;
+    s_scale[j] = in ? (p.sb_rowwise ? __ldg(p.sb + col) : sb_t) : 0.0f;
+    s_bias[j] = (in && p.bias != nullptr) ? load_bias(p.bias, p.bias_dtype, col) : 0.0f;
+  }
+}
+
+// Drain one 128-row x 256-column accumulator: each epilogue warp reads its
+// 32-lane quarter of TMEM (rows) in 32-column chunks.
+__device__ __forceinline__ void drain_accumulator(const Params &p, uint32_t t_acc, int row0, int n0, int quarter,
+                                                  int lane, float rs_t, const float *s_scale, const float *s_bias,
+                                                  float sr) {
+  const int row = row0 + quarter * 32 + lane;
+  const float rs = p.sa_rowwise ? ((row < p.M) ? __ldg(p.sa + row) : 0.0f) : rs_t;
+  const uint32_t t_row = t_acc + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; c++) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+    tmem_ld_wait();
+    const int col0 = n0 + c * 32;
+    if (row < p.M && col0 < p.N) store_row_chunk(p, row, col0, r, rs, s_scale + c * 32, s_bias + c * 32, sr);
+  }
+}
+
+// ------------------------------------------------------------------ single-CTA kernel
 __global__ void __launch_bounds__(THREADS, 1)
 scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const Params p) {
@@ -288,7 +317,9 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   uint8_t *smem = smem_raw + (base - raw_addr);
   const uint32_t sA = base;                     // STAGES x 16 KiB
   const uint32_t sB = base + STAGES * A_BYTES;  // STAGES x 32 KiB
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  float *s_scale = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES);
+  float *s_bias = s_scale + BN;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s_bias + BN);
   // barriers: full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], then the TMEM address slot
   const uint32_t bar_base = smem_u32(bars);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
@@ -377,6 +408,7 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   } else {
     // ---------------- epilogue: warps 2..5, TMEM lane quarter = warp % 4
     const int quarter = warp & 3;
+    const int etid = threadIdx.x - 64;
     int acc = 0;
     uint32_t acc_phase = 0;
     const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
@@ -385,23 +417,17 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int tm, tn;
       tile_coords(p, tile, tm, tn);
+      epilogue_sync();  // the previous tile's column tables are no longer read
+      stage_columns(p, tn * BN, sb_t, s_scale, s_bias, etid);
+      epilogue_sync();
       // warp-uniform bounded wait
       int ok = 0;
       if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int row = tm * BM + quarter * 32 + lane;
-      const float rs = p.sa_rowwise ? ((row < p.M) ? __ldg(p.sa + row) : 0.0f) : sa_t;
-      const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quarter * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
-        const int col0 = tn * BN + c * 32;
-        if (row < p.M && col0 < p.N) store_row_chunk(p, row, col0, r, rs, sb_t, sr);
-      }
+      drain_accumulator(p, tmem_base + (uint32_t)(acc * BN), tm * BM, tn * BN, quarter, lane, sa_t, s_scale,
+                        s_bias, sr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -414,6 +440,216 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ CTA-pair kernel
+// A cluster of two CTAs computes a 256x256 output tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=32). Each CTA loads its own 128
+// rows of A and its own 128-row half of B into its shared memory (same
+// offsets in both CTAs); the MMA reads A rows and B halves from both. The
+// loads of both CTAs complete on the leader's (rank 0) full barrier; the
+// leader's single MMA thread commits to the empty and tmem_full barriers of
+// both CTAs; each CTA's epilogue drains its own 128 accumulator rows and
+// arrives on the leader's tmem_empty barrier.
+constexpr int PAIR_BN = 256;              // output columns per pair tile
+constexpr int HALF_B = PAIR_BN / 2;       // B rows loaded per CTA
+constexpr int STAGES2 = 6;
+constexpr int A2_BYTES = BM * BK;         // 16 KiB
+constexpr int B2_BYTES = HALF_B * BK;     // 16 KiB
+constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 /*align*/ + 2 * BN * 4 /*column tables*/ + 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t leader_bar, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(dst),
+      "l"(map), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f8f6f4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on the barrier at this shared offset in both CTAs of the pair when
+// the issuing thread's MMAs complete
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\t"
+      "mov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const uint32_t sA = base;                       // STAGES2 x 16 KiB
+  const uint32_t sB = base + STAGES2 * A2_BYTES;  // STAGES2 x 16 KiB
+  float *s_scale = reinterpret_cast<float *>(smem + STAGES2 * STAGE2_BYTES);
+  float *s_bias = s_scale + BN;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s_bias + BN);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES2 + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES2 + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES2 + 2 + b); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES2 + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = (int)cluster_id_x();
+  const int npairs = (int)num_clusters_x();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; s++) {
+      mbar_init(full_bar(s), 1);   // used in the leader only
+      mbar_init(empty_bar(s), 1);  // one multicast commit per use
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 8);  // four epilogue warps in each CTA (leader's barrier)
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {  // same warp in both CTAs, same destination offset
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        const int arow = tm * (2 * BM) + (int)rank * BM;
+        const int brow = tn * PAIR_BN + (int)rank * HALF_B;
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (p.debug_skip_first_load) { ok = false; break; }
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * STAGE2_BYTES);
+          tma_load_2d_pair(sA + stage * A2_BYTES, &tmap_a, leader_full, kb * BK, arow);
+          tma_load_2d_pair(sB + stage * B2_BYTES, &tmap_b, leader_full, kb * BK, brow);
+          if (++stage == STAGES2) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only)
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * PAIR_BN);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128_kmajor(sA + stage * A2_BYTES);
+          const uint64_t bdesc = sdesc_sw128_kmajor(sB + stage * B2_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; k++)
+            umma_f8f6f4_pair(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
+                             p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(empty_bar(stage));
+          if (++stage == STAGES2) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of the pair tile
+    const int quarter = warp & 3;
+    const int etid = threadIdx.x - 64;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
+    const float sb_t = p.sb_rowwise ? 0.0f : __ldg(p.sb);
+    const float sr = p.scale_result ? __ldg(p.scale_result) : 1.0f;
+    for (int tile = pair; tile < p.num_tiles; tile += npairs) {
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      epilogue_sync();
+      stage_columns(p, tn * PAIR_BN, sb_t, s_scale, s_bias, etid);
+      epilogue_sync();
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      drain_accumulator(p, tmem_base + (uint32_t)(acc * PAIR_BN), tm * (2 * BM) + (int)rank * BM, tn * PAIR_BN,
+                        quarter, lane, sa_t, s_scale, s_bias, sr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still touch its shared memory
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -451,6 +687,24 @@ int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, in
 
 unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
 int g_debug_skip_first_load = 0;
+int g_path = 0;  // 0 = choose by shape, 1 = single-CTA kernel, 2 = CTA-pair kernel
+
+// Resident 2-CTA clusters of the pair kernel on the current device.
+int pair_clusters(int dev) {
+  static int cached[64] = {};
+  if (dev < 0 || dev >= 64) return 1;
+  if (!cached[dev]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, scaled_mm_pair_kernel, &cfg) != cudaSuccess || n < 1)
+      n = current_sm_count() / 2;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
 
 }  // namespace gemm
 }  // namespace fp8b200
@@ -485,14 +739,15 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   int dev;
   if (int rc = check_device(&dev)) return rc;
 
+  const bool pair = g_path == 2 || (g_path == 0 && M >= 2 * BM && N >= PAIR_BN);
   CUtensorMap ma, mb;
   if (int rc = make_kmajor_map(&ma, A, M, K, lda, BM)) return rc;
-  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, BN)) return rc;
+  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, pair ? HALF_B : BN)) return rc;
 
   Params p;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.num_kb = (int)((K + BK - 1) / BK);
-  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   p.tiles_n = (int)((N + BN - 1) / BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.sa = scale_a; p.sb = scale_b;
@@ -505,18 +760,26 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.vec_store = aligned16(D) && ((ldd * esz) % 16 == 0);
   const uint32_t afmt = a_dtype == FP8B200_E5M2 ? 1u : 0u, bfmt = b_dtype == FP8B200_E5M2 ? 1u : 0u;
   // instruction descriptor: f32 accumulate, A/B formats, both K-major, N>>3, M>>4
-  p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  const uint32_t mma_m = pair ? 2 * BM : BM;
+  p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((mma_m >> 4) << 24);
   p.timeout_ns = g_timeout_ns;
   p.debug_skip_first_load = g_debug_skip_first_load;
 
   static bool attr_done[64] = {};
   if (dev < 64 && !attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(scaled_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(scaled_mm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
   }
-  const int grid = std::min(p.num_tiles, current_sm_count());
-  scaled_mm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
+  if (pair) {
+    const int clusters = std::min(p.num_tiles, pair_clusters(dev));
+    scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
+  } else {
+    const int grid = std::min(p.num_tiles, current_sm_count());
+    scaled_mm_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
+  }
   count_launch();
   return check_launch("scaled_mm");
 }
@@ -537,5 +800,11 @@ extern "C" int fp8b200_gemm_status(uint32_t *status_out, int reset) {
 extern "C" int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns) {
   g_debug_skip_first_load = skip_first_load ? 1 : 0;
   g_timeout_ns = wait_timeout_ns ? wait_timeout_ns : 2000000000ull;
+  return FP8B200_OK;
+}
+
+extern "C" int fp8b200_gemm_set_path(int path) {
+  if (path < 0 || path > 2) return set_error(FP8B200_EINVAL, "gemm path must be 0 (auto), 1 or 2");
+  g_path = path;
   return FP8B200_OK;
 }

@@ -99,3 +99,124 @@ def rowwise_operands(m: int, n: int, k: int, seed: int = 0):
     sw = (w.abs().amax(dim=1, keepdim=True) / 448.0).float()
     wq = (w / sw).to(torch.float8_e4m3fn)
     return aq, wq, sa, sw.reshape(1, n)
+
+
+# ---------------------------------------------------------------------------
+# FP8 weight-only inference stack: Llama-3-8B-shaped layers with random
+# weights. Every linear is torch._scaled_mm on e4m3 weights (per-tensor fp32
+# scale, broadcast per output column) and per-token e4m3 activations; norms,
+# rotary embedding, attention (SDPA) and SiLU stay in bf16 PyTorch.
+
+LLAMA = dict(hidden=4096, intermediate=14336, heads=32, kv_heads=8, head_dim=128, layers=32,
+             rope_theta=500000.0, eps=1e-5)
+
+
+class Fp8LlamaLayer:
+    """One decoder layer. Weights are generated on `device` from a seeded
+    CUDA generator (deterministic) and quantised to e4m3 per tensor."""
+
+    def __init__(self, device, gen: torch.Generator, cfg=LLAMA):
+        from . import fp8_mps_native as nat
+        h, f = cfg["hidden"], cfg["intermediate"]
+        kvd = cfg["kv_heads"] * cfg["head_dim"]
+        self.cfg = cfg
+        self.nat = nat
+
+        def qw(n, k):
+            w = torch.randn(n, k, generator=gen, device=device, dtype=torch.bfloat16) * 0.02
+            q, s = nat.quantize_fp8(w)          # s = [scale, 1/scale]
+            return q.view(torch.float8_e4m3fn), s[1:2].clone()
+
+        wq, sq = qw(h, h)
+        wk, sk = qw(kvd, h)
+        wv, sv = qw(kvd, h)
+        self.w_qkv = torch.cat([wq, wk, wv])    # (h + 2*kvd, h) rows = output features
+        self.s_qkv = torch.cat([sq.expand(h), sk.expand(kvd), sv.expand(kvd)]).reshape(1, -1).contiguous()
+        self.w_o, so = qw(h, h)
+        self.s_o = so.expand(h).reshape(1, -1).contiguous()
+        wg, sg = qw(f, h)
+        wu, su = qw(f, h)
+        self.w_gu = torch.cat([wg, wu])
+        self.s_gu = torch.cat([sg.expand(f), su.expand(f)]).reshape(1, -1).contiguous()
+        self.w_d, sd = qw(h, f)
+        self.s_d = sd.expand(h).reshape(1, -1).contiguous()
+        self.n1 = torch.ones(h, device=device, dtype=torch.bfloat16)
+        self.n2 = torch.ones(h, device=device, dtype=torch.bfloat16)
+
+    gemm_events = None  # set to a list to record (start, end) CUDA events around each GEMM
+
+    def linear(self, x2d, w, sw):
+        xq, xs = self.nat.quantize_rows_fp8(x2d)
+        if self.gemm_events is None:
+            return torch._scaled_mm(xq, w.t(), xs, sw, out_dtype=torch.bfloat16)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        y = torch._scaled_mm(xq, w.t(), xs, sw, out_dtype=torch.bfloat16)
+        e1.record()
+        self.gemm_events.append((e0, e1, 2.0 * xq.shape[0] * xq.shape[1] * w.shape[0]))
+        return y
+
+    def forward(self, x, cos, sin, batch, seq):
+        import torch.nn.functional as F
+        c = self.cfg
+        h, hd, nh, nkv = c["hidden"], c["head_dim"], c["heads"], c["kv_heads"]
+        t = x.shape[0]
+        r = F.rms_norm(x, (h,), self.n1, c["eps"])
+        qkv = self.linear(r, self.w_qkv, self.s_qkv)
+        q, k, v = qkv.split([h, nkv * hd, nkv * hd], dim=1)
+        q = q.view(batch, seq, nh, hd)
+        k = k.view(batch, seq, nkv, hd)
+        v = v.view(batch, seq, nkv, hd)
+        q, k = _rope(q, cos, sin), _rope(k, cos, sin)
+        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           is_causal=True, enable_gqa=True)
+        a = a.transpose(1, 2).reshape(t, h)
+        x = x + self.linear(a, self.w_o, self.s_o)
+        r = F.rms_norm(x, (h,), self.n2, c["eps"])
+        gu = self.linear(r, self.w_gu, self.s_gu)
+        g, u = gu.chunk(2, dim=1)
+        x = x + self.linear(F.silu(g) * u, self.w_d, self.s_d)
+        return x
+
+    def gemm_flops(self, tokens: int) -> float:
+        c = self.cfg
+        h, f, kvd = c["hidden"], c["intermediate"], c["kv_heads"] * c["head_dim"]
+        return 2.0 * tokens * h * (h + 2 * kvd + h + 2 * f) + 2.0 * tokens * f * h
+
+
+def _rope(x, cos, sin):
+    x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+
+def rope_tables(seq: int, device, cfg=LLAMA):
+    hd = cfg["head_dim"]
+    inv = 1.0 / (cfg["rope_theta"] ** (torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd))
+    ang = torch.arange(seq, device=device, dtype=torch.float32)[:, None] * inv[None, :]
+    cos = ang.cos().to(torch.bfloat16)[None, :, None, :]
+    sin = ang.sin().to(torch.bfloat16)[None, :, None, :]
+    return cos, sin
+
+
+class Fp8LlamaStack:
+    """`layers` decoder layers over a batch of `batch` x `seq` tokens."""
+
+    def __init__(self, device, layers: int = LLAMA["layers"], seed: int = 0):
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.layers = [Fp8LlamaLayer(device, gen) for _ in range(layers)]
+        self.device = device
+
+    def forward(self, x, batch, seq):
+        cos, sin = rope_tables(seq, x.device)
+        for layer in self.layers:
+            x = layer.forward(x, cos, sin, batch, seq)
+        return x
+
+    def gemm_flops(self, tokens: int) -> float:
+        return sum(l.gemm_flops(tokens) for l in self.layers)
+
+
+def llama_input(batch: int, seq: int, seed: int = 0) -> torch.Tensor:
+    """Hidden states N(0,1) bf16, (batch*seq, hidden), generated on the CPU."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(batch * seq, LLAMA["hidden"], generator=g).to(torch.bfloat16)

@@ -53,6 +53,15 @@ def nat(device):
     return fp8_mps_native
 
 
+@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"])
+def path(request, nat):
+    """Run the test on the single-CTA kernel and on the CTA-pair kernel."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    L.check(L.lib().fp8b200_gemm_set_path(request.param), "gemm path")
+    yield request.param
+    L.check(L.lib().fp8b200_gemm_set_path(0), "gemm path")
+
+
 def codes(t):
     return t.view(torch.uint8).cpu().numpy()
 
@@ -87,7 +96,7 @@ SHAPES = [(1, 16, 16), (1, 256, 512), (17, 48, 64), (64, 128, 256), (128, 256, 1
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("rowwise", [False, True])
-def test_shapes_bf16(nat, M, N, K, rowwise):
+def test_shapes_bf16(nat, path, M, N, K, rowwise):
     g = torch.Generator().manual_seed(M * 7 + N * 3 + K)
     a = rand_fp8((M, K), E4, g)
     b = rand_fp8((N, K), E4, g)
@@ -105,7 +114,7 @@ def test_shapes_bf16(nat, M, N, K, rowwise):
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("fmts", [(E4, E4), (E4, E5), (E5, E4)])
 @pytest.mark.parametrize("bias_dtype", [None, torch.float32, torch.bfloat16])
-def test_dtypes_and_bias(nat, out_dtype, fmts, bias_dtype):
+def test_dtypes_and_bias(nat, path, out_dtype, fmts, bias_dtype):
     M, N, K = 200, 320, 384
     g = torch.Generator().manual_seed(11)
     a = rand_fp8((M, K), fmts[0], g, 20.0)
@@ -121,7 +130,7 @@ def test_dtypes_and_bias(nat, out_dtype, fmts, bias_dtype):
     check_close(out, ref, S, f"{out_dtype} {fmts} bias={bias_dtype}")
 
 
-def test_fp8_output_and_scale_result(nat):
+def test_fp8_output_and_scale_result(nat, path):
     """out_dtype=None returns self.dtype (fp8), as torch._scaled_mm does."""
     M, N, K = 128, 256, 256
     g = torch.Generator().manual_seed(5)
@@ -138,7 +147,7 @@ def test_fp8_output_and_scale_result(nat):
     assert ok.all(), (dec[~ok][:5], ref[~ok][:5])
 
 
-def test_strided_operands_and_output(nat):
+def test_strided_operands_and_output(nat, path):
     """Row strides larger than K (views into wider buffers) on both operands."""
     M, N, K = 256, 256, 256
     g = torch.Generator().manual_seed(9)
@@ -188,6 +197,7 @@ def test_reference_custom_ops_accuracy(nat):
 # ---------------------------------------------------------------- full-size workloads
 @pytest.mark.parametrize("size", [4096, 8192, 16384])
 def test_per_tensor_workload(nat, size):
+    """Default kernel choice (the CTA-pair kernel at these sizes)."""
     from fp4_fp8_for_torch_mps.workloads import scaled_mm_operands
     aq, bq, sa, sb = scaled_mm_operands(size, size, size)
     out = torch._scaled_mm(aq.cuda(), bq.cuda().t(), sa.cuda(), sb.cuda(), out_dtype=torch.bfloat16)
@@ -208,7 +218,7 @@ def test_rowwise_workload(nat, shape):
 
 
 # ---------------------------------------------------------------- failure detection
-def test_bounded_wait_times_out_and_context_survives(nat):
+def test_bounded_wait_times_out_and_context_survives(nat, path):
     """A wait that nothing will satisfy (the producer is told never to fill the
     first stage) gives up after 50 ms with a status word; the next GEMM on the
     same context is correct."""
@@ -231,3 +241,17 @@ def test_bounded_wait_times_out_and_context_survives(nat):
     assert L.gemm_status() == 0
     ref, S = O.scaled_mm_ref(codes(a), codes(b), 0.01, 0.01)
     check_close(out, ref, S, "after timeout")
+
+
+def test_single_cta_kernel_at_8192(nat):
+    from fp4_fp8_for_torch_mps import _lib as L
+    from fp4_fp8_for_torch_mps.workloads import scaled_mm_operands
+    aq, bq, sa, sb = scaled_mm_operands(8192, 8192, 8192, seed=3)
+    L.check(L.lib().fp8b200_gemm_set_path(1), "gemm path")
+    try:
+        out = torch._scaled_mm(aq.cuda(), bq.cuda().t(), sa.cuda(), sb.cuda(), out_dtype=torch.bfloat16)
+    finally:
+        L.lib().fp8b200_gemm_set_path(0)
+    rows = np.sort(np.random.default_rng(1).choice(8192, 64, replace=False))
+    ref, S = O.scaled_mm_ref(codes(aq), codes(bq), sa.item(), sb.item(), rows=rows)
+    check_close(out[torch.from_numpy(rows).cuda()], ref, S, "8192^3 single-CTA")
