@@ -89,58 +89,79 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons during the timed region:
+    NVML polled every 2 ms from a background thread (the device is matched by
+    PCI bus id), falling back to `nvidia-smi -lms 100`."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
-    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu, self.proc, self.path, self.err = gpu_index, None, None, None
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples, self.reason_bits, self.max_mhz = [], 0, None
+        self.thread, self.stop_flag, self.proc, self.err = None, False, None, None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def start(self):
+        import threading
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.PIPE, text=True)
-            time.sleep(0.3)
-        except OSError as e:
-            self.proc, self.err = None, str(e)
+            nv, h = self._nvml_handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+            def loop():
+                while not self.stop_flag:
+                    try:
+                        self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        self.reason_bits |= nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except Exception:  # noqa: BLE001 - keep sampling
+                        pass
+                    time.sleep(0.002)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+        except Exception as e:  # noqa: BLE001 - fall back to nvidia-smi
+            self.err = f"nvml: {e}"
+            try:
+                fd, self.path = tempfile.mkstemp(suffix=".csv")
+                os.close(fd)
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.sw_power_cap,"
+                     "clocks_event_reasons.hw_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                     "clocks_event_reasons.hw_thermal_slowdown", "--format=csv,noheader,nounits", "-lms", "100"],
+                    stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                time.sleep(0.3)
+            except OSError as e2:
+                self.err += f"; nvidia-smi: {e2}"
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=2)
+            if not self.samples:
+                return {"error": "no NVML samples"}
+            reasons = sorted(v for k, v in self.REASONS.items() if self.reason_bits & k)
+            return {"sm_mhz": statistics.median(self.samples), "sm_min_mhz": min(self.samples),
+                    "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+                    "source": "nvml"}
         if self.proc is None:
-            return {"error": self.err or "nvidia-smi unavailable"}
+            return {"error": self.err or "no sampler"}
         self.proc.terminate()
-        try:
-            _, err = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            err = ""
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 7:
-                    rows.append(parts)
+        self.proc.wait(timeout=5)
+        rows = [[x.strip() for x in line.split(",")] for line in open(self.path) if line.count(",") >= 5]
         os.unlink(self.path)
         if not rows:
-            return {"error": (err or "no samples").strip()[:200]}
-
-        def num(x):
-            try:
-                return float(x)
-            except ValueError:
-                return None
-
-        sm = [num(r[0]) for r in rows if num(r[0]) is not None]
-        mx = [num(r[1]) for r in rows if num(r[1]) is not None]
-        reasons = sorted({self.NAMES[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+            return {"error": "no nvidia-smi samples"}
+        names = ["sw_power_cap", "hw_slowdown", "sw_thermal_slowdown", "hw_thermal_slowdown"]
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][1]),
+                "reasons": sorted({names[i] for r in rows for i in range(4) if r[2 + i].lower() == "active"}),
+                "samples": len(rows), "source": "nvidia-smi"}
 
 
 def timed_region(step, steps: int, stream, dist_on: bool):
