@@ -48,22 +48,6 @@ constexpr int kUnroll = 4;  // units per thread per step
 // ------------------------------------------------------------------ loads/stores
 struct U8x32 { uint32_t w[8]; };
 
-__device__ __forceinline__ uint32_t ld_u32(const void *p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint2 ld_u64(const void *p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint4 ld_u128(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
 __device__ __forceinline__ U8x32 ld_u256(const void *p) {
   U8x32 v;
   asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -74,11 +58,6 @@ __device__ __forceinline__ U8x32 ld_u256(const void *p) {
 }
 __device__ __forceinline__ void st_u128(void *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-__device__ __forceinline__ void st_u256(void *p, const uint32_t (&w)[8]) {
-  asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-               : "memory");
 }
 
 inline bool aligned32(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
@@ -137,120 +116,153 @@ __constant__ float kFp4Values[16] = {
     -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f,
 };
 
-// ------------------------------------------------------------------ lookup tables
-// Entry type: u32 for one fp8 output (any dtype) and for an fp4 pair of
-// 16-bit outputs; u64 (uint2) for an fp4 pair of f32 outputs.
-template <bool FP4, int OUT_BYTES>
-struct Lut {
-  using T = typename std::conditional<FP4 && OUT_BYTES == 4, uint2, uint32_t>::type;
-  static constexpr int kBytes = 256 * 32 * (int)sizeof(T);
-};
-
-// Builds the 32-way replicated table: 256 distinct entries, then copies.
-template <bool FP4, int OUT_BYTES>
-__device__ __forceinline__ void build_lut(typename Lut<FP4, OUT_BYTES>::T *lut, int fmt, int odt, float s, int mode) {
-  using T = typename Lut<FP4, OUT_BYTES>::T;
-  __shared__ T distinct[256];
-  for (int c = threadIdx.x; c < 256; c += blockDim.x) {
-    if constexpr (!FP4) {
-      distinct[c] = apply_scale(fp8_to_f32_bits((uint32_t)c, fmt), odt, s, mode);
-    } else {
-      const uint32_t lo = apply_scale(f2u(kFp4Values[c & 15]), odt, s, mode);
-      const uint32_t hi = apply_scale(f2u(kFp4Values[c >> 4]), odt, s, mode);
-      if constexpr (OUT_BYTES == 4) distinct[c] = make_uint2(lo, hi);
-      else distinct[c] = lo | (hi << 16);
-    }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) lut[i] = distinct[i >> 5];
-  __syncthreads();
-}
-
 // ------------------------------------------------------------------ decoders
-// One unit = the input bytes that give 32 output bytes:
-//   fp8 -> 16-bit: 16 codes;  fp8 -> f32: 8 codes;
-//   fp4 -> 16-bit: 8 bytes;   fp4 -> f32: 4 bytes.
-template <bool FP4, int OUT_BYTES>
-struct DecodeUnit {
-  static constexpr int kOutPerByte = FP4 ? 2 : 1;
-  static constexpr int kInBytes = 32 / (OUT_BYTES * kOutPerByte);
+// Bulk-copy pipeline. A CTA streams chunks of CIN input bytes that decode to
+// exactly 16 KiB of output: one thread issues cp.async.bulk loads of the next
+// chunks into a 3-stage shared-memory ring (mbarrier completion); all threads
+// decode from shared memory through the table into a 3-stage output ring; one
+// thread writes each finished output chunk back with a single
+// cp.async.bulk store. HBM traffic is then only bulk transfers, no LSU global
+// loads or stores, and the bytes in flight do not depend on registers.
+//
+// Tables (replicated per lane so lane L reads bank L, conflict-free):
+//   fp8 -> any:     256 codes -> output bits (u32)            32 KiB
+//   fp4 -> 16-bit:  256 bytes -> (lo, hi) output pair (u32)   32 KiB
+//   fp4 -> f32:     16 nibbles -> output bits (u32)            2 KiB
+// Each thread step reads G input bytes and writes 8 or 16 contiguous output
+// bytes at thread-contiguous offsets (conflict-free shared stores).
+constexpr int kDecThreads = 256;
+constexpr int kStages = 3;
+constexpr int kOutChunk = 16384;
+
+enum DecKind { DEC_FP8_16 = 0, DEC_FP8_32 = 1, DEC_FP4_16 = 2, DEC_FP4_32 = 3 };
+
+template <int KIND>
+struct Dec {
+  static constexpr int kOutPerIn = KIND == DEC_FP8_16 ? 2 : KIND == DEC_FP8_32 ? 4 : KIND == DEC_FP4_16 ? 4 : 8;
+  static constexpr int kIn = kOutChunk / kOutPerIn;            // input bytes per chunk
+  static constexpr int kG = KIND == DEC_FP4_32 ? 2 : 4;         // input bytes per thread step
+  static constexpr int kSteps = kIn / kG / kDecThreads;
+  static constexpr int kLutEntries = KIND == DEC_FP4_32 ? 16 : 256;
+  static constexpr int kLutBytes = kLutEntries * 32 * 4;
+  static constexpr int kSmem = kLutBytes + kStages * (kIn + kOutChunk) + 64;
 };
 
-template <int IB>
-struct UnitIn { uint32_t x[IB / 4]; };
-
-template <int IB>
-__device__ __forceinline__ UnitIn<IB> load_unit(const uint8_t *in) {
-  UnitIn<IB> u;
-  if constexpr (IB == 16) { const uint4 v = ld_u128(in); u.x[0] = v.x; u.x[1] = v.y; u.x[2] = v.z; u.x[3] = v.w; }
-  else if constexpr (IB == 8) { const uint2 v = ld_u64(in); u.x[0] = v.x; u.x[1] = v.y; }
-  else { u.x[0] = ld_u32(in); }
-  return u;
+// output bits for input code c (fp8 code, fp4 byte pair, or fp4 nibble)
+template <int KIND>
+__device__ __forceinline__ uint32_t dec_entry(uint32_t c, int fmt, int odt, float s, int mode) {
+  if constexpr (KIND == DEC_FP8_16 || KIND == DEC_FP8_32) return apply_scale(fp8_to_f32_bits(c, fmt), odt, s, mode);
+  else if constexpr (KIND == DEC_FP4_16)
+    return apply_scale(f2u(kFp4Values[c & 15u]), odt, s, mode) | (apply_scale(f2u(kFp4Values[c >> 4]), odt, s, mode) << 16);
+  else return apply_scale(f2u(kFp4Values[c & 15u]), odt, s, mode);
 }
 
-template <bool FP4, int OUT_BYTES>
-__device__ __forceinline__ void decode_unit(const UnitIn<DecodeUnit<FP4, OUT_BYTES>::kInBytes> &in, uint8_t *out,
-                                            const typename Lut<FP4, OUT_BYTES>::T *tab) {
-  constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
-  uint32_t w[8];
-  // tab[c << 5] is this lane's copy of entry c
-#pragma unroll
-  for (int q = 0; q < IB / 4; q++) {
-    const uint32_t x = in.x[q];
-    const uint32_t c0 = x & 0xFFu, c1 = (x >> 8) & 0xFFu, c2 = (x >> 16) & 0xFFu, c3 = x >> 24;
-    if constexpr (!FP4 && OUT_BYTES == 2) {        // 4 codes -> 4 halves -> 2 words
-      w[2 * q] = tab[c0 << 5] | (tab[c1 << 5] << 16);
-      w[2 * q + 1] = tab[c2 << 5] | (tab[c3 << 5] << 16);
-    } else if constexpr (!FP4) {                    // 4 codes -> 4 words
-      w[4 * q] = tab[c0 << 5]; w[4 * q + 1] = tab[c1 << 5];
-      w[4 * q + 2] = tab[c2 << 5]; w[4 * q + 3] = tab[c3 << 5];
-    } else if constexpr (OUT_BYTES == 2) {          // 4 bytes -> 8 halves -> 4 words
-      w[4 * q] = tab[c0 << 5]; w[4 * q + 1] = tab[c1 << 5];
-      w[4 * q + 2] = tab[c2 << 5]; w[4 * q + 3] = tab[c3 << 5];
-    } else {                                        // 4 bytes -> 8 f32 words
-      const uint2 p0 = tab[c0 << 5], p1 = tab[c1 << 5], p2 = tab[c2 << 5], p3 = tab[c3 << 5];
-      w[0] = p0.x; w[1] = p0.y; w[2] = p1.x; w[3] = p1.y;
-      w[4] = p2.x; w[5] = p2.y; w[6] = p3.x; w[7] = p3.y;
+// decode one thread step: G input bytes -> 8 or 16 output bytes
+template <int KIND>
+__device__ __forceinline__ void dec_step(const uint8_t *in, uint8_t *out, int idx, const uint32_t *tab) {
+#define T(c) tab[(uint32_t)(c) << 5]
+  if constexpr (KIND == DEC_FP8_16) {
+    const uint32_t x = reinterpret_cast<const uint32_t *>(in)[idx];
+    reinterpret_cast<uint2 *>(out)[idx] =
+        make_uint2(T(x & 255u) | (T((x >> 8) & 255u) << 16), T((x >> 16) & 255u) | (T(x >> 24) << 16));
+  } else if constexpr (KIND == DEC_FP8_32 || KIND == DEC_FP4_16) {
+    const uint32_t x = reinterpret_cast<const uint32_t *>(in)[idx];
+    reinterpret_cast<uint4 *>(out)[idx] = make_uint4(T(x & 255u), T((x >> 8) & 255u), T((x >> 16) & 255u), T(x >> 24));
+  } else {
+    const uint32_t x = reinterpret_cast<const uint16_t *>(in)[idx];
+    reinterpret_cast<uint4 *>(out)[idx] = make_uint4(T(x & 15u), T((x >> 4) & 15u), T((x >> 8) & 15u), T(x >> 12));
+  }
+#undef T
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Wait-loop bound for the bulk pipeline (the loads it waits for are plain
+// global->shared copies, complete in microseconds).
+constexpr long long kBulkSpinLimit = 1ll << 24;
+__device__ int g_bulk_status;
+
+template <int KIND>
+__global__ void __launch_bounds__(kDecThreads)
+decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t nbytes, int fmt, int odt,
+                   const float *__restrict__ scale, int mode) {
+  using C = Dec<KIND>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
+  uint8_t *in_ring = smem_raw + C::kLutBytes;
+  uint8_t *out_ring = in_ring + kStages * C::kIn;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * kOutChunk);
+  const float s = load_scale(scale, mode);
+  const int64_t nch = nbytes / C::kIn;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < kStages; i++) {
+      const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
+      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
     }
   }
-  st_u256(out, w);
-}
-
-// in/out must be 32-byte aligned for the unit loop; the ragged tail (fewer
-// bytes than one unit per ... ) is decoded element-wise by block 0.
-template <bool FP4, int OUT_BYTES>
-__global__ void __launch_bounds__(kThreads)
-decode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t nbytes, int fmt, int odt,
-              const float *__restrict__ scale, int mode) {
-  using T = typename Lut<FP4, OUT_BYTES>::T;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  T *lut = reinterpret_cast<T *>(smem_raw);
-  build_lut<FP4, OUT_BYTES>(lut, fmt, odt, load_scale(scale, mode), mode);
-  const T *tab = lut + (threadIdx.x & 31u);
-
-  constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
-  const int64_t nunits = nbytes / IB;
-  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-  int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (; u + (kUnroll - 1) * nthreads < nunits; u += kUnroll * nthreads) {
-    // all loads of the step first: several independent loads in flight per thread
-    UnitIn<IB> in[kUnroll];
-#pragma unroll
-    for (int j = 0; j < kUnroll; j++) in[j] = load_unit<IB>(src + (u + j * nthreads) * IB);
-#pragma unroll
-    for (int j = 0; j < kUnroll; j++) decode_unit<FP4, OUT_BYTES>(in[j], dst + (u + j * nthreads) * 32, tab);
+  {  // table: distinct entries once, then one copy per lane
+    __shared__ uint32_t distinct[C::kLutEntries];
+    for (int c = threadIdx.x; c < C::kLutEntries; c += kDecThreads) distinct[c] = dec_entry<KIND>(c, fmt, odt, s, mode);
+    __syncthreads();
+    for (int i = threadIdx.x; i < C::kLutEntries * 32; i += kDecThreads) lut[i] = distinct[i >> 5];
+    __syncthreads();
   }
-  for (; u < nunits; u += nthreads) decode_unit<FP4, OUT_BYTES>(load_unit<IB>(src + u * IB), dst + u * 32, tab);
+  const uint32_t *tab = lut + (threadIdx.x & 31u);
 
-  if (blockIdx.x == 0) {
-    for (int64_t i = nunits * IB + threadIdx.x; i < nbytes; i += blockDim.x) {
-      const T e = tab[(uint32_t)src[i] << 5];
-      if constexpr (!FP4) {
-        if (OUT_BYTES == 4) reinterpret_cast<uint32_t *>(dst)[i] = e;
-        else reinterpret_cast<uint16_t *>(dst)[i] = (uint16_t)e;
-      } else {
-        reinterpret_cast<T *>(dst)[i] = e;
-      }
+  for (int64_t i = 0;; i++) {
+    const int64_t c = blockIdx.x + i * gridDim.x;
+    if (c >= nch) break;
+    const int st = (int)(i % kStages);
+    const uint32_t ph = (uint32_t)((i / kStages) & 1);
+    int timed_out = 0;
+    for (long long n = 0; !mbar_try(smem_addr(bar + st), ph);)
+      if (++n > kBulkSpinLimit) { timed_out = 1; break; }
+    if (__syncthreads_or(timed_out)) {  // block-uniform exit; the host sees the status word
+      if (threadIdx.x == 0) atomicExch(&g_bulk_status, 1);
+      break;
+    }
+    // the store issued kStages chunks ago must have finished reading out[st]
+    if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStages - 1) : "memory");
+    __syncthreads();
+    const uint8_t *in = in_ring + st * C::kIn;
+    uint8_t *out = out_ring + st * kOutChunk;
+#pragma unroll
+    for (int j = 0; j < C::kSteps; j++) dec_step<KIND>(in, out, threadIdx.x + j * kDecThreads, tab);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy smem accesses before the bulk copies
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + c * kOutChunk),
+                   "r"(smem_addr(out)), "r"(kOutChunk)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      const int64_t c2 = blockIdx.x + (i + kStages) * gridDim.x;
+      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + c2 * C::kIn, C::kIn, smem_addr(bar + st));
+    }
+  }
+  if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+
+  // ragged tail (fewer than kIn input bytes), element-wise through the table
+  if (blockIdx.x == gridDim.x - 1) {
+    for (int64_t b = nch * C::kIn + threadIdx.x; b < nbytes; b += kDecThreads) {
+      const uint32_t code = src[b];
+      if constexpr (KIND == DEC_FP8_16) reinterpret_cast<uint16_t *>(dst)[b] = (uint16_t)tab[code << 5];
+      else if constexpr (KIND == DEC_FP8_32 || KIND == DEC_FP4_16) reinterpret_cast<uint32_t *>(dst)[b] = tab[code << 5];
+      else reinterpret_cast<uint2 *>(dst)[b] = make_uint2(tab[(code & 15u) << 5], tab[(code >> 4) << 5]);
     }
   }
 }
@@ -574,7 +586,7 @@ quantize_rows_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *_
 // Resident CTAs per SM for `kernel` (queried once per kernel and device),
 // after raising its dynamic shared-memory limit when it needs more than 48 KiB.
 // The cache is keyed by the kernel's address: many kernels share one type.
-int resident_per_sm(const void *kernel, int smem_bytes) {
+int resident_per_sm(const void *kernel, int smem_bytes, int threads = kThreads) {
   struct Entry { const void *k; int dev; int n; };
   static Entry cache[128];
   static int used = 0;
@@ -587,20 +599,20 @@ int resident_per_sm(const void *kernel, int smem_bytes) {
   if (smem_bytes > 48 * 1024)
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem_bytes) != cudaSuccess || n < 1) n = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem_bytes) != cudaSuccess || n < 1) n = 1;
   if (used < 128) cache[used++] = Entry{kernel, dev, n};
   return n;
 }
 
-template <bool FP4, int OUT_BYTES>
+template <int KIND>
 void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt, const float *scale, int mode,
-                   cudaStream_t st, int dev) {
-  constexpr int smem = Lut<FP4, OUT_BYTES>::kBytes;
-  constexpr int IB = DecodeUnit<FP4, OUT_BYTES>::kInBytes;
-  const int per_sm = resident_per_sm((const void *)decode_kernel<FP4, OUT_BYTES>, smem);
-  const int g = grid_for(std::max<int64_t>(nbytes / IB, 1), kThreads, per_sm);
-  decode_kernel<FP4, OUT_BYTES><<<g, kThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, fmt, odt,
-                                                           scale, mode);
+                   cudaStream_t st) {
+  constexpr int smem = Dec<KIND>::kSmem;
+  const int per_sm = resident_per_sm((const void *)decode_bulk_kernel<KIND>, smem, kDecThreads);
+  const int64_t nch = nbytes / Dec<KIND>::kIn;
+  const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)current_sm_count() * per_sm));
+  decode_bulk_kernel<KIND><<<g, kDecThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, fmt, odt, scale,
+                                                        mode);
 }
 
 template <int SRC, int FMT>
@@ -702,9 +714,9 @@ extern "C" int fp8b200_decode_fp8(const void *src, int fp8_dtype, void *dst, int
   int dev;
   if (int rc = check_device(&dev)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  if (aligned32(src) && aligned32(dst)) {
-    if (out_dtype == FP8B200_F32) launch_decode<false, 4>(src, dst, n, fp8_dtype, out_dtype, scale, scale_mode, st, dev);
-    else launch_decode<false, 2>(src, dst, n, fp8_dtype, out_dtype, scale, scale_mode, st, dev);
+  if (aligned16(src) && aligned16(dst)) {
+    if (out_dtype == FP8B200_F32) launch_decode<DEC_FP8_32>(src, dst, n, fp8_dtype, out_dtype, scale, scale_mode, st);
+    else launch_decode<DEC_FP8_16>(src, dst, n, fp8_dtype, out_dtype, scale, scale_mode, st);
   } else {
     const int g = grid_for(n, kThreads, 4);
     decode_scalar_kernel<<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, 0, fp8_dtype, out_dtype,
@@ -724,9 +736,9 @@ extern "C" int fp8b200_decode_fp4(const void *src, int64_t nbytes, void *dst, in
   int dev;
   if (int rc = check_device(&dev)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  if (aligned32(src) && aligned32(dst)) {
-    if (out_dtype == FP8B200_F32) launch_decode<true, 4>(src, dst, nbytes, 0, out_dtype, scale, scale_mode, st, dev);
-    else launch_decode<true, 2>(src, dst, nbytes, 0, out_dtype, scale, scale_mode, st, dev);
+  if (aligned16(src) && aligned16(dst)) {
+    if (out_dtype == FP8B200_F32) launch_decode<DEC_FP4_32>(src, dst, nbytes, 0, out_dtype, scale, scale_mode, st);
+    else launch_decode<DEC_FP4_16>(src, dst, nbytes, 0, out_dtype, scale, scale_mode, st);
   } else {
     const int g = grid_for(nbytes, kThreads, 4);
     decode_scalar_kernel<<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, 1, 0, out_dtype,
