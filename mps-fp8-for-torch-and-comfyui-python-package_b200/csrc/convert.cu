@@ -421,6 +421,106 @@ encode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_
     dst[i] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(src, i), scaled, s);
 }
 
+// Bulk-copy pipeline for the encoders (same ring structure as the decoders):
+// chunks of 4096 elements (16 KiB of f32 or 8 KiB of 16-bit input) encode to
+// 4 KiB of fp8; each thread step converts 4 elements with one shared load.
+constexpr int kEncElems = 4096;
+
+template <int SRC>
+struct Enc {
+  static constexpr int kEB = SRC == FP8B200_F32 ? 4 : 2;
+  static constexpr int kIn = kEncElems * kEB;
+  static constexpr int kOut = kEncElems;
+  static constexpr int kSteps = kEncElems / 4 / kDecThreads;
+  static constexpr int kSmem = kStages * (kIn + kOut) + 64;
+};
+
+template <int SRC, int FMT>
+__device__ __forceinline__ uint32_t encode4(const uint8_t *in, int idx, bool scaled, float s) {
+  uint32_t raw[4];
+  if constexpr (SRC == FP8B200_F32) {
+    const uint4 v = reinterpret_cast<const uint4 *>(in)[idx];
+    raw[0] = v.x; raw[1] = v.y; raw[2] = v.z; raw[3] = v.w;
+  } else {
+    const uint2 v = reinterpret_cast<const uint2 *>(in)[idx];
+    raw[0] = v.x & 0xFFFFu; raw[1] = v.x >> 16; raw[2] = v.y & 0xFFFFu; raw[3] = v.y >> 16;
+  }
+  float x[4];
+  uint32_t amax = 0, sg;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    x[i] = widen<SRC>(raw[i], sg);
+    if (scaled) x[i] = __fmul_rn(x[i], s);
+    amax = max(amax, f2u(x[i]) & 0x7FFFFFFFu);
+  }
+  uint32_t o = cvt_pair<FMT>(x[0], x[1]) | (cvt_pair<FMT>(x[2], x[3]) << 16);
+  if (amax > special_threshold<FMT>()) {  // rare: overflow, inf or NaN present
+    o = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) o |= encode_one<SRC, FMT>(raw[i], scaled, s) << (8 * i);
+  }
+  return o;
+}
+
+template <int SRC, int FMT>
+__global__ void __launch_bounds__(kDecThreads)
+encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t n,
+                   const float *__restrict__ scale) {
+  using C = Enc<SRC>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint8_t *in_ring = smem_raw;
+  uint8_t *out_ring = in_ring + kStages * C::kIn;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * C::kOut);
+  const bool scaled = scale != nullptr;
+  const float s = scaled ? __ldg(scale) : 1.0f;
+  const int64_t nch = n / kEncElems;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < kStages; i++) {
+      const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
+      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
+    }
+  }
+  __syncthreads();
+  for (int64_t i = 0;; i++) {
+    const int64_t c = blockIdx.x + i * gridDim.x;
+    if (c >= nch) break;
+    const int st = (int)(i % kStages);
+    const uint32_t ph = (uint32_t)((i / kStages) & 1);
+    int timed_out = 0;
+    for (long long k = 0; !mbar_try(smem_addr(bar + st), ph);)
+      if (++k > kBulkSpinLimit) { timed_out = 1; break; }
+    if (__syncthreads_or(timed_out)) {
+      if (threadIdx.x == 0) atomicExch(&g_bulk_status, 1);
+      break;
+    }
+    if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStages - 1) : "memory");
+    __syncthreads();
+    const uint8_t *in = in_ring + st * C::kIn;
+    uint32_t *out = reinterpret_cast<uint32_t *>(out_ring + st * C::kOut);
+#pragma unroll
+    for (int j = 0; j < C::kSteps; j++) {
+      const int idx = threadIdx.x + j * kDecThreads;
+      out[idx] = encode4<SRC, FMT>(in, idx, scaled, s);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + c * C::kOut),
+                   "r"(smem_addr(out)), "r"(C::kOut)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      const int64_t c2 = blockIdx.x + (i + kStages) * gridDim.x;
+      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + c2 * C::kIn, C::kIn, smem_addr(bar + st));
+    }
+  }
+  if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (blockIdx.x == gridDim.x - 1)
+    for (int64_t e = nch * kEncElems + threadIdx.x; e < n; e += kDecThreads)
+      dst[e] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(src, e), scaled, s);
+}
+
 // ------------------------------------------------------------------ fp4 encode
 // The reference's nearest-of-8 threshold encoder (shaders/fp8_matmul.metal:
 // 88-102): not round-to-nearest-even at ties (0.25 -> 0.5, 1.25 -> 1.5), NaN
@@ -617,11 +717,16 @@ void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt,
 
 template <int SRC, int FMT>
 void launch_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
-  const bool vec = aligned32(src) && aligned16(dst);
-  const int64_t nunits = vec ? n / 16 : 0;
-  const int g = grid_for(std::max<int64_t>(vec ? nunits : n, 1), kThreads,
-                         resident_per_sm((const void *)encode_kernel<SRC, FMT>, 0));
-  encode_kernel<SRC, FMT><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, nunits, scale);
+  if (aligned16(src) && aligned16(dst)) {
+    constexpr int smem = Enc<SRC>::kSmem;
+    const int per_sm = resident_per_sm((const void *)encode_bulk_kernel<SRC, FMT>, smem, kDecThreads);
+    const int64_t nch = n / kEncElems;
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)current_sm_count() * per_sm));
+    encode_bulk_kernel<SRC, FMT><<<g, kDecThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, n, scale);
+  } else {  // unaligned: element-wise (the kernel's scalar loop)
+    const int g = grid_for(std::max<int64_t>(n, 1), kThreads, resident_per_sm((const void *)encode_kernel<SRC, FMT>, 0));
+    encode_kernel<SRC, FMT><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, 0, scale);
+  }
 }
 
 void launch_encode_any(int sdt, int fmt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
