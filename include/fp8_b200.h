@@ -115,6 +115,20 @@ int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t rows, int6
                               float *inv_scale, void *stream);
 
 /*
+ * Fused SiLU-gate + per-row quantisation (no counterpart in the reference;
+ * it feeds the rowwise fp8b200_scaled_mm of an FP8 MLP). gate_up is a
+ * rows x (2f) bfloat16 matrix with row stride ld elements whose row r holds
+ * [g_r | u_r]; for each row y_r = bf16(bf16(silu(g_r)) * u_r), rounded exactly
+ * as PyTorch computes F.silu(g) * u in bfloat16, is quantised like
+ * fp8b200_quantize_rows_fp8: dst_r = encode(y_r * scale_r) with scale_r =
+ * fmax/amax(y_r), inv_scale[r] = 1/scale_r. dst has row stride ld_dst bytes.
+ * Limits: f <= 102400 (the row of y is staged in shared memory).
+ */
+int fp8b200_silu_mul_quantize_rows_fp8(const void *gate_up, int64_t rows, int64_t f, int64_t ld,
+                                       void *dst, int64_t ld_dst, int fp8_dtype,
+                                       float *inv_scale, void *stream);
+
+/*
  * Allocation-free fp8b200_quantize_fp8 (no counterpart in the reference; the
  * reference has no device memory management of its own). Same inputs,
  * outputs and results, but no amax_scratch argument: the scratch is a fixed

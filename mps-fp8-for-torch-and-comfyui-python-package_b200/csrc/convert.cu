@@ -682,12 +682,89 @@ quantize_rows_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *_
   }
 }
 
+// ------------------------------------------------------------------ fused SiLU-gate quantize
+// For a row [g | u] of 2F bf16 values (the output of a fused gate/up
+// projection), y = bf16(bf16(silu(g)) * u) exactly as PyTorch's bf16 ops
+// compute F.silu(g) * u (silu in float: x / (1 + exp(-x)), rounded; product
+// in float, rounded), then y is quantised per row like quantize_rows_kernel.
+// One CTA per row; y is kept in shared memory between the two passes, so the
+// row is read from HBM once and the bf16 activation is never written.
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ uint32_t silu_mul_bf16(uint32_t g, uint32_t u) {
+  const float gf = u2f(g << 16), uf = u2f(u << 16);
+  const float s = bf16_round(gf / (1.0f + expf(-gf)));
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(s * uf));
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kRowThreads)
+silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *__restrict__ dst, int64_t ld_dst,
+                         int64_t rows, int64_t F, int vec, float fmax, float *__restrict__ inv_scale) {
+  extern __shared__ __align__(16) uint16_t ybuf[];  // F bf16 values of the current row
+  __shared__ uint32_t warp_max[kRowThreads / 32];
+  __shared__ float row_scale;
+  const int64_t nvec = vec ? F / 8 : 0;  // 8 bf16 per 16-byte vector
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t *g = gu + r * ld, *u = g + F;
+    uint32_t m = 0;
+    for (int64_t v = threadIdx.x; v < nvec; v += kRowThreads) {
+      const uint4 gv = reinterpret_cast<const uint4 *>(g)[v], uv = reinterpret_cast<const uint4 *>(u)[v];
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+      uint32_t yw[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint32_t y0 = silu_mul_bf16(gw[q] & 0xFFFFu, uw[q] & 0xFFFFu);
+        const uint32_t y1 = silu_mul_bf16(gw[q] >> 16, uw[q] >> 16);
+        m = max(m, max((y0 << 16) & 0x7FFFFFFFu, (y1 << 16) & 0x7FFFFFFFu));
+        yw[q] = y0 | (y1 << 16);
+      }
+      reinterpret_cast<uint4 *>(ybuf)[v] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+    }
+    for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads) {
+      const uint32_t y = silu_mul_bf16(g[i], u[i]);
+      m = max(m, (y << 16) & 0x7FFFFFFFu);
+      ybuf[i] = (uint16_t)y;
+    }
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < kRowThreads / 32; w++) t = max(t, warp_max[w]);
+      const double a = (double)u2f(t);
+      const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+      row_scale = (float)sd;
+      inv_scale[r] = (float)(1.0 / sd);
+    }
+    __syncthreads();
+    const float s = row_scale;
+    uint8_t *rd = dst + r * ld_dst;
+    for (int64_t v = threadIdx.x; v < nvec; v += kRowThreads) {  // 8 elements -> 8 bytes
+      const uint4 yv = reinterpret_cast<const uint4 *>(ybuf)[v];
+      const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+      uint32_t o[2] = {0u, 0u};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint32_t c0 = encode_one<FP8B200_BF16, FMT>(yw[q] & 0xFFFFu, true, s);
+        const uint32_t c1 = encode_one<FP8B200_BF16, FMT>(yw[q] >> 16, true, s);
+        o[q >> 1] |= (c0 | (c1 << 8)) << (16 * (q & 1));
+      }
+      reinterpret_cast<uint2 *>(rd)[v] = make_uint2(o[0], o[1]);
+    }
+    for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads)
+      rd[i] = (uint8_t)encode_one<FP8B200_BF16, FMT>(ybuf[i], true, s);
+    __syncthreads();  // ybuf / warp_max / row_scale are reused by the next row
+  }
+}
+
 // ------------------------------------------------------------------ launch helpers
 // Resident CTAs per SM for `kernel` (queried once per kernel and device),
 // after raising its dynamic shared-memory limit when it needs more than 48 KiB.
-// The cache is keyed by the kernel's address: many kernels share one type.
+// The cache is keyed by the kernel's address (many kernels share one type) and
+// the dynamic shared memory, which the fused row kernels size per call.
 int resident_per_sm(const void *kernel, int smem_bytes, int threads = kThreads) {
-  struct Entry { const void *k; int dev; int n; };
+  struct Entry { const void *k; int dev; int smem; int n; };
   static Entry cache[128];
   static int used = 0;
   static std::mutex mu;
@@ -695,12 +772,12 @@ int resident_per_sm(const void *kernel, int smem_bytes, int threads = kThreads) 
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; i++)
-    if (cache[i].k == kernel && cache[i].dev == dev) return cache[i].n;
+    if (cache[i].k == kernel && cache[i].dev == dev && cache[i].smem == smem_bytes) return cache[i].n;
   if (smem_bytes > 48 * 1024)
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem_bytes) != cudaSuccess || n < 1) n = 1;
-  if (used < 128) cache[used++] = Entry{kernel, dev, n};
+  if (used < 128) cache[used++] = Entry{kernel, dev, smem_bytes, n};
   return n;
 }
 
@@ -935,4 +1012,35 @@ extern "C" int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t
 #undef QR
   count_launch();
   return check_launch("quantize_rows");
+}
+
+extern "C" int fp8b200_silu_mul_quantize_rows_fp8(const void *gate_up, int64_t rows, int64_t f, int64_t ld,
+                                                  void *dst, int64_t ld_dst, int fp8_dtype, float *inv_scale,
+                                                  void *stream) {
+  if (rows < 0 || f < 0) return set_error(FP8B200_EINVAL, "silu_mul_quantize: negative size");
+  if (!is_fp8_dtype(fp8_dtype)) return set_error(FP8B200_EINVAL, "silu_mul_quantize: target dtype %d is not e4m3fn/e5m2", fp8_dtype);
+  if (ld < 2 * f || ld_dst < f) return set_error(FP8B200_EINVAL, "silu_mul_quantize: row stride smaller than the row");
+  const int64_t smem = f * 2;
+  if (smem > 200 * 1024) return set_error(FP8B200_EINVAL, "silu_mul_quantize: F=%lld exceeds the 102400-element row limit", (long long)f);
+  if (rows == 0) return FP8B200_OK;
+  if (!gate_up || !dst || !inv_scale) return set_error(FP8B200_EINVAL, "silu_mul_quantize: null pointer");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  // 16-byte vectors need every g and u row start 16-byte aligned (f and ld multiples of 8) and 8-byte output rows
+  const int vec = aligned16(gate_up) && f % 8 == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0 &&
+                  ld_dst % 8 == 0;
+  const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
+  const void *k = fp8_dtype == FP8B200_E4M3 ? (const void *)silu_mul_quantize_kernel<FP8B200_E4M3>
+                                            : (const void *)silu_mul_quantize_kernel<FP8B200_E5M2>;
+  const int per_sm = resident_per_sm(k, (int)smem, kRowThreads);
+  const int g = (int)std::min<int64_t>(rows, (int64_t)current_sm_count() * per_sm);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (fp8_dtype == FP8B200_E4M3)
+    silu_mul_quantize_kernel<FP8B200_E4M3><<<g, kRowThreads, smem, st>>>((const uint16_t *)gate_up, ld, (uint8_t *)dst,
+                                                                        ld_dst, rows, f, vec, fmax, inv_scale);
+  else
+    silu_mul_quantize_kernel<FP8B200_E5M2><<<g, kRowThreads, smem, st>>>((const uint16_t *)gate_up, ld, (uint8_t *)dst,
+                                                                        ld_dst, rows, f, vec, fmax, inv_scale);
+  count_launch();
+  return check_launch("silu_mul_quantize");
 }

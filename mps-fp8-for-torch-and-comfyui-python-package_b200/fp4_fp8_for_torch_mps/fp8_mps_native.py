@@ -170,6 +170,29 @@ def quantize_rows_fp8(x: torch.Tensor, fp8_dtype: torch.dtype = torch.float8_e4m
     return out.view(fp8_dtype), inv
 
 
+def silu_mul_quantize_rows_fp8(gate_up: torch.Tensor, fp8_dtype: torch.dtype = torch.float8_e4m3fn):
+    """Fused F.silu(g) * u followed by quantize_rows_fp8, for a bfloat16
+    (rows, 2F) gate/up projection whose columns are [g | u]: one launch reads
+    the projection once and writes the (rows, F) fp8 codes and the (rows, 1)
+    inverse scales; the bf16 activation is never stored. Bit-identical to
+    quantize_rows_fp8(F.silu(g) * u)."""
+    if fp8_dtype not in _FP8:
+        raise RuntimeError(f"silu_mul_quantize_rows_fp8: {fp8_dtype} is not an fp8 dtype")
+    if gate_up.dtype != torch.bfloat16 or gate_up.dim() != 2 or gate_up.shape[1] % 2:
+        raise RuntimeError("silu_mul_quantize_rows_fp8: expected a bfloat16 (rows, 2F) tensor")
+    rows, f = gate_up.shape[0], gate_up.shape[1] // 2
+    if gate_up.stride(1) != 1 or (rows > 1 and gate_up.stride(0) < 2 * f):
+        gate_up = gate_up.contiguous()
+    ld = gate_up.stride(0) if rows > 1 else 2 * f
+    out = torch.empty((rows, f), dtype=torch.uint8, device=gate_up.device)
+    inv = torch.empty((rows, 1), dtype=torch.float32, device=gate_up.device)
+    with torch.cuda.device(gate_up.device):
+        L.check(L.lib().fp8b200_silu_mul_quantize_rows_fp8(gate_up.data_ptr(), rows, f, ld,
+                                                           out.data_ptr(), f, L.dtype_code(fp8_dtype), inv.data_ptr(),
+                                                           L.stream_of(gate_up)), "silu_mul_quantize_rows")
+    return out.view(fp8_dtype), inv
+
+
 def fp8_quantize(input):
     """amax-scaled e4m3 encode; returns (codes, inv_scale f32[1])
     (fp8_mps_native.py:101-120), with the scale computed on the device."""

@@ -104,8 +104,9 @@ def rowwise_operands(m: int, n: int, k: int, seed: int = 0):
 # ---------------------------------------------------------------------------
 # FP8 weight-only inference stack: Llama-3-8B-shaped layers with random
 # weights. Every linear is torch._scaled_mm on e4m3 weights (per-tensor fp32
-# scale, broadcast per output column) and per-token e4m3 activations; norms,
-# rotary embedding, attention (SDPA) and SiLU stay in bf16 PyTorch.
+# scale, broadcast per output column) and per-token e4m3 activations; the
+# MLP's SiLU(g) * u is fused with its per-token quantisation; norms, rotary
+# embedding and attention (SDPA) stay in bf16 PyTorch.
 
 LLAMA = dict(hidden=4096, intermediate=14336, heads=32, kv_heads=8, head_dim=128, layers=32,
              rope_theta=500000.0, eps=1e-5)
@@ -144,9 +145,12 @@ class Fp8LlamaLayer:
         self.n2 = torch.ones(h, device=device, dtype=torch.bfloat16)
 
     gemm_events = None  # set to a list to record (start, end) CUDA events around each GEMM
+    fused = True        # SiLU(g) * u and its per-token quantisation in one kernel
 
     def linear(self, x2d, w, sw):
-        xq, xs = self.nat.quantize_rows_fp8(x2d)
+        return self.linear_q(*self.nat.quantize_rows_fp8(x2d), w, sw)
+
+    def linear_q(self, xq, xs, w, sw):
         if self.gemm_events is None:
             return torch._scaled_mm(xq, w.t(), xs, sw, out_dtype=torch.bfloat16)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -174,8 +178,12 @@ class Fp8LlamaLayer:
         x = x + self.linear(a, self.w_o, self.s_o)
         r = F.rms_norm(x, (h,), self.n2, c["eps"])
         gu = self.linear(r, self.w_gu, self.s_gu)
-        g, u = gu.chunk(2, dim=1)
-        x = x + self.linear(F.silu(g) * u, self.w_d, self.s_d)
+        if self.fused:
+            y = self.linear_q(*self.nat.silu_mul_quantize_rows_fp8(gu), self.w_d, self.s_d)
+        else:
+            g, u = gu.chunk(2, dim=1)
+            y = self.linear(F.silu(g) * u, self.w_d, self.s_d)
+        x = x + y
         return x
 
     def gemm_flops(self, tokens: int) -> float:

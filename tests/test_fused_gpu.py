@@ -1,0 +1,101 @@
+"""Device parity of the fused SiLU-gate + per-row quantisation kernel
+(fp8b200_silu_mul_quantize_rows_fp8) against the unfused path it replaces:
+PyTorch's bf16 F.silu(g) * u on the same GPU, then quantize_rows_fp8.
+Codes and inverse scales must be bit-identical."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+FP8 = (torch.float8_e4m3fn, torch.float8_e5m2)
+
+
+@pytest.fixture(scope="module")
+def nat(device):
+    from fp4_fp8_for_torch_mps import fp8_mps_native
+    return fp8_mps_native
+
+
+def unfused(nat, gu, fmt):
+    g, u = gu.chunk(2, dim=1)
+    return nat.quantize_rows_fp8(F.silu(g) * u, fmt)
+
+
+def assert_same(a, b):
+    (qa, sa), (qb, sb) = a, b
+    assert qa.shape == qb.shape and sa.shape == sb.shape
+    assert torch.equal(qa.view(torch.uint8), qb.view(torch.uint8))
+    assert torch.equal(sa.view(torch.int32), sb.view(torch.int32))
+
+
+@pytest.mark.parametrize("fmt", FP8)
+@pytest.mark.parametrize("rows,f", [(0, 64), (1, 1), (3, 7), (5, 8), (17, 1000), (257, 14336), (2, 24577)])
+def test_matches_unfused(nat, fmt, rows, f):
+    g = torch.Generator(device="cuda").manual_seed(rows * 131 + f)
+    gu = (torch.randn(rows, 2 * f, generator=g, device="cuda") * 3).to(torch.bfloat16)
+    assert_same(nat.silu_mul_quantize_rows_fp8(gu, fmt), unfused(nat, gu, fmt))
+
+
+@pytest.mark.parametrize("fmt", FP8)
+def test_every_bf16_gate_value(nat, fmt):
+    """All 65536 bf16 patterns as g (NaNs, infs, denormals included) in one
+    row of F = 65536 (128 KiB of shared memory), against three u rows."""
+    g = torch.arange(65536, dtype=torch.int32, device="cuda").to(torch.int16).view(torch.bfloat16)
+    for u in (torch.ones_like(g), -torch.full_like(g, 0.75),
+              torch.randn(65536, generator=torch.Generator(device="cuda").manual_seed(1),
+                          device="cuda").to(torch.bfloat16)):
+        gu = torch.cat([g, u])[None]
+        assert_same(nat.silu_mul_quantize_rows_fp8(gu, fmt), unfused(nat, gu, fmt))
+
+
+@pytest.mark.parametrize("fmt", FP8)
+def test_special_rows(nat, fmt):
+    """Rows that are all zero (scale 1), hold a NaN or an inf (amax NaN/inf),
+    or have one large value among tiny ones."""
+    f = 40
+    gu = torch.randn(6, 2 * f, generator=torch.Generator(device="cuda").manual_seed(2),
+                     device="cuda").to(torch.bfloat16)
+    gu[0] = 0
+    gu[1, 3] = float("nan")
+    gu[2, f + 5] = float("inf")
+    gu[3, 7] = float("-inf")
+    gu[4] *= 1e-30
+    gu[4, 9], gu[4, f + 9] = 30.0, 1000.0
+    gu[5, :f] = 80.0          # silu saturates to g
+    assert_same(nat.silu_mul_quantize_rows_fp8(gu, fmt), unfused(nat, gu, fmt))
+
+
+def test_strided_rows(nat):
+    """A row stride wider than 2F (a column slice of a wider projection) and
+    an unaligned base (odd element offset) takes the scalar path."""
+    base = (torch.randn(33, 304, generator=torch.Generator(device="cuda").manual_seed(3), device="cuda")
+            ).to(torch.bfloat16)
+    for off in (0, 1, 8):
+        gu = base[:, off:off + 256]
+        assert gu.stride(0) == 304
+        assert_same(nat.silu_mul_quantize_rows_fp8(gu), unfused(nat, gu.contiguous(), torch.float8_e4m3fn))
+
+
+def test_rejects_bad_input(nat):
+    x = torch.zeros(4, 6, dtype=torch.float32, device="cuda")
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        nat.silu_mul_quantize_rows_fp8(x)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        nat.silu_mul_quantize_rows_fp8(torch.zeros(4, 5, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(RuntimeError, match="row limit"):
+        nat.silu_mul_quantize_rows_fp8(torch.zeros(1, 2 * 102401, dtype=torch.bfloat16, device="cuda"))
+
+
+def test_llama_mlp_fused_equals_unfused(device):
+    """One Llama-shaped layer gives bit-identical hidden states with the
+    fused and the unfused MLP activation."""
+    from fp4_fp8_for_torch_mps import workloads as W
+    stack = W.Fp8LlamaStack("cuda", layers=1, seed=0)
+    x = W.llama_input(1, 256).cuda()
+    out = {}
+    for fused in (True, False):
+        stack.layers[0].fused = fused
+        out[fused] = stack.forward(x, 1, 256)
+    assert torch.equal(out[True].view(torch.int16), out[False].view(torch.int16))
