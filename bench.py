@@ -434,6 +434,86 @@ class ScaledMM:
             f"{rows}x{self.N}x{self.K} f32 dequantised matmul (CPU torch, {threads} threads)"
 
 
+class ScaledMMSmallM:
+    """Decode-sized rowwise GEMM: M (--m, default 16) activation rows against
+    Llama-shaped e4m3 weights (N, K from --shape). The weights dominate the
+    bytes, so the bound is HBM: work = N*K + M*K bytes read + 2*M*N written.
+    Weight sets rotate (>= 300 MB in total) so that every step reads its
+    weights from HBM, not L2."""
+    name = "scaled_mm_small_m"
+    metric = "scaled_mm_small_m_GBps"
+    unit, bound, kernels_per_step = "GB/s", "hbm", 1
+    dtype = "e4m3xe4m3->bf16 (f32 acc)"
+
+    def __init__(self, rank, args):
+        from fp4_fp8_for_torch_mps import _lib as L
+        from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
+        self.L = L
+        _, N, K = ROWWISE_SHAPES[args.shape]
+        M = args.m
+        aq, bq, sa, sb = rowwise_operands(M, N, K, seed=rank)
+        self.M, self.N, self.K = M, N, K
+        self.profile = f"{self.name}_{M}x{N}x{K}"
+        self.a_host, self.b_host, self.sa_host, self.sb_host = aq, bq, sa, sb
+        self.nsets = max(2, min(32, -(-300_000_000 // (N * K))))
+        self.a, self.sa, self.sb = aq.cuda(), sa.cuda(), sb.cuda()
+        b = bq.cuda()
+        self.bs = [b] + [b.clone() for _ in range(self.nsets - 1)]
+        self.out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        self.work = float(N * K + M * K + 2 * M * N)
+        self.h2d = M * K
+        self.d2h = M * N * 2
+        self.config = {"workload": self.name, "M": M, "N": N, "K": K, "scales": "rowwise", "out": "bf16",
+                       "l2": f"{self.nsets} rotating weight sets, {self.nsets * N * K / 2**20:.0f} MiB > L2"}
+        self.stream = torch.cuda.current_stream()
+        self.lib = L.lib()
+        self.i = 0
+        self.h_a = aq.view(torch.uint8).pin_memory()
+        self.h_out = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.d_a = torch.empty_like(self.a.view(torch.uint8))
+
+    def step(self):
+        L = self.L
+        b = self.bs[self.i % self.nsets]
+        self.i += 1
+        rc = self.lib.fp8b200_scaled_mm(self.a.data_ptr(), L.E4M3, self.K, b.data_ptr(), L.E4M3, self.K,
+                                        self.M, self.N, self.K, self.sa.data_ptr(), L.SCALE_ROWWISE,
+                                        self.sb.data_ptr(), L.SCALE_ROWWISE, None, 0, None, self.out.data_ptr(),
+                                        L.BF16, self.N, self.stream.cuda_stream)
+        if rc:
+            L.check(rc, "scaled_mm")
+
+    def e2e_step(self):
+        # public API: torch._scaled_mm on activations copied from pinned host
+        # memory (the weights stay resident, as in decoding), result read back
+        b = self.bs[self.i % self.nsets]
+        self.i += 1
+        self.d_a.copy_(self.h_a, non_blocking=True)
+        r = torch._scaled_mm(self.d_a.view(torch.float8_e4m3fn), b.t(), self.sa, self.sb,
+                             out_dtype=torch.bfloat16)
+        self.h_out.copy_(r, non_blocking=True)
+
+    def check(self):
+        import numpy as np
+        from oracle import oracle as O
+        ref, S = O.scaled_mm_ref(self.a_host.view(torch.uint8).numpy(), self.b_host.view(torch.uint8).numpy(),
+                                 self.sa_host.numpy().reshape(-1), self.sb_host.numpy().reshape(-1))
+        got = self.h_out.float().double().numpy()
+        return bool(np.all(np.abs(got - ref) <= O.bf16_ulp(ref) + 2.0 ** -20 * S))
+
+    def cpu_run(self, reps=3):
+        """float32 dequantise-and-matmul of the same M rows on the host."""
+        threads = torch.get_num_threads()
+        A = self.a_host.float() * self.sa_host.reshape(-1, 1)
+        B = self.b_host.float() * self.sb_host.reshape(-1, 1)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            (A @ B.t()).to(torch.bfloat16)
+        dt = (time.perf_counter() - t0) / reps
+        return self.work / dt / 1e9, threads, \
+            f"{self.M}x{self.N}x{self.K} f32 dequantised matmul (CPU torch, {threads} threads; weights pre-dequantised)"
+
+
 class LlamaFp8:
     """32 Llama-3-8B-shaped layers, e4m3 weights, per-token e4m3 activations,
     every linear through torch._scaled_mm; batch 8 x 2048 tokens split across
@@ -535,7 +615,7 @@ def llama_cpu_tokens_per_s(layers: int, reps: int = 1, seq: int = 256):
 
 WORKLOADS = {"fp4_decode": Fp4Decode, "fp8_roundtrip": Fp8RoundTrip, "llama_fp8": LlamaFp8,
              "scaled_mm": lambda r, a: ScaledMM(r, a, False),
-             "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True)}
+             "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True), "scaled_mm_small_m": ScaledMMSmallM}
 
 
 # ---------------------------------------------------------------- reference arm
@@ -553,6 +633,16 @@ def reference_line(args):
         vals = [Fp8RoundTrip.cpu_run(rows=4096, reps=1) for _ in range(max(args.steps, 1))]
         unit, metric = "GB/s", "fp8_roundtrip_GBps"
         config = {"workload": "fp8_roundtrip", "shape": [4096, 4096], "fp8": "e4m3fn"}
+    elif args.workload == "scaled_mm_small_m":
+        w = ScaledMMSmallM.__new__(ScaledMMSmallM)
+        from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
+        _, N, K = ROWWISE_SHAPES[args.shape]
+        w.a_host, w.b_host, w.sa_host, w.sb_host = rowwise_operands(args.m, N, K)
+        w.M, w.N, w.K = args.m, N, K
+        w.work = float(N * K + args.m * K + 2 * args.m * N)
+        vals = [w.cpu_run() for _ in range(max(args.steps, 1))]
+        unit, metric = "GB/s", "scaled_mm_small_m_GBps"
+        config = {"workload": args.workload, "M": args.m, "N": N, "K": K, "out": "bf16"}
     else:
         w = ScaledMM.__new__(ScaledMM)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands, scaled_mm_operands
@@ -583,6 +673,7 @@ def main():
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--shape", type=int, default=0, choices=[0, 1, 2])
     ap.add_argument("--layers", type=int, default=0, help="llama_fp8: number of layers (default 32)")
+    ap.add_argument("--m", type=int, default=16, help="scaled_mm_small_m: activation rows")
     args = ap.parse_args()
     rank, local, ws = rank_info()
 

@@ -63,6 +63,7 @@ struct Params {
   uint32_t idesc;
   unsigned long long timeout_ns;
   int debug_skip_first_load;
+  int sk_mt, sk_stages, sk_cs, sk_tmem_cols;  // small-M kernel: rows per tile, ring depth, split-K cluster, TMEM
 };
 
 // Status word: 0 = ok, otherwise (1 << 31) | site of the first wait that timed out.
@@ -653,6 +654,261 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   }
 }
 
+// ------------------------------------------------------------------ small-M kernel
+// For few rows of A (decode-time activations, M <= 256) the tiles above leave
+// most SMs idle: an M x N output has only ceil(N/256) column tiles. This
+// kernel swaps the operands so that the weights fill the MMA's 128 rows:
+// TMEM holds D^T for 128 output columns (lanes) x MT rows of A (fp32
+// columns, MT = M rounded up to 16, at most 256), computed by
+// tcgen05.mma.kind::f8f6f4 with M=128, N=MT, K=32. To fill the GPU when there
+// are few column tiles, the K range of each tile is split over a cluster of
+// `cs` CTAs (cs in 1, 2, 4, 8); after its MMAs every non-leader CTA writes
+// its fp32 partial tile into its own (now idle) shared-memory ring and the
+// leader adds the partials through distributed shared memory
+// (ld.shared::cluster) before the epilogue. No global scratch, no atomics.
+// Roles as in the other kernels: warp 0 TMA producer, warp 1 MMA issuer,
+// warps 2-5 epilogue; one tile per cluster.
+constexpr int SK_BN = 128;                 // output columns per tile (the MMA's M)
+constexpr int SK_B_BYTES = SK_BN * BK;     // 16 KiB of weights per stage
+constexpr int SK_MAX_MT = 256;
+constexpr int SK_MAX_STAGES = 8;
+constexpr int SK_RING_LIMIT = 192 * 1024;  // shared memory for the stage ring
+constexpr int SK_SMEM_MAX = SK_RING_LIMIT + 1024 /*align*/ + SK_MAX_MT * 4 /*row scales*/ + 256 /*barriers*/;
+
+constexpr int SK_MAX_CS = 8;               // largest split-K cluster
+
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+// Store four consecutive columns col0..col0+3 of one output row. `full`: all
+// four are in range and the row is 16-byte aligned (one vector store).
+__device__ __forceinline__ void store_quad(const Params &p, long long row, int col0, const float (&v)[4], bool full) {
+  char *base = reinterpret_cast<char *>(p.D);
+  const long long off = row * p.ldd + col0;
+  switch (p.out_dtype) {
+    case FP8B200_BF16:
+    case FP8B200_F16: {
+      const bool bf = p.out_dtype == FP8B200_BF16;
+      const uint32_t w0 = bf ? pack_bf16(v[0], v[1]) : pack_f16(v[0], v[1]);
+      const uint32_t w1 = bf ? pack_bf16(v[2], v[3]) : pack_f16(v[2], v[3]);
+      uint16_t *d = reinterpret_cast<uint16_t *>(base) + off;
+      if (full) {
+        *reinterpret_cast<uint2 *>(d) = make_uint2(w0, w1);
+      } else {
+        const uint32_t w[2] = {w0, w1};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          if (col0 + j < p.N) d[j] = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+      }
+      break;
+    }
+    case FP8B200_F32: {
+      float *d = reinterpret_cast<float *>(base) + off;
+      if (full) {
+        *reinterpret_cast<float4 *>(d) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          if (col0 + j < p.N) d[j] = v[j];
+      }
+      break;
+    }
+    default: {
+      uint32_t w = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        w |= (p.out_dtype == FP8B200_E4M3 ? enc8<FP8B200_E4M3>(v[j]) : enc8<FP8B200_E5M2>(v[j])) << (8 * j);
+      uint8_t *d = reinterpret_cast<uint8_t *>(base) + off;
+      if (full) {
+        *reinterpret_cast<uint32_t *>(d) = w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          if (col0 + j < p.N) d[j] = (uint8_t)(w >> (8 * j));
+      }
+      break;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const int MT = p.sk_mt, S = p.sk_stages, CS = p.sk_cs;
+  const uint32_t a_bytes = (uint32_t)MT * BK;
+  const uint32_t stage_bytes = SK_B_BYTES + a_bytes;
+  float *s_rs = reinterpret_cast<float *>(smem + S * stage_bytes);  // row scales of this tile's MT rows
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s_rs + SK_MAX_MT);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (S + s); };
+  const uint32_t tfull = bar_base + 8u * (2 * S);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
+  float *part = reinterpret_cast<float *>(smem);  // partial tile [MT][128] fp32, over the drained ring
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = CS > 1 ? cluster_rank() : 0u;
+  const int tile = CS > 1 ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int tn = tile % p.tiles_n, tm = tile / p.tiles_n;
+  const int kb0 = (int)((long long)rank * p.num_kb / CS), kb1 = (int)((long long)(rank + 1) * p.num_kb / CS);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(p.sk_tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  int ok = 1;
+  if (warp == 0) {
+    // ---------------- TMA producer: this CTA's K range of the tile
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; kb++) {
+        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) break;
+        if (p.debug_skip_first_load) break;  // test hook: never fill stage 0
+        mbar_expect_tx(full_bar(stage), stage_bytes);
+        const uint32_t st = base + (uint32_t)stage * stage_bytes;
+        tma_load_2d(st, &tmap_b, full_bar(stage), kb * BK, tn * SK_BN);
+        tma_load_2d(st + SK_B_BYTES, &tmap_a, full_bar(stage), kb * BK, tm * MT);
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: D^T[128 x MT] += B_tile . A_tile^T
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool fine = true;
+      for (int kb = kb0; kb < kb1; kb++) {
+        if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { fine = false; break; }
+        tc_fence_after();
+        const uint32_t st = base + (uint32_t)stage * stage_bytes;
+        const uint64_t wdesc = sdesc_sw128_kmajor(st);
+        const uint64_t xdesc = sdesc_sw128_kmajor(st + SK_B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; k++)
+          umma_f8f6f4(tmem_base, wdesc + (uint64_t)((k * UMMA_K) >> 4), xdesc + (uint64_t)((k * UMMA_K) >> 4),
+                      p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        umma_commit(empty_bar(stage));
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+      if (fine) umma_commit(tfull);
+    }
+  } else {
+    // ---------------- epilogue, part 1: row scales; wait for the accumulator;
+    // every CTA copies its fp32 tile (a partial sum when cs > 1) from TMEM
+    // into its drained shared-memory ring as part[row][128 columns]
+    const int etid = threadIdx.x - 64;
+    const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
+    for (int t = etid; t < MT; t += 128) {
+      const long long row = (long long)tm * MT + t;
+      s_rs[t] = p.sa_rowwise ? (row < p.M ? __ldg(p.sa + row) : 0.0f) : sa_t;
+    }
+    if (lane == 0) ok = mbar_wait(tfull, 0, p.timeout_ns, 4) ? 1 : 0;
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    tc_fence_after();
+    if (ok) {
+      const int quarter = warp & 3, nl = quarter * 32 + lane;
+      const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < MT; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_lane + (uint32_t)c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (c + j < MT) part[(c + j) * SK_BN + nl] = __uint_as_float(r[j]);
+      }
+    }
+  }
+  __syncwarp();
+  if (CS > 1) cluster_sync();  // every partial tile written; every CTA of the cluster is running
+  else __syncthreads();
+
+  if (warp >= 2) {
+    // ---------------- epilogue, part 2: CTA `rank` owns rows [r0, r1) of the
+    // tile; it sums the cs partial tiles (its own and its peers', through
+    // distributed shared memory, 16 bytes per lane), scales, adds the bias
+    // and stores. A warp handles one output row at a time: lane l covers
+    // columns 4l..4l+3, so a row segment is written with contiguous stores.
+    int okw = ok;
+    okw = __shfl_sync(0xFFFFFFFFu, okw, 0);
+    const int rows_valid = min(MT, p.M - tm * MT);
+    const int per = (rows_valid + CS - 1) / CS;
+    const int r0 = (int)rank * per, r1 = min(rows_valid, r0 + per);
+    const int ew = warp - 2;
+    const int c0 = tn * SK_BN + 4 * lane;  // first of this lane's four columns
+    float cs4[4], b4[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int col = c0 + j;
+      const bool in = col < p.N;
+      cs4[j] = in ? (p.sb_rowwise ? __ldg(p.sb + col) : __ldg(p.sb)) : 0.0f;
+      b4[j] = (in && p.bias != nullptr) ? load_bias(p.bias, p.bias_dtype, col) : 0.0f;
+    }
+    const float sr = p.scale_result ? __ldg(p.scale_result) : 1.0f;
+    const uint32_t part_addr = smem_u32(part);
+    const bool full = p.vec_store && c0 + 4 <= p.N;
+#pragma unroll 1
+    for (int t = r0 + ew; okw && t < r1; t += 4) {
+      const uint32_t off = (uint32_t)((t * SK_BN + 4 * lane) * 4);
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (CS == 1) {
+        const float4 a = *reinterpret_cast<const float4 *>(reinterpret_cast<const uint8_t *>(part) + off);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      } else {
+        float4 a[SK_MAX_CS];
+#pragma unroll
+        for (int q = 0; q < SK_MAX_CS; q++)
+          if (q < CS) a[q] = ld_cluster_v4(map_to_rank(part_addr + off, (uint32_t)q));
+#pragma unroll
+        for (int q = 0; q < SK_MAX_CS; q++)
+          if (q < CS) { v[0] += a[q].x; v[1] += a[q].y; v[2] += a[q].z; v[3] += a[q].w; }
+      }
+      const float rs = s_rs[t];
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] = (v[j] * (rs * cs4[j]) + b4[j]) * sr;
+      store_quad(p, (long long)tm * MT + t, c0, v, full);
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  if (CS > 1) cluster_sync();  // no CTA leaves while a peer may still read its shared memory
+  else __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.sk_tmem_cols)
+                 : "memory");
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -687,7 +943,7 @@ int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, in
 
 unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
 int g_debug_skip_first_load = 0;
-int g_path = 0;  // 0 = choose by shape, 1 = single-CTA kernel, 2 = CTA-pair kernel
+int g_path = 0;  // 0 = choose by shape, 1 = single-CTA kernel, 2 = CTA-pair kernel, 3 = small-M kernel
 
 // Resident 2-CTA clusters of the pair kernel on the current device.
 int pair_clusters(int dev) {
@@ -704,6 +960,60 @@ int pair_clusters(int dev) {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+// Resident clusters of `cs` CTAs of the small-M kernel with `smem` bytes of
+// dynamic shared memory on device `dev` (cs == 1: resident CTAs).
+int skinny_resident(int dev, int cs, int smem) {
+  struct Entry { int dev, cs, smem, n; };
+  static Entry cache[64];
+  static int used = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; i++)
+    if (cache[i].dev == dev && cache[i].cs == cs && cache[i].smem == smem) return cache[i].n;
+  int n = 0;
+  if (cs == 1) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scaled_mm_skinny_kernel, THREADS, smem) != cudaSuccess)
+      per_sm = 1;
+    n = std::max(per_sm, 1) * current_sm_count();
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)cs, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, scaled_mm_skinny_kernel, &cfg) != cudaSuccess) n = 0;
+    cudaGetLastError();  // an unsupported cluster size only disqualifies that size
+  }
+  if (used < 64) cache[used++] = Entry{dev, cs, smem, n};
+  return n;
+}
+
+// Split-K cluster size for `tiles` output tiles of `num_kb` k-blocks: the
+// size that keeps the most CTAs busy per wave; a larger cluster must gain at
+// least 15 % over the best smaller one (the partial reduction is not free).
+int skinny_cluster_size(int dev, long long tiles, int num_kb, int smem) {
+  int best_cs = 1;
+  double best = 0.0;
+  for (int cs = 1; cs <= 8; cs *= 2) {
+    if (cs > num_kb) break;
+    const int n = skinny_resident(dev, cs, smem);
+    if (n < 1) continue;
+    const long long waves = (tiles + n - 1) / n;
+    const double score = (double)(tiles * cs) / (double)waves;
+    if (cs == 1 || score > best * 1.15) {
+      if (score > best) { best = score; best_cs = cs; }
+    }
+  }
+  return best_cs;
 }
 
 }  // namespace gemm
@@ -739,16 +1049,25 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   int dev;
   if (int rc = check_device(&dev)) return rc;
 
-  const bool pair = g_path == 2 || (g_path == 0 && M >= 2 * BM && N >= PAIR_BN);
+  const bool skinny = g_path == 3 || (g_path == 0 && M <= SK_MAX_MT);
+  const bool pair = !skinny && (g_path == 2 || (g_path == 0 && M >= 2 * BM && N >= PAIR_BN));
+  // small-M kernel: MT rows of A per tile (M rounded up to 16, at most 256)
+  const int mt = skinny ? (int)std::min<int64_t>(SK_MAX_MT, (M + 15) / 16 * 16) : 0;
   CUtensorMap ma, mb;
-  if (int rc = make_kmajor_map(&ma, A, M, K, lda, BM)) return rc;
-  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, pair ? HALF_B : BN)) return rc;
+  if (int rc = make_kmajor_map(&ma, A, M, K, lda, skinny ? mt : BM)) return rc;
+  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, skinny ? SK_BN : (pair ? HALF_B : BN))) return rc;
 
   Params p;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.num_kb = (int)((K + BK - 1) / BK);
-  p.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
-  p.tiles_n = (int)((N + BN - 1) / BN);
+  if (skinny) {
+    p.tiles_m = (int)((M + mt - 1) / mt);
+    p.tiles_n = (int)((N + SK_BN - 1) / SK_BN);
+  } else {
+    p.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
+    p.tiles_n = (int)((N + BN - 1) / BN);
+  }
+  if ((long long)p.tiles_m * p.tiles_n > 0x7FFFFFFFLL / 8) return set_error(FP8B200_EINVAL, "scaled_mm: too many tiles");
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.sa = scale_a; p.sb = scale_b;
   p.sa_rowwise = scale_a_layout == FP8B200_SCALE_ROWWISE;
@@ -764,16 +1083,46 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((mma_m >> 4) << 24);
   p.timeout_ns = g_timeout_ns;
   p.debug_skip_first_load = g_debug_skip_first_load;
+  p.sk_mt = mt;
+  p.sk_stages = p.sk_cs = p.sk_tmem_cols = 0;
+  int sk_smem = 0;
+  if (skinny) {
+    // swapped operands: the weights (B) are the MMA's A (M=128), the rows of A its N (= mt)
+    p.idesc = (1u << 4) | (bfmt << 7) | (afmt << 10) | ((uint32_t)(mt >> 3) << 17) | ((uint32_t)(SK_BN >> 4) << 24);
+    const int stage_bytes = SK_B_BYTES + mt * BK;
+    p.sk_stages = std::min(SK_MAX_STAGES, SK_RING_LIMIT / stage_bytes);
+    int cols = 32;
+    while (cols < mt) cols *= 2;
+    p.sk_tmem_cols = cols;
+    sk_smem = p.sk_stages * stage_bytes + 1024 + SK_MAX_MT * 4 + 256;
+  }
 
   static bool attr_done[64] = {};
   if (dev < 64 && !attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(scaled_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(scaled_mm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
   }
-  if (pair) {
+  if (skinny) {
+    p.sk_cs = skinny_cluster_size(dev, p.num_tiles, p.num_kb, sk_smem);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.sk_cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(p.num_tiles * p.sk_cs), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)sk_smem;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.sk_cs > 1 ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel, ma, mb, p);
+  } else if (pair) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev));
     scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
   } else {
@@ -804,7 +1153,7 @@ extern "C" int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_t
 }
 
 extern "C" int fp8b200_gemm_set_path(int path) {
-  if (path < 0 || path > 2) return set_error(FP8B200_EINVAL, "gemm path must be 0 (auto), 1 or 2");
+  if (path < 0 || path > 3) return set_error(FP8B200_EINVAL, "gemm path must be 0 (auto), 1, 2 or 3");
   g_path = path;
   return FP8B200_OK;
 }

@@ -53,9 +53,9 @@ def nat(device):
     return fp8_mps_native
 
 
-@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"])
+@pytest.fixture(params=[1, 2, 3], ids=["single_cta", "cta_pair", "small_m"])
 def path(request, nat):
-    """Run the test on the single-CTA kernel and on the CTA-pair kernel."""
+    """Run the test on the single-CTA, the CTA-pair and the small-M kernel."""
     from fp4_fp8_for_torch_mps import _lib as L
     L.check(L.lib().fp8b200_gemm_set_path(request.param), "gemm path")
     yield request.param
@@ -215,6 +215,43 @@ def test_rowwise_workload(nat, shape):
     rows = np.sort(np.random.default_rng(N).choice(M, 96, replace=False))
     ref, S = O.scaled_mm_ref(codes(aq), codes(wq), sa.numpy().reshape(-1), sw.numpy().reshape(-1), rows=rows)
     check_close(out[torch.from_numpy(rows).cuda()], ref, S, f"rowwise {shape}")
+
+
+# ---------------------------------------------------------------- small M (split-K clusters)
+@pytest.mark.parametrize("M", [1, 2, 16, 33, 64, 200, 256])
+@pytest.mark.parametrize("N,K", [(1024, 8192), (4096, 4096), (6144, 4096), (4096, 14336)])
+def test_small_m_split_k(nat, M, N, K):
+    """Decode-sized activations against Llama-shaped weights on the default
+    (by shape) path: few column tiles, so K is split over clusters of up to 8
+    CTAs and reduced through distributed shared memory. Rowwise scales."""
+    g = torch.Generator().manual_seed(M * 13 + N + K)
+    a = rand_fp8((M, K), E4, g, 30.0)
+    b = rand_fp8((N, K), E4, g, 30.0)
+    sa = torch.rand(M, 1, generator=g) * 0.01 + 1e-3
+    sb = torch.rand(1, N, generator=g) * 0.01 + 1e-3
+    out = torch._scaled_mm(a.cuda(), b.cuda().t(), sa.cuda(), sb.cuda(), out_dtype=torch.bfloat16)
+    ref, S = O.scaled_mm_ref(codes(a), codes(b), sa.numpy().reshape(-1), sb.numpy().reshape(-1))
+    check_close(out, ref, S, f"{M}x{N}x{K}")
+
+
+def test_small_m_matches_other_kernels_closely(nat):
+    """The small-M kernel (split-K, DSMEM reduction) and the single-CTA kernel
+    agree to within the accumulation-order tolerance on the same inputs."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    g = torch.Generator().manual_seed(77)
+    a = rand_fp8((48, 8192), E4, g, 30.0).cuda()
+    b = rand_fp8((2048, 8192), E4, g, 30.0).cuda()
+    s = torch.tensor(0.003)
+    outs = []
+    for path_id in (3, 1):
+        L.check(L.lib().fp8b200_gemm_set_path(path_id), "gemm path")
+        try:
+            outs.append(nat.scaled_mm(a, b, s, s, out_dtype=torch.float32))
+        finally:
+            L.lib().fp8b200_gemm_set_path(0)
+    ref, S = O.scaled_mm_ref(codes(a), codes(b), 0.003, 0.003)
+    d = (outs[0] - outs[1]).abs().cpu().double().numpy()
+    assert np.all(d <= 2 * ACC_TOL * S + 2 * ulp(ref, torch.float32))
 
 
 # ---------------------------------------------------------------- failure detection
