@@ -682,49 +682,44 @@ quantize_rows_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *_
   }
 }
 
-// ------------------------------------------------------------------ fused SiLU-gate quantize
-// For a row [g | u] of 2F bf16 values (the output of a fused gate/up
-// projection), y = bf16(bf16(silu(g)) * u) exactly as PyTorch's bf16 ops
-// compute F.silu(g) * u (silu in float: x / (1 + exp(-x)), rounded; product
-// in float, rounded), then y is quantised per row like quantize_rows_kernel.
-// One CTA per row; y is kept in shared memory between the two passes, so the
-// row is read from HBM once and the bf16 activation is never written.
-__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
-__device__ __forceinline__ uint32_t silu_mul_bf16(uint32_t g, uint32_t u) {
-  const float gf = u2f(g << 16), uf = u2f(u << 16);
-  const float s = bf16_round(gf / (1.0f + expf(-gf)));
-  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(s * uf));
-}
-
-template <int FMT>
+// Register-resident variant for rows of at most KV * 256 * 16 elements whose
+// rows start 32-byte aligned (source) and 16-byte aligned (destination):
+// each thread loads its KV 16-element units once, keeps them in registers
+// through the amax reduction and encodes from registers, so every row is
+// read from HBM exactly once. Same results as quantize_rows_kernel.
+template <int SRC, int FMT, int KV>
 __global__ void __launch_bounds__(kRowThreads)
-silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *__restrict__ dst, int64_t ld_dst,
-                         int64_t rows, int64_t F, int vec, float fmax, float *__restrict__ inv_scale) {
-  extern __shared__ __align__(16) uint16_t ybuf[];  // F bf16 values of the current row
+quantize_rows_reg_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *__restrict__ dst, int64_t ld_dst,
+                         int64_t rows, int64_t cols, float fmax, float *__restrict__ inv_scale) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
   __shared__ uint32_t warp_max[kRowThreads / 32];
   __shared__ float row_scale;
-  const int64_t nvec = vec ? F / 8 : 0;  // 8 bf16 per 16-byte vector
+  const int nunits = (int)(cols / 16);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const uint16_t *g = gu + r * ld, *u = g + F;
-    uint32_t m = 0;
-    for (int64_t v = threadIdx.x; v < nvec; v += kRowThreads) {
-      const uint4 gv = reinterpret_cast<const uint4 *>(g)[v], uv = reinterpret_cast<const uint4 *>(u)[v];
-      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
-      uint32_t yw[4];
+    const uint8_t *rs = src + r * ld_src * EB;
+    uint8_t *rd = dst + r * ld_dst;
+    EncIn<SRC> in[KV];
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const uint32_t y0 = silu_mul_bf16(gw[q] & 0xFFFFu, uw[q] & 0xFFFFu);
-        const uint32_t y1 = silu_mul_bf16(gw[q] >> 16, uw[q] >> 16);
-        m = max(m, max((y0 << 16) & 0x7FFFFFFFu, (y1 << 16) & 0x7FFFFFFFu));
-        yw[q] = y0 | (y1 << 16);
-      }
-      reinterpret_cast<uint4 *>(ybuf)[v] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+    for (int k = 0; k < KV; k++) {
+      const int u = threadIdx.x + k * kRowThreads;
+      if (u < nunits) in[k] = load_enc<SRC>(rs + (int64_t)u * 16 * EB);
     }
-    for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads) {
-      const uint32_t y = silu_mul_bf16(g[i], u[i]);
-      m = max(m, (y << 16) & 0x7FFFFFFFu);
-      ybuf[i] = (uint16_t)y;
+    uint32_t m = 0, sg;
+#pragma unroll
+    for (int k = 0; k < KV; k++) {
+      if (threadIdx.x + k * kRowThreads < nunits) {
+#pragma unroll
+        for (int h = 0; h < EB / 2; h++) {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            if constexpr (EB == 4) m = max(m, f2u(widen<SRC>(in[k].a[h].w[j], sg)) & 0x7FFFFFFFu);
+            else {
+              m = max(m, f2u(widen<SRC>(in[k].a[h].w[j] & 0xFFFFu, sg)) & 0x7FFFFFFFu);
+              m = max(m, f2u(widen<SRC>(in[k].a[h].w[j] >> 16, sg)) & 0x7FFFFFFFu);
+            }
+          }
+        }
+      }
     }
     m = __reduce_max_sync(0xFFFFFFFFu, m);
     if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
@@ -739,19 +734,151 @@ silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *_
     }
     __syncthreads();
     const float s = row_scale;
-    uint8_t *rd = dst + r * ld_dst;
-    for (int64_t v = threadIdx.x; v < nvec; v += kRowThreads) {  // 8 elements -> 8 bytes
-      const uint4 yv = reinterpret_cast<const uint4 *>(ybuf)[v];
-      const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
-      uint32_t o[2] = {0u, 0u};
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const uint32_t c0 = encode_one<FP8B200_BF16, FMT>(yw[q] & 0xFFFFu, true, s);
-        const uint32_t c1 = encode_one<FP8B200_BF16, FMT>(yw[q] >> 16, true, s);
-        o[q >> 1] |= (c0 | (c1 << 8)) << (16 * (q & 1));
-      }
-      reinterpret_cast<uint2 *>(rd)[v] = make_uint2(o[0], o[1]);
+    for (int k = 0; k < KV; k++) {
+      const int u = threadIdx.x + k * kRowThreads;
+      if (u < nunits) encode_unit<SRC, FMT>(in[k], rd + (int64_t)u * 16, true, s);
     }
+    __syncthreads();  // warp_max / row_scale are reused by the next row
+  }
+}
+
+// ------------------------------------------------------------------ fused SiLU-gate quantize
+// For a row [g | u] of 2F bf16 values (the output of a fused gate/up
+// projection), y = bf16(bf16(silu(g)) * u) exactly as PyTorch's bf16 ops
+// compute F.silu(g) * u (silu in float: x / (1 + exp(-x)), rounded; product
+// in float, rounded), then y is quantised per row like quantize_rows_kernel.
+// One CTA per row; y is kept in shared memory between the two passes, so the
+// row is read from HBM once and the bf16 activation is never written.
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// bf16(silu(x)) for PyTorch's float formula x / (1 + expf(-x)) (expf, IEEE
+// division). Fast path: __expf and __fdividef, whose float result is within a
+// few tens of ulp of the formula for |x| <= 16; the rounding to bf16 agrees
+// whenever the fast value is more than 64 ulp from a bf16 rounding midpoint
+// (low 16 bits 0x8000). Otherwise, and for |x| > 16 or non-finite x, the
+// formula itself is evaluated. The inputs are bf16, so the agreement is checked
+// exhaustively (all 65536 gate values) against PyTorch on the device.
+__device__ __forceinline__ float silu_bf16(float x) {
+  if (fabsf(x) <= 16.0f) {
+    const float s = __fdividef(x, 1.0f + __expf(-x));
+    const int d = (int)(__float_as_uint(s) & 0xFFFFu) - 0x8000;
+    if (d > 64 || d < -64) return bf16_round(s);
+  }
+  return bf16_round(x / (1.0f + expf(-x)));
+}
+
+__device__ __forceinline__ uint32_t silu_mul_bf16(uint32_t g, uint32_t u) {
+  const float gf = u2f(g << 16), uf = u2f(u << 16);
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(silu_bf16(gf) * uf));
+}
+
+// The float silu(x) value that silu_bf16 rounds (fast or exact, whichever
+// rounds to the formula's bf16), for two values at once packed to bf16x2.
+__device__ __forceinline__ float silu_pre(float x) {
+  if (fabsf(x) <= 16.0f) {
+    const float s = __fdividef(x, 1.0f + __expf(-x));
+    const int d = (int)(__float_as_uint(s) & 0xFFFFu) - 0x8000;
+    if (d > 64 || d < -64) return s;
+  }
+  return x / (1.0f + expf(-x));
+}
+
+// Two bf16(silu(g)) * u products from packed bf16x2 words g and u. The
+// product of two bf16 values is exact in float, so one bf16x2 multiply
+// (round to nearest even, no contraction) equals PyTorch's float product
+// rounded to bf16.
+__device__ __forceinline__ uint32_t silu_mul_bf16x2(uint32_t g, uint32_t u) {
+  const __nv_bfloat162 s2 = __floats2bfloat162_rn(silu_pre(u2f(g << 16)), silu_pre(u2f(g & 0xFFFF0000u)));
+  uint32_t y;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t *>(&s2)), "r"(u));
+  return y;
+}
+
+// Eight bf16 values (one 16-byte vector) -> eight fp8 codes of value * s,
+// with the same results as encode_one (cvt pairs; per-element fix-up only
+// when an overflow, inf or NaN is present).
+template <int FMT>
+__device__ __forceinline__ uint2 encode8_bf16(uint4 v, float s) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float x[8];
+  uint32_t amax = 0;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    x[2 * q] = __fmul_rn(u2f(w[q] << 16), s);
+    x[2 * q + 1] = __fmul_rn(u2f(w[q] & 0xFFFF0000u), s);
+    amax = max(amax, max(f2u(x[2 * q]) & 0x7FFFFFFFu, f2u(x[2 * q + 1]) & 0x7FFFFFFFu));
+  }
+  uint32_t o[2];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+    o[h] = cvt_pair<FMT>(x[4 * h], x[4 * h + 1]) | (cvt_pair<FMT>(x[4 * h + 2], x[4 * h + 3]) << 16);
+  if (amax > special_threshold<FMT>()) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint32_t c = encode_one<FP8B200_BF16, FMT>((w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, true, s);
+      o[i >> 2] = (o[i >> 2] & ~(0xFFu << (8 * (i & 3)))) | (c << (8 * (i & 3)));
+    }
+  }
+  return make_uint2(o[0], o[1]);
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kRowThreads)
+silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *__restrict__ dst, int64_t ld_dst,
+                         int64_t rows, int64_t F, int vec, float fmax, float *__restrict__ inv_scale) {
+  extern __shared__ __align__(16) uint16_t ybuf[];  // F bf16 values of the current row
+  __shared__ uint32_t warp_max[kRowThreads / 32];
+  __shared__ float row_scale;
+  const int64_t nvec = vec ? F / 8 : 0;  // 8 bf16 per 16-byte vector
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t *g = gu + r * ld, *u = g + F;
+    const uint4 *g4 = reinterpret_cast<const uint4 *>(g), *u4 = reinterpret_cast<const uint4 *>(u);
+    uint32_t m_lo = 0, m_hi = 0;  // amax bits of the low and high bf16 halves
+    int64_t v = threadIdx.x;
+    for (; v + kRowThreads < nvec; v += 2 * kRowThreads) {  // two vectors of g and u in flight
+      const uint4 ga = g4[v], ua = u4[v], gb = g4[v + kRowThreads], ub = u4[v + kRowThreads];
+      const uint4 ya = make_uint4(silu_mul_bf16x2(ga.x, ua.x), silu_mul_bf16x2(ga.y, ua.y),
+                                  silu_mul_bf16x2(ga.z, ua.z), silu_mul_bf16x2(ga.w, ua.w));
+      const uint4 yb = make_uint4(silu_mul_bf16x2(gb.x, ub.x), silu_mul_bf16x2(gb.y, ub.y),
+                                  silu_mul_bf16x2(gb.z, ub.z), silu_mul_bf16x2(gb.w, ub.w));
+      const uint32_t ys[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
+#pragma unroll
+      for (int q = 0; q < 8; q++) { m_lo = max(m_lo, ys[q] & 0x7FFFu); m_hi = max(m_hi, ys[q] & 0x7FFF0000u); }
+      reinterpret_cast<uint4 *>(ybuf)[v] = ya;
+      reinterpret_cast<uint4 *>(ybuf)[v + kRowThreads] = yb;
+    }
+    for (; v < nvec; v += kRowThreads) {
+      const uint4 ga = g4[v], ua = u4[v];
+      const uint4 ya = make_uint4(silu_mul_bf16x2(ga.x, ua.x), silu_mul_bf16x2(ga.y, ua.y),
+                                  silu_mul_bf16x2(ga.z, ua.z), silu_mul_bf16x2(ga.w, ua.w));
+      const uint32_t ys[4] = {ya.x, ya.y, ya.z, ya.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) { m_lo = max(m_lo, ys[q] & 0x7FFFu); m_hi = max(m_hi, ys[q] & 0x7FFF0000u); }
+      reinterpret_cast<uint4 *>(ybuf)[v] = ya;
+    }
+    for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads) {
+      const uint32_t y = silu_mul_bf16(g[i], u[i]);
+      m_lo = max(m_lo, y & 0x7FFFu);
+      ybuf[i] = (uint16_t)y;
+    }
+    uint32_t m = max(m_lo << 16, m_hi);
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < kRowThreads / 32; w++) t = max(t, warp_max[w]);
+      const double a = (double)u2f(t);
+      const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+      row_scale = (float)sd;
+      inv_scale[r] = (float)(1.0 / sd);
+    }
+    __syncthreads();
+    const float s = row_scale;
+    uint8_t *rd = dst + r * ld_dst;
+    for (int64_t w = threadIdx.x; w < nvec; w += kRowThreads)  // 8 elements -> 8 bytes
+      reinterpret_cast<uint2 *>(rd)[w] = encode8_bf16<FMT>(reinterpret_cast<const uint4 *>(ybuf)[w], s);
     for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads)
       rd[i] = (uint8_t)encode_one<FP8B200_BF16, FMT>(ybuf[i], true, s);
     __syncthreads();  // ybuf / warp_max / row_scale are reused by the next row
@@ -981,6 +1108,36 @@ extern "C" int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, i
   return FP8B200_OK;
 }
 
+template <int SRC, int FMT, int KV>
+void launch_rows_reg_t(const uint8_t *s, int64_t ld_src, uint8_t *d, int64_t ld_dst, int64_t rows, int64_t cols,
+                       float fmax, float *inv, cudaStream_t st) {
+  const void *k = (const void *)quantize_rows_reg_kernel<SRC, FMT, KV>;
+  const int g = (int)std::min<int64_t>(rows, (int64_t)current_sm_count() * resident_per_sm(k, 0, kRowThreads));
+  quantize_rows_reg_kernel<SRC, FMT, KV><<<g, kRowThreads, 0, st>>>(s, ld_src, d, ld_dst, rows, cols, fmax, inv);
+}
+
+template <int SRC, int FMT>
+void launch_rows_reg_kv(int kv, const uint8_t *s, int64_t ld_src, uint8_t *d, int64_t ld_dst, int64_t rows,
+                        int64_t cols, float fmax, float *inv, cudaStream_t st) {
+  if (kv == 1) launch_rows_reg_t<SRC, FMT, 1>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  else if (kv == 2) launch_rows_reg_t<SRC, FMT, 2>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  else if (kv == 4) launch_rows_reg_t<SRC, FMT, 4>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  else launch_rows_reg_t<SRC, FMT, 8>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+}
+
+void launch_rows_reg(int src_dtype, int fp8_dtype, int kv, const uint8_t *s, int64_t ld_src, uint8_t *d,
+                     int64_t ld_dst, int64_t rows, int64_t cols, float fmax, float *inv, cudaStream_t st) {
+  if (fp8_dtype == FP8B200_E4M3) {
+    if (src_dtype == FP8B200_F32) launch_rows_reg_kv<FP8B200_F32, FP8B200_E4M3>(kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else if (src_dtype == FP8B200_BF16) launch_rows_reg_kv<FP8B200_BF16, FP8B200_E4M3>(kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else launch_rows_reg_kv<FP8B200_F16, FP8B200_E4M3>(kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  } else {
+    if (src_dtype == FP8B200_F32) launch_rows_reg_kv<FP8B200_F32, FP8B200_E5M2>(kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else if (src_dtype == FP8B200_BF16) launch_rows_reg_kv<FP8B200_BF16, FP8B200_E5M2>(kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else launch_rows_reg_kv<FP8B200_F16, FP8B200_E5M2>(kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  }
+}
+
 extern "C" int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t ld_src,
                                          void *dst, int64_t ld_dst, int fp8_dtype, float *inv_scale, void *stream) {
   if (rows < 0 || cols < 0) return set_error(FP8B200_EINVAL, "quantize_rows: negative size");
@@ -995,10 +1152,17 @@ extern "C" int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t
   // 32-byte loads need every row start 32-byte aligned, 16-byte stores every output row 16-byte aligned
   const int vec = aligned32(src) && (ld_src * eb) % 32 == 0 && aligned16(dst) && ld_dst % 16 == 0;
   const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
-  const int g = (int)std::min<int64_t>(rows, (int64_t)current_sm_count() * 8);
   cudaStream_t st = (cudaStream_t)stream;
   const uint8_t *s = (const uint8_t *)src;
   uint8_t *d = (uint8_t *)dst;
+  const int64_t nunits = cols / 16;
+  if (vec && cols % 16 == 0 && nunits <= 8 * kRowThreads) {  // whole row in registers
+    const int kv = nunits <= kRowThreads ? 1 : nunits <= 2 * kRowThreads ? 2 : nunits <= 4 * kRowThreads ? 4 : 8;
+    launch_rows_reg(src_dtype, fp8_dtype, kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv_scale, st);
+    count_launch();
+    return check_launch("quantize_rows");
+  }
+  const int g = (int)std::min<int64_t>(rows, (int64_t)current_sm_count() * 8);
 #define QR(SRC, FMT) quantize_rows_kernel<SRC, FMT><<<g, kRowThreads, 0, st>>>(s, ld_src, d, ld_dst, rows, cols, vec, fmax, inv_scale)
   if (fp8_dtype == FP8B200_E4M3) {
     if (src_dtype == FP8B200_F32) QR(FP8B200_F32, FP8B200_E4M3);

@@ -927,7 +927,39 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows);
+
+// Tensor maps describe only an address, extents, a stride and a box, so an
+// encoded map stays valid for any later call with the same five values. A
+// small per-thread cache skips the driver's encode on repeated calls (the
+// decode-time case: the same weights and activation buffers every step).
 int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+  struct Entry { const void *ptr; int64_t rows, k, ld; int box; int dev; CUtensorMap map; };
+  constexpr int kEntries = 32;
+  thread_local Entry cache[kEntries];
+  thread_local int used = 0, next = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (int i = 0; i < used; i++) {
+    const Entry &e = cache[i];
+    if (e.ptr == ptr && e.rows == rows && e.k == k && e.ld == ld && e.box == box_rows && e.dev == dev) {
+      *m = e.map;
+      return FP8B200_OK;
+    }
+  }
+  if (int rc = encode_kmajor_map(m, ptr, rows, k, ld, box_rows)) return rc;
+  int slot;
+  if (used < kEntries) {
+    slot = used++;
+  } else {  // round-robin replacement
+    slot = next;
+    next = (next + 1) % kEntries;
+  }
+  cache[slot] = Entry{ptr, rows, k, ld, box_rows, dev, *m};
+  return FP8B200_OK;
+}
+
+int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};

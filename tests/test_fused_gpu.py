@@ -64,6 +64,8 @@ def test_special_rows(nat, fmt):
     gu[4] *= 1e-30
     gu[4, 9], gu[4, f + 9] = 30.0, 1000.0
     gu[5, :f] = 80.0          # silu saturates to g
+    gu[5, 2], gu[5, f + 2] = float("inf"), 0.0     # inf * 0 -> NaN
+    gu[5, 3], gu[5, f + 3] = float("-inf"), 2.0    # silu(-inf) is NaN
     assert_same(nat.silu_mul_quantize_rows_fp8(gu, fmt), unfused(nat, gu, fmt))
 
 
