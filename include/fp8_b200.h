@@ -212,10 +212,12 @@ int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
 /*
  * Kernel choice for fp8b200_scaled_mm: 0 = by shape (M <= 256: the small-M
  * kernel, which puts 128 output columns on the MMA's rows and splits K over
- * a cluster of up to 8 CTAs; else the CTA-pair kernel with 256x256 tiles when
- * N >= 256, else the single-CTA kernel with 128x256 tiles), 1 = always
- * single-CTA, 2 = always CTA-pair, 3 = always small-M (tiles of 256 rows of
- * A when M > 256). Process-wide; for tests and tuning.
+ * a cluster of up to 8 CTAs; else, when N >= 256, a CTA pair per 256x512
+ * output tile, or per 256x256 tile where the wider tiles would leave too many
+ * SMs idle in the last wave; else the single-CTA kernel with 128x256 tiles),
+ * 1 = always single-CTA, 2 = always CTA-pair 256x256, 3 = always small-M
+ * (tiles of 256 rows of A when M > 256), 4 = always CTA-pair 256x512.
+ * Process-wide; for tests and tuning.
  */
 int fp8b200_gemm_set_path(int path);
 

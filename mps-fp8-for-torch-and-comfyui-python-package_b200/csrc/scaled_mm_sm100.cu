@@ -31,6 +31,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace fp8b200 {
@@ -64,6 +65,7 @@ struct Params {
   unsigned long long timeout_ns;
   int debug_skip_first_load;
   int sk_mt, sk_stages, sk_cs, sk_tmem_cols;  // small-M kernel: rows per tile, ring depth, split-K cluster, TMEM
+  int tma_store;                              // epilogue stores through the output tensor map
 };
 
 // Status word: 0 = ok, otherwise (1 << 31) | site of the first wait that timed out.
@@ -307,6 +309,104 @@ __device__ __forceinline__ void drain_accumulator(const Params &p, uint32_t t_ac
   }
 }
 
+// ---- epilogue through TMA stores
+// Each epilogue warp converts a 32-row x 32-column chunk of its accumulator
+// rows into a staging buffer in shared memory laid out as the TMA store's box
+// (32 rows of 32 * esz bytes) with the tensor map's swizzle (32, 64 or
+// 128 bytes: the 16-byte unit u of row r sits at u ^ f(r)), so that the
+// warp's 16-byte shared stores are conflict-free without any dynamic register
+// indexing; one lane then stores the box with cp.async.bulk.tensor (whole row
+// segments, asynchronous, clipped at the tensor's edges). Two buffers per
+// warp (one for fp32 output) alternate; a buffer is rewritten only after the
+// store that reads it has finished reading.
+constexpr int STG_WARP_BYTES = 4096;  // per epilogue warp
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Drain 256 accumulator columns of this warp's 32 rows through TMA stores.
+// stg: this warp's 4 KiB staging region (1024-byte aligned); nstore counts the
+// stores this warp has issued (selects the buffer).
+__device__ __forceinline__ void drain_accumulator_tma(const Params &p, const CUtensorMap *tmap_d, uint32_t t_acc,
+                                                      int row0, int n0, int quarter, int lane, float rs_t,
+                                                      const float *col_scale, const float *col_bias, float sr,
+                                                      uint32_t stg, uint32_t &nstore) {
+  const int row = row0 + quarter * 32 + lane;
+  const float rs = p.sa_rowwise ? ((row < p.M) ? __ldg(p.sa + row) : 0.0f) : rs_t;
+  const uint32_t t_row = t_acc + ((uint32_t)(quarter * 32) << 16);
+  const int esz = p.out_dtype == FP8B200_F32 ? 4 : (p.out_dtype == FP8B200_BF16 || p.out_dtype == FP8B200_F16) ? 2 : 1;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; c++) {
+    const int col0 = n0 + c * 32;
+    if (col0 >= p.N) break;  // warp-uniform
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      v[j] = (__uint_as_float(r[j]) * (rs * col_scale[c * 32 + j]) + col_bias[c * 32 + j]) * sr;
+    // pick the buffer; wait until the store that last read it is done reading
+    uint32_t buf;
+    if (esz == 4) {
+      buf = stg;
+      if (lane == 0) bulk_wait_read_0();
+    } else {
+      buf = stg + (nstore & 1u) * 2048u;
+      if (lane == 0) bulk_wait_read_1();
+    }
+    __syncwarp();
+    if (esz == 4) {  // 128-byte rows, 128-byte swizzle: unit u of row r at u ^ (r & 7)
+      const uint32_t rb = buf + (uint32_t)lane * 128u;
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        st_shared_v4(rb + (uint32_t)((u ^ (lane & 7)) * 16), __float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                     __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
+    } else if (esz == 2) {  // 64-byte rows, 64-byte swizzle: unit u of row r at u ^ ((r >> 1) & 3)
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        w[j] = p.out_dtype == FP8B200_BF16 ? pack_bf16(v[2 * j], v[2 * j + 1]) : pack_f16(v[2 * j], v[2 * j + 1]);
+      const uint32_t rb = buf + (uint32_t)lane * 64u;
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        st_shared_v4(rb + (uint32_t)((u ^ ((lane >> 1) & 3)) * 16), w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+    } else {  // 32-byte rows, 32-byte swizzle: unit u of row r at u ^ ((r >> 2) & 1)
+      uint32_t w[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        uint32_t cc[4];
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+          cc[t] = p.out_dtype == FP8B200_E4M3 ? enc8<FP8B200_E4M3>(v[4 * q + t]) : enc8<FP8B200_E5M2>(v[4 * q + t]);
+        w[q] = cc[0] | (cc[1] << 8) | (cc[2] << 16) | (cc[3] << 24);
+      }
+      const uint32_t rb = buf + (uint32_t)lane * 32u;
+#pragma unroll
+      for (int u = 0; u < 2; u++)
+        st_shared_v4(rb + (uint32_t)((u ^ ((lane >> 2) & 1)) * 16), w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+    }
+    fence_proxy_async_smem();  // make the generic-proxy writes visible to the bulk copy
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmap_d, buf, col0, row0 + quarter * 32);
+      bulk_commit();
+    }
+    ++nstore;
+  }
+}
+
 // ------------------------------------------------------------------ single-CTA kernel
 __global__ void __launch_bounds__(THREADS, 1)
 scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -455,11 +555,16 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 // arrives on the leader's tmem_empty barrier.
 constexpr int PAIR_BN = 256;              // output columns per pair tile
 constexpr int HALF_B = PAIR_BN / 2;       // B rows loaded per CTA
-constexpr int STAGES2 = 6;
+constexpr int STAGES2_MAX = 7;
 constexpr int A2_BYTES = BM * BK;         // 16 KiB
 constexpr int B2_BYTES = HALF_B * BK;     // 16 KiB
 constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 /*align*/ + 2 * BN * 4 /*column tables*/ + 256;
+constexpr int SMEM2_TAIL = 2 * BN * 4 /*column tables*/ + 256 /*barriers*/;
+// The per-CTA maximum: the ring takes as many 32 KiB stages as fit after the
+// 1024-byte alignment of its base (7 when the dynamic shared memory starts at
+// most 768 bytes before a 1024-byte boundary, else 6), then the tables.
+constexpr int SMEM2_BYTES = 227 * 1024;
+static_assert(6 * STAGE2_BYTES + 1023 + SMEM2_TAIL <= SMEM2_BYTES, "six stages always fit");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -523,17 +628,19 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t *smem = smem_raw + (base - raw_addr);
-  const uint32_t sA = base;                       // STAGES2 x 16 KiB
-  const uint32_t sB = base + STAGES2 * A2_BYTES;  // STAGES2 x 16 KiB
-  float *s_scale = reinterpret_cast<float *>(smem + STAGES2 * STAGE2_BYTES);
+  // ring depth: the same in both CTAs (same kernel, same dynamic shared-memory base)
+  const int nst = min(STAGES2_MAX, (int)((raw_addr + SMEM2_BYTES - base - SMEM2_TAIL) / STAGE2_BYTES));
+  const uint32_t sA = base;                   // nst x 16 KiB
+  const uint32_t sB = base + nst * A2_BYTES;  // nst x 16 KiB
+  float *s_scale = reinterpret_cast<float *>(smem + nst * STAGE2_BYTES);
   float *s_bias = s_scale + BN;
   uint64_t *bars = reinterpret_cast<uint64_t *>(s_bias + BN);
   const uint32_t bar_base = smem_u32(bars);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
-  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES2 + s); };
-  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES2 + b); };
-  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES2 + 2 + b); };
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES2 + 4);
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES2_MAX + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES2_MAX + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES2_MAX + 2 + b); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES2_MAX + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -542,7 +649,7 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   const int npairs = (int)num_clusters_x();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES2; s++) {
+    for (int s = 0; s < nst; s++) {
       mbar_init(full_bar(s), 1);   // used in the leader only
       mbar_init(empty_bar(s), 1);  // one multicast commit per use
     }
@@ -583,7 +690,7 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * STAGE2_BYTES);
           tma_load_2d_pair(sA + stage * A2_BYTES, &tmap_a, leader_full, kb * BK, arow);
           tma_load_2d_pair(sB + stage * B2_BYTES, &tmap_b, leader_full, kb * BK, brow);
-          if (++stage == STAGES2) { stage = 0; phase ^= 1u; }
+          if (++stage == nst) { stage = 0; phase ^= 1u; }
         }
       }
     }
@@ -609,7 +716,7 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             umma_f8f6f4_pair(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
                              p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
           umma_commit_pair(empty_bar(stage));
-          if (++stage == STAGES2) { stage = 0; phase ^= 1u; }
+          if (++stage == nst) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         umma_commit_pair(tfull_bar(acc));
@@ -643,6 +750,213 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still touch its shared memory
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ CTA-pair wide kernel
+// 256 x 512 output tile per pair. Each K step issues two
+// tcgen05.mma.cta_group::2 (M=256, N=256) that share the A tile, so a k-block
+// moves 48 KiB per CTA (its 128 rows of A plus a 128-row half of each of the
+// two B blocks) for twice the MMA work of the 256 x 256 kernel: a quarter
+// fewer bytes from L2 per flop, which is what bounds the 256 x 256 kernel on
+// large shapes. The two 256-column accumulators fill TMEM, so the accumulator
+// is single-buffered: the MMA thread waits for the epilogue to drain it while
+// the producer keeps prefetching the next tile's k-blocks into the 4-stage ring.
+constexpr int WIDE_BN = 512;
+constexpr int W_STAGES = 4;
+constexpr int W_STAGE_BYTES = A2_BYTES + 2 * B2_BYTES;  // 48 KiB
+constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + 4 * STG_WARP_BYTES /*epilogue staging*/ + 1024 /*align*/ +
+                             2 * WIDE_BN * 4 /*column tables*/ + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_d, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  // stage s: [A 16 KiB | B half of block 0, 16 KiB | B half of block 1, 16 KiB]
+  auto stage_a = [&](int s) { return base + (uint32_t)(s * W_STAGE_BYTES); };
+  const uint32_t stg_base = base + (uint32_t)(W_STAGES * W_STAGE_BYTES);  // 4 x 4 KiB epilogue staging
+  float *s_scale = reinterpret_cast<float *>(smem + W_STAGES * W_STAGE_BYTES + 4 * STG_WARP_BYTES);  // 512 columns
+  float *s_bias = s_scale + WIDE_BN;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s_bias + WIDE_BN);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (W_STAGES + s); };
+  const uint32_t tfull = bar_base + 8u * (2 * W_STAGES);
+  auto tempty_bar = [&](int h) { return bar_base + 8u * (2 * W_STAGES + 1 + h); };  // accumulator half h drained
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * W_STAGES + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = (int)cluster_id_x();
+  const int npairs = (int)num_clusters_x();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < W_STAGES; s++) {
+      mbar_init(full_bar(s), 1);   // used in the leader only
+      mbar_init(empty_bar(s), 1);  // one multicast commit per use
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty_bar(0), 8);  // four epilogue warps in each CTA (leader's barriers)
+    mbar_init(tempty_bar(1), 8);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    if (p.tma_store) tma_prefetch_desc(&tmap_d);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        const int arow = tm * (2 * BM) + (int)rank * BM;
+        const int brow0 = tn * WIDE_BN + (int)rank * HALF_B;
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (p.debug_skip_first_load) { ok = false; break; }
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * W_STAGE_BYTES);
+          const uint32_t st = stage_a(stage);
+          tma_load_2d_pair(st, &tmap_a, leader_full, kb * BK, arow);
+          tma_load_2d_pair(st + A2_BYTES, &tmap_b, leader_full, kb * BK, brow0);
+          tma_load_2d_pair(st + A2_BYTES + B2_BYTES, &tmap_b, leader_full, kb * BK, brow0 + PAIR_BN);
+          if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only)
+    // From the second tile on, the first W_STAGES k-blocks are issued in two
+    // passes: the half-0 MMAs as soon as the epilogue has drained accumulator
+    // half 0, then (stages still resident, their empty barriers not yet
+    // committed) the half-1 MMAs once half 1 is drained, so the tensor core
+    // works through most of the previous tile's epilogue.
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+        const int head = min(W_STAGES, p.num_kb);  // k-blocks issued in two passes
+        if (!mbar_wait(tempty_bar(0), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        tc_fence_after();
+        {
+          int st = stage;
+          uint32_t ph = phase;
+          for (int kb = 0; kb < head; kb++) {
+            if (!mbar_wait(full_bar(st), ph, p.timeout_ns, 3)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = stage_a(st);
+            const uint64_t adesc = sdesc_sw128_kmajor(sa);
+            const uint64_t b0desc = sdesc_sw128_kmajor(sa + A2_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; k++) {
+              const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
+              umma_f8f6f4_pair(tmem_base, adesc + koff, b0desc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            }
+            if (++st == W_STAGES) { st = 0; ph ^= 1u; }
+          }
+        }
+        if (!ok) break;
+        if (!mbar_wait(tempty_bar(1), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < head; kb++) {  // same stages, already full
+          const uint32_t sa = stage_a(stage);
+          const uint64_t adesc = sdesc_sw128_kmajor(sa);
+          const uint64_t b1desc = sdesc_sw128_kmajor(sa + A2_BYTES + B2_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; k++) {
+            const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
+            umma_f8f6f4_pair(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(empty_bar(stage));
+          if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        for (int kb = head; kb < p.num_kb; kb++) {
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = stage_a(stage);
+          const uint64_t adesc = sdesc_sw128_kmajor(sa);
+          const uint64_t b0desc = sdesc_sw128_kmajor(sa + A2_BYTES);
+          const uint64_t b1desc = sdesc_sw128_kmajor(sa + A2_BYTES + B2_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; k++) {
+            const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
+            umma_f8f6f4_pair(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
+            umma_f8f6f4_pair(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc, 1u);
+          }
+          umma_commit_pair(empty_bar(stage));
+          if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull);
+        acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows x 512 columns
+    const int quarter = warp & 3;
+    const int etid = threadIdx.x - 64;
+    const uint32_t stg = stg_base + (uint32_t)((warp - 2) * STG_WARP_BYTES);
+    uint32_t nstore = 0;
+    uint32_t acc_phase = 0;
+    const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
+    const float sb_t = p.sb_rowwise ? 0.0f : __ldg(p.sb);
+    const float sr = p.scale_result ? __ldg(p.scale_result) : 1.0f;
+    for (int tile = pair; tile < p.num_tiles; tile += npairs) {
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      epilogue_sync();
+      stage_columns(p, tn * WIDE_BN, sb_t, s_scale, s_bias, etid);
+      stage_columns(p, tn * WIDE_BN + PAIR_BN, sb_t, s_scale + PAIR_BN, s_bias + PAIR_BN, etid);
+      epilogue_sync();
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(tfull, acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row0 = tm * (2 * BM) + (int)rank * BM;
+#pragma unroll 1
+      for (int h = 0; h < 2; h++) {  // release each half as soon as it is read
+        if (p.tma_store)
+          drain_accumulator_tma(p, &tmap_d, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN,
+                                quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, stg, nstore);
+        else
+          drain_accumulator(p, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN, quarter, lane,
+                            sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(h), 0));
+      }
+      acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_all();  // this warp's stores are done before its staging memory goes away
   }
 
   tc_fence_before();
@@ -973,25 +1287,60 @@ int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, 
   return FP8B200_OK;
 }
 
+// Output tensor map for the TMA-store epilogue: rows x cols of esz-byte
+// elements, row stride ldd elements, 32 x 32 boxes, swizzle matching the
+// staging layout (32 * esz bytes per box row).
+int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ldd, int esz) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ldd * esz)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : esz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = enc(m, dt, 2, D, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FP8B200_EINVAL, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return FP8B200_OK;
+}
+
 unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
 int g_debug_skip_first_load = 0;
-int g_path = 0;  // 0 = choose by shape, 1 = single-CTA kernel, 2 = CTA-pair kernel, 3 = small-M kernel
+int g_path = 0;  // 0 = by shape, 1 = single-CTA, 2 = CTA-pair 256x256, 3 = small-M, 4 = CTA-pair 256x512
 
-// Resident 2-CTA clusters of the pair kernel on the current device.
-int pair_clusters(int dev) {
-  static int cached[64] = {};
+// Resident 2-CTA clusters of the pair kernel (wide = false) or the wide
+// kernel (wide = true) on device `dev`.
+int pair_clusters(int dev, bool wide) {
+  static int cached[2][64] = {};
   if (dev < 0 || dev >= 64) return 1;
-  if (!cached[dev]) {
+  int &c = cached[wide ? 1 : 0][dev];
+  if (!c) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74, 1, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
-    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    cfg.dynamicSmemBytes = wide ? W_SMEM_BYTES : SMEM2_BYTES;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, scaled_mm_pair_kernel, &cfg) != cudaSuccess || n < 1)
-      n = current_sm_count() / 2;
-    cached[dev] = n;
+    const cudaError_t e = wide ? cudaOccupancyMaxActiveClusters(&n, scaled_mm_wide_kernel, &cfg)
+                               : cudaOccupancyMaxActiveClusters(&n, scaled_mm_pair_kernel, &cfg);
+    if (e != cudaSuccess || n < 1) n = current_sm_count() / 2;
+    c = n;
   }
-  return cached[dev];
+  return c;
+}
+
+// The wide kernel does twice the work per tile; prefer it unless its tile
+// count fills the resident clusters in so few waves that the coarser
+// granularity costs more than 10 % against 256 x 256 tiles.
+bool prefer_wide(int dev, int64_t M, int64_t N) {
+  if (N < WIDE_BN) return false;
+  const int64_t slots = pair_clusters(dev, true);
+  const int64_t tm = (M + 2 * BM - 1) / (2 * BM);
+  const int64_t waves_pair = (tm * ((N + PAIR_BN - 1) / PAIR_BN) + slots - 1) / slots;
+  const int64_t waves_wide = (tm * ((N + WIDE_BN - 1) / WIDE_BN) + slots - 1) / slots;
+  return 2.0 * (double)waves_wide <= 1.1 * (double)waves_pair;
 }
 
 // Resident clusters of `cs` CTAs of the small-M kernel with `smem` bytes of
@@ -1080,9 +1429,22 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     return set_error(FP8B200_EINVAL, "scaled_mm: bias must be f32/bf16/f16");
   int dev;
   if (int rc = check_device(&dev)) return rc;
+  static bool attr_done[64] = {};
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(scaled_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(scaled_mm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(scaled_mm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(scaled_mm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
 
   const bool skinny = g_path == 3 || (g_path == 0 && M <= SK_MAX_MT);
-  const bool pair = !skinny && (g_path == 2 || (g_path == 0 && M >= 2 * BM && N >= PAIR_BN));
+  const bool pair = !skinny && (g_path == 2 || g_path == 4 || (g_path == 0 && M >= 2 * BM && N >= PAIR_BN));
+  const bool wide = pair && (g_path == 4 || (g_path == 0 && prefer_wide(dev, M, N)));
   // small-M kernel: MT rows of A per tile (M rounded up to 16, at most 256)
   const int mt = skinny ? (int)std::min<int64_t>(SK_MAX_MT, (M + 15) / 16 * 16) : 0;
   CUtensorMap ma, mb;
@@ -1097,7 +1459,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     p.tiles_n = (int)((N + SK_BN - 1) / SK_BN);
   } else {
     p.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
-    p.tiles_n = (int)((N + BN - 1) / BN);
+    p.tiles_n = (int)((N + (wide ? WIDE_BN : BN) - 1) / (wide ? WIDE_BN : BN));
   }
   if ((long long)p.tiles_m * p.tiles_n > 0x7FFFFFFFLL / 8) return set_error(FP8B200_EINVAL, "scaled_mm: too many tiles");
   p.num_tiles = p.tiles_m * p.tiles_n;
@@ -1117,6 +1479,13 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.debug_skip_first_load = g_debug_skip_first_load;
   p.sk_mt = mt;
   p.sk_stages = p.sk_cs = p.sk_tmem_cols = 0;
+  p.tma_store = 0;
+  CUtensorMap md;
+  memset(&md, 0, sizeof(md));
+  if (wide && p.vec_store) {
+    if (int rc = make_out_map(&md, D, M, N, ldd, esz)) return rc;
+    p.tma_store = 1;
+  }
   int sk_smem = 0;
   if (skinny) {
     // swapped operands: the weights (B) are the MMA's A (M=128), the rows of A its N (= mt)
@@ -1129,16 +1498,6 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     sk_smem = p.sk_stages * stage_bytes + 1024 + SK_MAX_MT * 4 + 256;
   }
 
-  static bool attr_done[64] = {};
-  if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(scaled_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(scaled_mm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(scaled_mm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
-    if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
-    attr_done[dev] = true;
-  }
   if (skinny) {
     p.sk_cs = skinny_cluster_size(dev, p.num_tiles, p.num_kb, sk_smem);
     cudaLaunchConfig_t cfg = {};
@@ -1154,8 +1513,11 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     cfg.attrs = attr;
     cfg.numAttrs = p.sk_cs > 1 ? 1 : 0;
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel, ma, mb, p);
+  } else if (wide) {
+    const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
+    scaled_mm_wide_kernel<<<2 * clusters, THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
   } else if (pair) {
-    const int clusters = std::min(p.num_tiles, pair_clusters(dev));
+    const int clusters = std::min(p.num_tiles, pair_clusters(dev, false));
     scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
   } else {
     const int grid = std::min(p.num_tiles, current_sm_count());
@@ -1185,7 +1547,7 @@ extern "C" int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_t
 }
 
 extern "C" int fp8b200_gemm_set_path(int path) {
-  if (path < 0 || path > 3) return set_error(FP8B200_EINVAL, "gemm path must be 0 (auto), 1, 2 or 3");
+  if (path < 0 || path > 4) return set_error(FP8B200_EINVAL, "gemm path must be 0 (auto), 1, 2, 3 or 4");
   g_path = path;
   return FP8B200_OK;
 }

@@ -53,9 +53,10 @@ def nat(device):
     return fp8_mps_native
 
 
-@pytest.fixture(params=[1, 2, 3], ids=["single_cta", "cta_pair", "small_m"])
+@pytest.fixture(params=[1, 2, 3, 4], ids=["single_cta", "cta_pair", "small_m", "cta_pair_wide"])
 def path(request, nat):
-    """Run the test on the single-CTA, the CTA-pair and the small-M kernel."""
+    """Run the test on the single-CTA, the CTA-pair (256x256 and 256x512
+    tiles) and the small-M kernel."""
     from fp4_fp8_for_torch_mps import _lib as L
     L.check(L.lib().fp8b200_gemm_set_path(request.param), "gemm path")
     yield request.param
