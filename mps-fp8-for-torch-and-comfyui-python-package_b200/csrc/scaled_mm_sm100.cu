@@ -153,6 +153,18 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait for the outstanding TMEM loads, with r as read-write operands so that
+// no use of the loaded registers can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
 // 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1 (sm_100).
@@ -278,6 +290,8 @@ __device__ __forceinline__ void store_row_chunk(const Params &p, int row, int co
 
 // Named barrier among the four epilogue warps (128 threads).
 __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier among the eight epilogue warps of the wide kernel (256 threads).
+__device__ __forceinline__ void wide_epilogue_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // The tile's per-column factors (tensorwise or rowwise scale_b; bias or 0),
 // loaded once per tile by the 128 epilogue threads into shared memory.
@@ -295,15 +309,15 @@ __device__ __forceinline__ void stage_columns(const Params &p, int n0, float sb_
 // 32-lane quarter of TMEM (rows) in 32-column chunks.
 __device__ __forceinline__ void drain_accumulator(const Params &p, uint32_t t_acc, int row0, int n0, int quarter,
                                                   int lane, float rs_t, const float *s_scale, const float *s_bias,
-                                                  float sr) {
+                                                  float sr, int cfirst = 0, int cstep = 1) {
   const int row = row0 + quarter * 32 + lane;
   const float rs = p.sa_rowwise ? ((row < p.M) ? __ldg(p.sa + row) : 0.0f) : rs_t;
   const uint32_t t_row = t_acc + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; c++) {
+  for (int c = cfirst; c < BN / 32; c += cstep) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
-    tmem_ld_wait();
+    tmem_ld_wait(r);
     const int col0 = n0 + c * 32;
     if (row < p.M && col0 < p.N) store_row_chunk(p, row, col0, r, rs, s_scale + c * 32, s_bias + c * 32, sr);
   }
@@ -311,15 +325,15 @@ __device__ __forceinline__ void drain_accumulator(const Params &p, uint32_t t_ac
 
 // ---- epilogue through TMA stores
 // Each epilogue warp converts a 32-row x 32-column chunk of its accumulator
-// rows into a staging buffer in shared memory laid out as the TMA store's box
-// (32 rows of 32 * esz bytes) with the tensor map's swizzle (32, 64 or
-// 128 bytes: the 16-byte unit u of row r sits at u ^ f(r)), so that the
-// warp's 16-byte shared stores are conflict-free without any dynamic register
-// indexing; one lane then stores the box with cp.async.bulk.tensor (whole row
-// segments, asynchronous, clipped at the tensor's edges). Two buffers per
-// warp (one for fp32 output) alternate; a buffer is rewritten only after the
-// store that reads it has finished reading.
-constexpr int STG_WARP_BYTES = 4096;  // per epilogue warp
+// rows into a 2 KiB staging buffer in shared memory laid out as the TMA
+// store's box (32 rows of 64 bytes: 32 bf16/f16 or 16 fp32 values; 32 rows of
+// 32 bytes for fp8) with the tensor map's swizzle (the 16-byte unit u of row r
+// sits at u ^ f(r)), so that the warp's 16-byte shared stores are
+// conflict-free without dynamic register indexing; one lane then stores the
+// box with cp.async.bulk.tensor (whole row segments, asynchronous, clipped at
+// the tensor's edges). The buffer is rewritten only after the previous store
+// from it has finished reading.
+constexpr int W_STG_BYTES = 2048;  // per epilogue warp
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
@@ -335,75 +349,104 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-// Drain 256 accumulator columns of this warp's 32 rows through TMA stores.
-// stg: this warp's 4 KiB staging region (1024-byte aligned); nstore counts the
-// stores this warp has issued (selects the buffer).
+// Convert one 32-column chunk (accumulator values r, row scale rs) and store
+// it through this warp's staging buffer with TMA stores of box (col0, y0)
+// (two 16-column boxes for fp32).
+__device__ __forceinline__ void store_chunk_tma(const Params &p, const CUtensorMap *tmap_d, const uint32_t (&r)[32],
+                                                float rs, const float *cs, const float *cb, float sr, int lane,
+                                                int col0, int y0, int esz, uint32_t buf) {
+  float v[32];
+#pragma unroll
+  for (int q = 0; q < 8; q++) {  // 16-byte broadcast reads of the column tables
+    const float4 s4 = reinterpret_cast<const float4 *>(cs)[q];
+    const float4 b4 = reinterpret_cast<const float4 *>(cb)[q];
+    v[4 * q] = (__uint_as_float(r[4 * q]) * (rs * s4.x) + b4.x) * sr;
+    v[4 * q + 1] = (__uint_as_float(r[4 * q + 1]) * (rs * s4.y) + b4.y) * sr;
+    v[4 * q + 2] = (__uint_as_float(r[4 * q + 2]) * (rs * s4.z) + b4.z) * sr;
+    v[4 * q + 3] = (__uint_as_float(r[4 * q + 3]) * (rs * s4.w) + b4.w) * sr;
+  }
+  const uint32_t row64 = buf + (uint32_t)lane * 64u;
+  const uint32_t sw64 = (uint32_t)((lane >> 1) & 3);  // 64-byte swizzle of row `lane`
+  if (esz == 4) {  // two boxes of 16 fp32 columns
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      if (lane == 0) bulk_wait_read_0();
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        st_shared_v4(row64 + ((u ^ sw64) * 16u), __float_as_uint(v[16 * h + 4 * u]),
+                     __float_as_uint(v[16 * h + 4 * u + 1]), __float_as_uint(v[16 * h + 4 * u + 2]),
+                     __float_as_uint(v[16 * h + 4 * u + 3]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmap_d, buf, col0 + 16 * h, y0);
+        bulk_commit();
+      }
+    }
+    return;
+  }
+  if (lane == 0) bulk_wait_read_0();
+  __syncwarp();
+  if (esz == 2) {
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+      w[j] = p.out_dtype == FP8B200_BF16 ? pack_bf16(v[2 * j], v[2 * j + 1]) : pack_f16(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+    for (int u = 0; u < 4; u++) st_shared_v4(row64 + ((u ^ sw64) * 16u), w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+  } else {  // fp8: 32-byte rows, 32-byte swizzle: unit u of row r at u ^ ((r >> 2) & 1)
+    uint32_t w[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      uint32_t cc[4];
+#pragma unroll
+      for (int t = 0; t < 4; t++)
+        cc[t] = p.out_dtype == FP8B200_E4M3 ? enc8<FP8B200_E4M3>(v[4 * q + t]) : enc8<FP8B200_E5M2>(v[4 * q + t]);
+      w[q] = cc[0] | (cc[1] << 8) | (cc[2] << 16) | (cc[3] << 24);
+    }
+    const uint32_t rb = buf + (uint32_t)lane * 32u;
+#pragma unroll
+    for (int u = 0; u < 2; u++)
+      st_shared_v4(rb + (uint32_t)((u ^ ((lane >> 2) & 1)) * 16), w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+  }
+  fence_proxy_async_smem();  // make the generic-proxy writes visible to the bulk copy
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmap_d, buf, col0, y0);
+    bulk_commit();
+  }
+}
+
+// Drain chunks cfirst, cfirst + cstep, ... of 256 accumulator columns of this
+// warp's 32 rows through TMA stores (buf: this warp's staging buffer). The
+// TMEM loads run one chunk ahead of the conversion (two register sets), so
+// their latency hides behind the previous chunk's arithmetic.
 __device__ __forceinline__ void drain_accumulator_tma(const Params &p, const CUtensorMap *tmap_d, uint32_t t_acc,
                                                       int row0, int n0, int quarter, int lane, float rs_t,
                                                       const float *col_scale, const float *col_bias, float sr,
-                                                      uint32_t stg, uint32_t &nstore) {
+                                                      uint32_t buf, int cfirst, int cstep) {
   const int row = row0 + quarter * 32 + lane;
   const float rs = p.sa_rowwise ? ((row < p.M) ? __ldg(p.sa + row) : 0.0f) : rs_t;
   const uint32_t t_row = t_acc + ((uint32_t)(quarter * 32) << 16);
   const int esz = p.out_dtype == FP8B200_F32 ? 4 : (p.out_dtype == FP8B200_BF16 || p.out_dtype == FP8B200_F16) ? 2 : 1;
+  const int y0 = row0 + quarter * 32;
+  const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);  // chunks with at least one column in range
+  if (cfirst >= nchunks) return;
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(t_row + (uint32_t)(cfirst * 32), ra);
+  tmem_ld_wait(ra);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; c++) {
-    const int col0 = n0 + c * 32;
-    if (col0 >= p.N) break;  // warp-uniform
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
-    tmem_ld_wait();
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; j++)
-      v[j] = (__uint_as_float(r[j]) * (rs * col_scale[c * 32 + j]) + col_bias[c * 32 + j]) * sr;
-    // pick the buffer; wait until the store that last read it is done reading
-    uint32_t buf;
-    if (esz == 4) {
-      buf = stg;
-      if (lane == 0) bulk_wait_read_0();
-    } else {
-      buf = stg + (nstore & 1u) * 2048u;
-      if (lane == 0) bulk_wait_read_1();
-    }
-    __syncwarp();
-    if (esz == 4) {  // 128-byte rows, 128-byte swizzle: unit u of row r at u ^ (r & 7)
-      const uint32_t rb = buf + (uint32_t)lane * 128u;
-#pragma unroll
-      for (int u = 0; u < 8; u++)
-        st_shared_v4(rb + (uint32_t)((u ^ (lane & 7)) * 16), __float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
-                     __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
-    } else if (esz == 2) {  // 64-byte rows, 64-byte swizzle: unit u of row r at u ^ ((r >> 1) & 3)
-      uint32_t w[16];
-#pragma unroll
-      for (int j = 0; j < 16; j++)
-        w[j] = p.out_dtype == FP8B200_BF16 ? pack_bf16(v[2 * j], v[2 * j + 1]) : pack_f16(v[2 * j], v[2 * j + 1]);
-      const uint32_t rb = buf + (uint32_t)lane * 64u;
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        st_shared_v4(rb + (uint32_t)((u ^ ((lane >> 1) & 3)) * 16), w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
-    } else {  // 32-byte rows, 32-byte swizzle: unit u of row r at u ^ ((r >> 2) & 1)
-      uint32_t w[8];
-#pragma unroll
-      for (int q = 0; q < 8; q++) {
-        uint32_t cc[4];
-#pragma unroll
-        for (int t = 0; t < 4; t++)
-          cc[t] = p.out_dtype == FP8B200_E4M3 ? enc8<FP8B200_E4M3>(v[4 * q + t]) : enc8<FP8B200_E5M2>(v[4 * q + t]);
-        w[q] = cc[0] | (cc[1] << 8) | (cc[2] << 16) | (cc[3] << 24);
-      }
-      const uint32_t rb = buf + (uint32_t)lane * 32u;
-#pragma unroll
-      for (int u = 0; u < 2; u++)
-        st_shared_v4(rb + (uint32_t)((u ^ ((lane >> 2) & 1)) * 16), w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
-    }
-    fence_proxy_async_smem();  // make the generic-proxy writes visible to the bulk copy
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(tmap_d, buf, col0, row0 + quarter * 32);
-      bulk_commit();
-    }
-    ++nstore;
+  for (int c = cfirst; c < nchunks; c += 2 * cstep) {
+    const int c1 = c + cstep, c2 = c + 2 * cstep;
+    if (c1 < nchunks) tmem_ld_32x32b_x32(t_row + (uint32_t)(c1 * 32), rb);
+    store_chunk_tma(p, tmap_d, ra, rs, col_scale + c * 32, col_bias + c * 32, sr, lane, n0 + c * 32, y0, esz, buf);
+    tmem_ld_wait(rb);
+    if (c1 >= nchunks) break;
+    if (c2 < nchunks) tmem_ld_32x32b_x32(t_row + (uint32_t)(c2 * 32), ra);
+    store_chunk_tma(p, tmap_d, rb, rs, col_scale + c1 * 32, col_bias + c1 * 32, sr, lane, n0 + c1 * 32, y0, esz,
+                    buf);
+    tmem_ld_wait(ra);
   }
 }
 
@@ -773,10 +816,12 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 constexpr int WIDE_BN = 512;
 constexpr int W_STAGES = 4;
 constexpr int W_STAGE_BYTES = A2_BYTES + 2 * B2_BYTES;  // 48 KiB
-constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + 4 * STG_WARP_BYTES /*epilogue staging*/ + 1024 /*align*/ +
-                             2 * WIDE_BN * 4 /*column tables*/ + 256;
+constexpr int W_EPI_WARPS = 8;                       // two per TMEM lane quarter, splitting the columns
+constexpr int W_THREADS = 64 + 32 * W_EPI_WARPS;     // producer warp, MMA warp, epilogue warps
+constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + W_EPI_WARPS * W_STG_BYTES /*epilogue staging*/ +
+                             1024 /*align*/ + 2 * WIDE_BN * 4 /*column tables*/ + 256;
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W_THREADS, 1)
 scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_d, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -785,8 +830,8 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   uint8_t *smem = smem_raw + (base - raw_addr);
   // stage s: [A 16 KiB | B half of block 0, 16 KiB | B half of block 1, 16 KiB]
   auto stage_a = [&](int s) { return base + (uint32_t)(s * W_STAGE_BYTES); };
-  const uint32_t stg_base = base + (uint32_t)(W_STAGES * W_STAGE_BYTES);  // 4 x 4 KiB epilogue staging
-  float *s_scale = reinterpret_cast<float *>(smem + W_STAGES * W_STAGE_BYTES + 4 * STG_WARP_BYTES);  // 512 columns
+  const uint32_t stg_base = base + (uint32_t)(W_STAGES * W_STAGE_BYTES);  // W_EPI_WARPS x 2 KiB epilogue staging
+  float *s_scale = reinterpret_cast<float *>(smem + W_STAGES * W_STAGE_BYTES + W_EPI_WARPS * W_STG_BYTES);
   float *s_bias = s_scale + WIDE_BN;
   uint64_t *bars = reinterpret_cast<uint64_t *>(s_bias + WIDE_BN);
   const uint32_t bar_base = smem_u32(bars);
@@ -808,8 +853,8 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       mbar_init(empty_bar(s), 1);  // one multicast commit per use
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty_bar(0), 8);  // four epilogue warps in each CTA (leader's barriers)
-    mbar_init(tempty_bar(1), 8);
+    mbar_init(tempty_bar(0), 2 * W_EPI_WARPS);  // every epilogue warp of both CTAs (leader's barriers)
+    mbar_init(tempty_bar(1), 2 * W_EPI_WARPS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
@@ -920,11 +965,14 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       }
     }
   } else {
-    // ---------------- epilogue (both CTAs): this CTA's 128 rows x 512 columns
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows x 512 columns;
+    // warps w and w + 4 share TMEM lane quarter w % 4 and take alternate
+    // 32-column chunks
     const int quarter = warp & 3;
+    const int e = warp - 2;
+    const int sub = e >> 2;
     const int etid = threadIdx.x - 64;
-    const uint32_t stg = stg_base + (uint32_t)((warp - 2) * STG_WARP_BYTES);
-    uint32_t nstore = 0;
+    const uint32_t buf = stg_base + (uint32_t)(e * W_STG_BYTES);
     uint32_t acc_phase = 0;
     const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
     const float sb_t = p.sb_rowwise ? 0.0f : __ldg(p.sb);
@@ -932,10 +980,14 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     for (int tile = pair; tile < p.num_tiles; tile += npairs) {
       int tm, tn;
       tile_coords(p, tile, tm, tn);
-      epilogue_sync();
-      stage_columns(p, tn * WIDE_BN, sb_t, s_scale, s_bias, etid);
-      stage_columns(p, tn * WIDE_BN + PAIR_BN, sb_t, s_scale + PAIR_BN, s_bias + PAIR_BN, etid);
-      epilogue_sync();
+      wide_epilogue_sync();  // the previous tile's column tables are no longer read
+      for (int j = etid; j < WIDE_BN; j += 32 * W_EPI_WARPS) {
+        const int col = tn * WIDE_BN + j;
+        const bool in = col < p.N;
+        s_scale[j] = in ? (p.sb_rowwise ? __ldg(p.sb + col) : sb_t) : 0.0f;
+        s_bias[j] = (in && p.bias != nullptr) ? load_bias(p.bias, p.bias_dtype, col) : 0.0f;
+      }
+      wide_epilogue_sync();
       int ok = 0;
       if (lane == 0) ok = mbar_wait(tfull, acc_phase, p.timeout_ns, 4) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
@@ -946,10 +998,10 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       for (int h = 0; h < 2; h++) {  // release each half as soon as it is read
         if (p.tma_store)
           drain_accumulator_tma(p, &tmap_d, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN,
-                                quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, stg, nstore);
+                                quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, buf, sub, 2);
         else
           drain_accumulator(p, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN, quarter, lane,
-                            sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr);
+                            sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, sub, 2);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(h), 0));
@@ -1154,7 +1206,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       for (int c = 0; c < MT; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_lane + (uint32_t)c, r);
-        tmem_ld_wait();
+        tmem_ld_wait(r);
 #pragma unroll
         for (int j = 0; j < 32; j++)
           if (c + j < MT) part[(c + j) * SK_BN + nl] = __uint_as_float(r[j]);
@@ -1288,19 +1340,18 @@ int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, 
 }
 
 // Output tensor map for the TMA-store epilogue: rows x cols of esz-byte
-// elements, row stride ldd elements, 32 x 32 boxes, swizzle matching the
-// staging layout (32 * esz bytes per box row).
+// elements, row stride ldd elements, boxes of 32 rows x 64 bytes (32 bytes
+// for fp8), swizzle matching the staging layout.
 int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ldd, int esz) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ldd * esz)};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {esz == 4 ? 16u : 32u, 32u};  // 64-byte box rows (32 bytes for fp8)
   cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType dt = esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  const CUtensorMapSwizzle sw = esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                : esz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUtensorMapSwizzle sw = esz == 1 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = enc(m, dt, 2, D, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FP8B200_EINVAL, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
@@ -1320,7 +1371,7 @@ int pair_clusters(int dev, bool wide) {
   if (!c) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74, 1, 1);
-    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.blockDim = dim3(wide ? W_THREADS : THREADS, 1, 1);
     cfg.dynamicSmemBytes = wide ? W_SMEM_BYTES : SMEM2_BYTES;
     int n = 0;
     const cudaError_t e = wide ? cudaOccupancyMaxActiveClusters(&n, scaled_mm_wide_kernel, &cfg)
@@ -1515,7 +1566,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel, ma, mb, p);
   } else if (wide) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
-    scaled_mm_wide_kernel<<<2 * clusters, THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
+    scaled_mm_wide_kernel<<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
   } else if (pair) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, false));
     scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
