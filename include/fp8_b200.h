@@ -129,6 +129,21 @@ int fp8b200_silu_mul_quantize_rows_fp8(const void *gate_up, int64_t rows, int64_
                                        float *inv_scale, void *stream);
 
 /*
+ * Rotary position embedding of the q and k heads of a fused bf16 qkv
+ * projection (no counterpart in the reference; it serves the FP8 inference
+ * stack around fp8b200_scaled_mm). qkv: tokens x ld bf16, row t holds
+ * n_q_heads then n_k_heads heads of head_dim values (position = t % seq).
+ * cos_table / sin_table: seq x head_dim/2 bf16. Writes out_q (tokens x
+ * n_q_heads x head_dim) and out_k (tokens x n_k_heads x head_dim), bf16,
+ * contiguous: out[:h] = x1*cos - x2*sin, out[h:] = x2*cos + x1*sin with
+ * PyTorch's bf16 roundings (each product, then the difference / sum).
+ * head_dim a multiple of 16, ld a multiple of 8, 16-byte aligned tensors.
+ */
+int fp8b200_rope_bf16(const void *qkv, int64_t tokens, int64_t ld, int n_q_heads, int n_k_heads,
+                      int head_dim, int seq, const void *cos_table, const void *sin_table,
+                      void *out_q, void *out_k, void *stream);
+
+/*
  * Allocation-free fp8b200_quantize_fp8 (no counterpart in the reference; the
  * reference has no device memory management of its own). Same inputs,
  * outputs and results, but no amax_scratch argument: the scratch is a fixed

@@ -1208,3 +1208,89 @@ extern "C" int fp8b200_silu_mul_quantize_rows_fp8(const void *gate_up, int64_t r
   count_launch();
   return check_launch("silu_mul_quantize");
 }
+
+// ------------------------------------------------------------------ rotary embedding (bf16)
+// Rotary position embedding of the q and k heads of a fused qkv projection,
+// with the roundings of PyTorch's bf16 expression
+//   cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
+// (each product of two bf16 values is exact in float and rounded to bf16; the
+// float difference / sum of those is rounded to bf16). One thread produces 8
+// outputs of each half of one head: 16-byte loads of x1, x2, cos and sin,
+// 16-byte stores. Rows of qkv are tokens (position = token % seq); q heads come
+// first, then k heads, head_dim contiguous elements each.
+namespace fp8b200 {
+namespace {
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__global__ void __launch_bounds__(256)
+rope_kernel(const uint16_t *__restrict__ qkv, int64_t ld, int64_t tokens, int nq, int nk, int hd, int seq,
+            const uint16_t *__restrict__ cosv, const uint16_t *__restrict__ sinv, uint16_t *__restrict__ oq,
+            uint16_t *__restrict__ ok) {
+  const int half = hd / 2, groups = half / 8, heads = nq + nk;
+  const int64_t total = tokens * heads * groups;
+  for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(w % groups);
+    const int64_t th = w / groups;
+    const int h = (int)(th % heads);
+    const int64_t t = th / heads;
+    const int pos = (int)(t % seq);
+    const uint16_t *x = qkv + t * ld + (int64_t)h * hd + g * 8;
+    const uint4 a = *reinterpret_cast<const uint4 *>(x);
+    const uint4 b = *reinterpret_cast<const uint4 *>(x + half);
+    const uint4 c = __ldg(reinterpret_cast<const uint4 *>(cosv + (int64_t)pos * half + g * 8));
+    const uint4 s = __ldg(reinterpret_cast<const uint4 *>(sinv + (int64_t)pos * half + g * 8));
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    const uint32_t cw[4] = {c.x, c.y, c.z, c.w}, sw[4] = {s.x, s.y, s.z, s.w};
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float o1[2], o2[2];
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const float x1 = e ? bf16hi(aw[q]) : bf16lo(aw[q]), x2 = e ? bf16hi(bw[q]) : bf16lo(bw[q]);
+        const float cc = e ? bf16hi(cw[q]) : bf16lo(cw[q]), ss = e ? bf16hi(sw[q]) : bf16lo(sw[q]);
+        o1[e] = rbf(x1 * cc) - rbf(x2 * ss);
+        o2[e] = rbf(x2 * cc) + rbf(x1 * ss);
+      }
+      const __nv_bfloat162 p1 = __floats2bfloat162_rn(o1[0], o1[1]), p2 = __floats2bfloat162_rn(o2[0], o2[1]);
+      lo[q] = *reinterpret_cast<const uint32_t *>(&p1);
+      hi[q] = *reinterpret_cast<const uint32_t *>(&p2);
+    }
+    uint16_t *o = h < nq ? oq + (t * nq + h) * hd : ok + (t * nk + (h - nq)) * hd;
+    *reinterpret_cast<uint4 *>(o + g * 8) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4 *>(o + half + g * 8) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  }
+}
+
+}  // namespace
+}  // namespace fp8b200
+
+extern "C" int fp8b200_rope_bf16(const void *qkv, int64_t tokens, int64_t ld, int n_q_heads, int n_k_heads,
+                                 int head_dim, int seq, const void *cos_table, const void *sin_table, void *out_q,
+                                 void *out_k, void *stream) {
+  using namespace fp8b200;
+  if (tokens < 0 || n_q_heads < 0 || n_k_heads < 0 || seq <= 0)
+    return set_error(FP8B200_EINVAL, "rope: negative size or seq <= 0");
+  if (head_dim <= 0 || head_dim % 16)
+    return set_error(FP8B200_EINVAL, "rope: head_dim=%d must be a positive multiple of 16", head_dim);
+  if (ld < (int64_t)(n_q_heads + n_k_heads) * head_dim || ld % 8)
+    return set_error(FP8B200_EINVAL, "rope: row stride must cover the q and k heads and be a multiple of 8");
+  if (tokens == 0 || n_q_heads + n_k_heads == 0) return FP8B200_OK;
+  if (!qkv || !cos_table || !sin_table || (n_q_heads && !out_q) || (n_k_heads && !out_k))
+    return set_error(FP8B200_EINVAL, "rope: null pointer");
+  if (!aligned16(qkv) || !aligned16(cos_table) || !aligned16(sin_table) || (out_q && !aligned16(out_q)) ||
+      (out_k && !aligned16(out_k)))
+    return set_error(FP8B200_EINVAL, "rope: tensors must be 16-byte aligned");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  const int64_t work = tokens * (n_q_heads + n_k_heads) * (head_dim / 16);
+  const int g = (int)std::min<int64_t>((work + 255) / 256, (int64_t)current_sm_count() * 8);
+  rope_kernel<<<g, 256, 0, (cudaStream_t)stream>>>((const uint16_t *)qkv, ld, tokens, n_q_heads, n_k_heads,
+                                                   head_dim, seq, (const uint16_t *)cos_table,
+                                                   (const uint16_t *)sin_table, (uint16_t *)out_q, (uint16_t *)out_k);
+  count_launch();
+  return check_launch("rope");
+}

@@ -54,6 +54,7 @@ def _declare(L):
         "fp8b200_encode_fp4": [vp, i32, vp, i64, vp, vp],
         "fp8b200_quantize_rows_fp8": [vp, i32, i64, i64, i64, vp, i64, i32, vp, vp],
         "fp8b200_silu_mul_quantize_rows_fp8": [vp, i64, i64, i64, vp, i64, i32, vp, vp],
+        "fp8b200_rope_bf16": [vp, i64, i64, i32, i32, i32, i32, vp, vp, vp, vp, vp],
         "fp8b200_quantize_fp4": [vp, i32, vp, i64, vp, vp, vp],
         "fp8b200_scaled_mm": [vp, i32, i64, vp, i32, i64, i64, i64, i64,
                               vp, i32, vp, i32, vp, i32, vp, vp, i32, i64, vp],

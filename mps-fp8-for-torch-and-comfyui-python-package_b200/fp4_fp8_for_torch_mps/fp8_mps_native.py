@@ -193,6 +193,27 @@ def silu_mul_quantize_rows_fp8(gate_up: torch.Tensor, fp8_dtype: torch.dtype = t
     return out.view(fp8_dtype), inv
 
 
+def rope_bf16(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_q_heads: int, n_k_heads: int,
+              head_dim: int, seq: int):
+    """Rotary embedding of the q and k heads of a bf16 (tokens, ld) qkv
+    projection in one launch, bit-identical to PyTorch's bf16
+    cat([x1*cos - x2*sin, x2*cos + x1*sin], -1). cos / sin: (seq, head_dim/2)
+    bf16 (any shape with that many contiguous elements). Returns q
+    (tokens, n_q_heads, head_dim) and k (tokens, n_k_heads, head_dim)."""
+    if qkv.dtype != torch.bfloat16 or qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise RuntimeError("rope_bf16: expected a bfloat16 (tokens, ld) tensor with unit column stride")
+    cos, sin = cos.contiguous(), sin.contiguous()
+    t = qkv.shape[0]
+    q = torch.empty(t, n_q_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
+    k = torch.empty(t, n_k_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
+    ld = qkv.stride(0) if t > 1 else qkv.shape[1]
+    with torch.cuda.device(qkv.device):
+        L.check(L.lib().fp8b200_rope_bf16(qkv.data_ptr(), t, ld, n_q_heads, n_k_heads, head_dim, seq,
+                                          cos.data_ptr(), sin.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                          L.stream_of(qkv)), "rope")
+    return q, k
+
+
 def fp8_quantize(input):
     """amax-scaled e4m3 encode; returns (codes, inv_scale f32[1])
     (fp8_mps_native.py:101-120), with the scale computed on the device."""

@@ -105,8 +105,9 @@ def rowwise_operands(m: int, n: int, k: int, seed: int = 0):
 # FP8 weight-only inference stack: Llama-3-8B-shaped layers with random
 # weights. Every linear is torch._scaled_mm on e4m3 weights (per-tensor fp32
 # scale, broadcast per output column) and per-token e4m3 activations; the
-# MLP's SiLU(g) * u is fused with its per-token quantisation; norms, rotary
-# embedding and attention (SDPA) stay in bf16 PyTorch.
+# MLP's SiLU(g) * u is fused with its per-token quantisation and the rotary
+# embedding is one kernel (both bit-identical to the PyTorch expressions);
+# norms and attention (SDPA) stay in bf16 PyTorch.
 
 LLAMA = dict(hidden=4096, intermediate=14336, heads=32, kv_heads=8, head_dim=128, layers=32,
              rope_theta=500000.0, eps=1e-5)
@@ -145,7 +146,7 @@ class Fp8LlamaLayer:
         self.n2 = torch.ones(h, device=device, dtype=torch.bfloat16)
 
     gemm_events = None  # set to a list to record (start, end) CUDA events around each GEMM
-    fused = True        # SiLU(g) * u and its per-token quantisation in one kernel
+    fused = True        # one kernel each for rotary embedding and for SiLU(g) * u + per-token quantisation
 
     def linear(self, x2d, w, sw):
         return self.linear_q(*self.nat.quantize_rows_fp8(x2d), w, sw)
@@ -168,10 +169,12 @@ class Fp8LlamaLayer:
         r = F.rms_norm(x, (h,), self.n1, c["eps"])
         qkv = self.linear(r, self.w_qkv, self.s_qkv)
         q, k, v = qkv.split([h, nkv * hd, nkv * hd], dim=1)
-        q = q.view(batch, seq, nh, hd)
-        k = k.view(batch, seq, nkv, hd)
         v = v.view(batch, seq, nkv, hd)
-        q, k = _rope(q, cos, sin), _rope(k, cos, sin)
+        if self.fused:
+            q, k = self.nat.rope_bf16(qkv, cos, sin, nh, nkv, hd, seq)
+            q, k = q.view(batch, seq, nh, hd), k.view(batch, seq, nkv, hd)
+        else:
+            q, k = _rope(q.view(batch, seq, nh, hd), cos, sin), _rope(k.view(batch, seq, nkv, hd), cos, sin)
         a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                            is_causal=True, enable_gqa=True)
         a = a.transpose(1, 2).reshape(t, h)

@@ -101,3 +101,32 @@ def test_llama_mlp_fused_equals_unfused(device):
         stack.layers[0].fused = fused
         out[fused] = stack.forward(x, 1, 256)
     assert torch.equal(out[True].view(torch.int16), out[False].view(torch.int16))
+
+
+@pytest.mark.parametrize("tokens,seq,nq,nk,hd", [(1, 1, 1, 1, 16), (7, 3, 2, 1, 32), (4096, 2048, 32, 8, 128),
+                                                 (33, 33, 4, 0, 64)])
+def test_rope_matches_pytorch(nat, tokens, seq, nq, nk, hd):
+    """The rotary kernel equals PyTorch's bf16 expression bit for bit (values
+    spanning small, large and zero, plus NaN/inf planted)."""
+    from fp4_fp8_for_torch_mps import workloads as W
+    g = torch.Generator(device="cuda").manual_seed(tokens + hd)
+    ld = (nq + 2 * nk) * hd
+    qkv = (torch.randn(tokens, ld, generator=g, device="cuda") * 4).to(torch.bfloat16)
+    qkv[0, :3] = torch.tensor([0.0, float("inf"), float("nan")])
+    ang = torch.rand(seq, hd // 2, generator=g, device="cuda") * 100
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    q, k = nat.rope_bf16(qkv, cos, sin, nq, nk, hd, seq)
+    pos = torch.arange(tokens, device="cuda") % seq
+    c4, s4 = cos[pos][:, None, :], sin[pos][:, None, :]
+    ref_q = W._rope(qkv[:, :nq * hd].reshape(tokens, nq, hd), c4, s4)
+    assert torch.equal(q.view(torch.int16), ref_q.contiguous().view(torch.int16))
+    if nk:
+        ref_k = W._rope(qkv[:, nq * hd:(nq + nk) * hd].reshape(tokens, nk, hd), c4, s4)
+        assert torch.equal(k.view(torch.int16), ref_k.contiguous().view(torch.int16))
+
+
+def test_rope_rejects_bad_input(nat):
+    qkv = torch.zeros(4, 96, dtype=torch.bfloat16, device="cuda")
+    c = torch.zeros(4, 12, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="head_dim"):
+        nat.rope_bf16(qkv, c, c, 2, 2, 24, 4)
