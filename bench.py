@@ -540,6 +540,79 @@ class ScaledMMSmallM:
             f"{self.M}x{self.N}x{self.K} f32 dequantised matmul (CPU torch, {threads} threads; weights pre-dequantised)"
 
 
+class LinearFp8W:
+    """FP8-weight linear with dequant-on-load: y = x @ (w * s)^T, x bf16
+    (M, K) N(0,1), w e4m3 quantised per output channel from N(0, 0.02),
+    Llama shapes (N, K from --shape, M from --m, default 16384). Compute in
+    bf16 on the tensor cores: the roofline peak is the measured bf16 rate."""
+    name = "linear_fp8w"
+    metric = "linear_fp8w_TFLOPS"
+    unit, bound, kernels_per_step = "TFLOP/s", "tensor_bf16", 1
+    dtype = "bf16 x e4m3 (dequantised on load) -> bf16, f32 acc"
+
+    def __init__(self, rank, args):
+        from fp4_fp8_for_torch_mps import _lib as L
+        from fp4_fp8_for_torch_mps import fp8_mps_native as nat
+        from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
+        self.L, self.nat = L, nat
+        _, N, K = ROWWISE_SHAPES[args.shape]
+        M = args.m if args.m != 16 else 16384
+        g = torch.Generator().manual_seed(rank)
+        self.x_host = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        _, wq, _, sw = rowwise_operands(1, N, K, seed=rank)
+        self.w_host, self.s_host = wq, sw.reshape(-1)
+        self.M, self.N, self.K = M, N, K
+        self.profile = f"{self.name}_{M}x{N}x{K}"
+        self.x, self.w, self.s = self.x_host.cuda(), wq.cuda(), self.s_host.cuda()
+        self.out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        self.work = 2.0 * M * N * K
+        self.h2d, self.d2h = M * K * 2, M * N * 2
+        self.config = {"workload": self.name, "M": M, "N": N, "K": K, "weights": "e4m3, per-channel scale",
+                       "activations": "bf16", "out": "bf16",
+                       "l2": "x+w+y {:.0f} MiB".format((M * K * 2 + N * K + M * N * 2) / 2**20)}
+        self.stream = torch.cuda.current_stream()
+        self.lib = L.lib()
+        self.h_x = self.x_host.pin_memory()
+        self.h_out = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.d_x = torch.empty_like(self.x)
+
+    def step(self):
+        L = self.L
+        rc = self.lib.fp8b200_linear_fp8w(self.x.data_ptr(), L.BF16, self.K, self.w.data_ptr(), L.E4M3, self.K,
+                                          self.M, self.N, self.K, self.s.data_ptr(), L.SCALE_ROWWISE, None, 0,
+                                          self.out.data_ptr(), L.BF16, self.N, self.stream.cuda_stream)
+        if rc:
+            L.check(rc, "linear_fp8w")
+
+    def e2e_step(self):
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        y = torch.ops.fp8_mps.fp8_linear(self.d_x, self.w, self.s)
+        self.h_out.copy_(y, non_blocking=True)
+
+    def check(self):
+        import numpy as np
+        from oracle import oracle as O
+        rows = np.arange(0, self.M, max(1, self.M // 16))[:16]
+        xv = self.x_host[torch.from_numpy(rows)].double().numpy()
+        W = O.fp8_table_f64(O.E4M3)[self.w_host.view(torch.uint8).numpy()] * self.s_host.double().numpy()[:, None]
+        ref = xv @ W.T
+        S = np.abs(xv) @ np.abs(W).T
+        got = self.h_out[torch.from_numpy(rows)].double().numpy()
+        return bool(np.all(np.abs(got - ref) <= O.bf16_ulp(ref) + 2.0 ** -20 * S))
+
+    def cpu_run(self, reps=1):
+        """float32 matmul of a 256-row slice against the dequantised weights (CPU torch)."""
+        threads = torch.get_num_threads()
+        W = self.w_host.float() * self.s_host.reshape(-1, 1)
+        A = self.x_host[:256].float()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            (A @ W.t()).to(torch.bfloat16)
+        dt = (time.perf_counter() - t0) / reps
+        return 2.0 * 256 * self.N * self.K / dt / 1e12, threads, \
+            f"256x{self.N}x{self.K} f32 matmul, weights dequantised beforehand (CPU torch, {threads} threads)"
+
+
 class LlamaFp8:
     """32 Llama-3-8B-shaped layers, e4m3 weights, per-token e4m3 activations,
     every linear through torch._scaled_mm; batch 8 x 2048 tokens split across
@@ -641,7 +714,8 @@ def llama_cpu_tokens_per_s(layers: int, reps: int = 1, seq: int = 256):
 
 WORKLOADS = {"fp4_decode": Fp4Decode, "fp8_roundtrip": Fp8RoundTrip, "llama_fp8": LlamaFp8,
              "scaled_mm": lambda r, a: ScaledMM(r, a, False),
-             "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True), "scaled_mm_small_m": ScaledMMSmallM}
+             "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True), "scaled_mm_small_m": ScaledMMSmallM,
+             "linear_fp8w": LinearFp8W}
 
 
 # ---------------------------------------------------------------- reference arm
@@ -659,6 +733,18 @@ def reference_line(args):
         vals = [Fp8RoundTrip.cpu_run(rows=4096, reps=1) for _ in range(max(args.steps, 1))]
         unit, metric = "GB/s", "fp8_roundtrip_GBps"
         config = {"workload": "fp8_roundtrip", "shape": [4096, 4096], "fp8": "e4m3fn"}
+    elif args.workload == "linear_fp8w":
+        w = LinearFp8W.__new__(LinearFp8W)
+        from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
+        _, N, K = ROWWISE_SHAPES[args.shape]
+        M = args.m if args.m != 16 else 16384
+        w.x_host = torch.randn(256, K, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+        _, w.w_host, _, sw = rowwise_operands(1, N, K)
+        w.s_host = sw.reshape(-1)
+        w.N, w.K = N, K
+        vals = [w.cpu_run() for _ in range(max(args.steps, 1))]
+        unit, metric = "TFLOP/s", "linear_fp8w_TFLOPS"
+        config = {"workload": args.workload, "M": M, "N": N, "K": K, "out": "bf16"}
     elif args.workload == "scaled_mm_small_m":
         w = ScaledMMSmallM.__new__(ScaledMMSmallM)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
@@ -761,6 +847,8 @@ def main():
                  "gemm_share": round(gemm_ms / (ms / args.steps), 4)}
     if w.bound == "hbm":
         peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
+    elif w.bound == "tensor_bf16":
+        peak, punit, psrc = pk["bf16_tflops"], "TFLOP/s", f"{pk_kind} bf16_tflops"
     else:
         peak, punit = 2.0 * pk["bf16_tflops"], "TFLOP/s"
         psrc = f"2 x {pk_kind} bf16_tflops (dense fp8 issue rate is twice bf16 on tcgen05)"
@@ -782,7 +870,7 @@ def main():
         "config": dict(w.config, parallelism=f"replicas{ws}" if ws > 1 else "single"),
         "e2e": {"value": round(e2e_value, 3), "unit": w.unit, "h2d_bytes_per_step": int(w.h2d),
                 "d2h_bytes_per_step": int(w.d2h)},
-        "roofline": {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
+        "roofline": {"bound": "tensor" if w.bound == "tensor_bf16" else w.bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
                      "frac": round(achieved / peak, 4), "peak_source": psrc,
                      "traffic": profile_traffic(w.profile), **extra},
         "cpu_baseline": cpu,

@@ -209,6 +209,25 @@ int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda,
                       void *stream);
 
 /*
+ * Linear layer with float8 weights dequantised on load:
+ * D = x @ (w * w_scale)^T [+ bias] -> out_dtype (F32/BF16/F16).
+ * x: M x K bf16 or f16 activations, row stride ldx elements (multiple of 8);
+ * w: N x K float8 weight codes, row stride ldw bytes (multiple of 16); x and w
+ * 16-byte aligned. w_scale: one float (FP8B200_SCALE_TENSOR) or N floats, one
+ * per output channel (FP8B200_SCALE_ROWWISE); bias: N values or NULL.
+ * The weights are converted to x's type inside shared memory (exact) and the
+ * products are accumulated in float32 on the tensor cores (kind::f16); the
+ * scale and bias are applied to the float32 sums.
+ * Replaces the reference's dequantise-then-matmul path: fp8_scaled_mm_fast
+ * (fp8_mps_native.py:129-159), which decodes both operands to f16 and calls
+ * an MPS f16 matmul, for the case where only the weights are float8.
+ */
+int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, const void *w, int w_dtype, int64_t ldw,
+                        int64_t M, int64_t N, int64_t K, const float *w_scale, int w_scale_layout,
+                        const void *bias, int bias_dtype, void *D, int out_dtype, int64_t ldd,
+                        void *stream);
+
+/*
  * Device-side status of the scaled GEMM on the current device: 0 if no
  * bounded wait has timed out, else FP8B200_ETIMEOUT with *status_out holding
  * the site code. Synchronises the device. `reset` clears the word.

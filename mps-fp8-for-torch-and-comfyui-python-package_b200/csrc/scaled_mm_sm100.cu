@@ -66,6 +66,8 @@ struct Params {
   int debug_skip_first_load;
   int sk_mt, sk_stages, sk_cs, sk_tmem_cols;  // small-M kernel: rows per tile, ring depth, split-K cluster, TMEM
   int tma_store;                              // epilogue stores through the output tensor map
+  int w_fp8;                                  // fp8-weight linear: weight format (FP8B200_E4M3 / E5M2)
+  int act_f16;                                // fp8-weight linear: activations f16 (1) or bf16 (0)
 };
 
 // Status word: 0 = ok, otherwise (1 << 31) | site of the first wait that timed out.
@@ -1275,6 +1277,337 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
   }
 }
 
+// ------------------------------------------------------------------ fp8-weight linear (dequant on load)
+// D[M,N] = x[M,K] @ (w[N,K] * w_scale)^T [+ bias] for bf16 or f16 activations x
+// and float8 weights w that are never materialised in a wider type in HBM.
+// A cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2.kind::f16 (M=256, N=256, K=16): each CTA holds its
+// 128 rows of x and converts its 128 of the tile's 256 weight rows, so every
+// SM reads only half of the B operand from shared memory (16-bit operands at
+// the single-CTA shape would need more shared-memory bandwidth than the SM
+// has once the converted tile is also written there). Per CTA, a 6-slot ring
+// holds each k-block's x tile (128 rows x 64 values, 128-byte swizzle; TMA,
+// completing on the leader's barrier) and raw weight half tile (128 rows x 64
+// bytes, 64-byte swizzle; TMA, completing on this CTA's barrier); four groups
+// of two converter warps (two weight rows per thread, k-blocks in turn)
+// convert the raw rows to the
+// activation type (exact, fp8x2_fast), write the 128-byte-swizzled K-major
+// half tile into a 4-slot ring, fence it to the async proxy and arrive on the
+// leader's `converted` barrier. (The weights come in through TMA, not loads
+// into registers: the release of that arrival would otherwise wait for every
+// load the thread still has in flight.) The
+// leader's MMA thread commits each slot back to both CTAs. The weight scale
+// (per tensor or per output channel) and the bias are applied to the fp32
+// accumulator in the epilogue, so the weight values enter the products
+// exactly. Warps: 0 TMA producer, 1 MMA issuer (leader), 2-5 epilogue,
+// 6-13 converters.
+constexpr int LW_BK = 64;                          // elements per k-block (128 bytes of 16-bit x)
+constexpr int LW_LOADS = 6;                        // x + raw weight ring
+constexpr int LW_CONVS = 4;                        // converted-weight ring
+constexpr int LW_A_BYTES = BM * LW_BK * 2;         // 16 KiB of x (128 rows)
+constexpr int LW_RAW_BYTES = HALF_B * LW_BK;       // 8 KiB of fp8 weights (128 rows)
+constexpr int LW_LOAD_BYTES = LW_A_BYTES + LW_RAW_BYTES;
+constexpr int LW_W_BYTES = HALF_B * LW_BK * 2;     // 16 KiB of converted weights (128 rows)
+constexpr int LW_CONV_WARPS = 8;                   // converter warps
+constexpr int LW_GROUPS = 4;                       // converter groups taking k-blocks in turn
+constexpr int LW_GROUP_THREADS = 32 * LW_CONV_WARPS / LW_GROUPS;
+constexpr int LW_THREADS = 192 + 32 * LW_CONV_WARPS;
+constexpr int LW_SMEM_BYTES = LW_LOADS * LW_LOAD_BYTES + LW_CONVS * LW_W_BYTES + 1024 /*align*/ +
+                              2 * PAIR_BN * 4 /*column tables*/ + 256;
+
+// Two fp8 codes (low byte = first element) -> two f16 values (low half first).
+template <int WF>
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
+  uint32_t h;
+  const uint16_t in = (uint16_t)two;
+  if constexpr (WF == FP8B200_E4M3) asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(in));
+  else asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h) : "h"(in));
+  return h;
+}
+// f16x2 -> bf16x2 for values with at most 3 significant mantissa bits (exact).
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
+  const __nv_bfloat162 b = __floats2bfloat162_rn(__half2float(__ushort_as_half((uint16_t)(h & 0xFFFFu))),
+                                                 __half2float(__ushort_as_half((uint16_t)(h >> 16))));
+  return *reinterpret_cast<const uint32_t *>(&b);
+}
+
+// Fast exact fp8 -> 16-bit conversion of two codes (bytes `sel` of w) without
+// conversion instructions: the code's exponent and mantissa bits are placed
+// where the target format's sit, the sign at bit 15, and the pair is scaled
+// by a power of two (the difference of the exponent biases) with one packed
+// multiply, which is exact for normal and subnormal codes alike. Codes with
+// an all-ones exponent (NaN for e4m3; inf / NaN for e5m2 into bf16) must not
+// come here (see fp8_unit_special); e5m2 -> f16 is a byte placement.
+template <int WF, bool TO_F16>
+__device__ __forceinline__ uint32_t fp8x2_fast(uint32_t w, uint32_t sel_lowbytes, uint32_t sel_highbytes) {
+  uint32_t x, r;
+  if constexpr (WF == FP8B200_E5M2 && TO_F16) {
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(x) : "r"(w), "r"(sel_highbytes));  // code -> high byte of each half
+    return x;
+  } else {
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(x) : "r"(w), "r"(sel_lowbytes));   // code -> low byte of each half
+    constexpr int SH = WF == FP8B200_E4M3 ? (TO_F16 ? 7 : 4) : 5;           // exponent-mantissa position
+    constexpr uint32_t EM = (WF == FP8B200_E4M3 ? 0x7Fu : 0x7Fu) << SH;
+    constexpr uint32_t MASK = EM | (EM << 16);
+    const uint32_t bits = ((x << SH) & MASK) | ((x << 8) & 0x80008000u);
+    // 2^(bias difference): e4m3 -> bf16 2^120, e4m3 -> f16 2^8, e5m2 -> bf16 2^112
+    constexpr uint32_t SCALE = WF == FP8B200_E4M3 ? (TO_F16 ? 0x5C005C00u : 0x7B807B80u) : 0x77807780u;
+    if constexpr (TO_F16) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(SCALE));
+    else asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(SCALE));
+    return r;
+  }
+}
+
+// Nonzero if any of the 16 codes in q needs the exact path.
+template <int WF, bool TO_F16>
+__device__ __forceinline__ uint32_t fp8_unit_special(const uint32_t (&q)[4]) {
+  if constexpr (WF == FP8B200_E5M2 && TO_F16) return 0u;
+  uint32_t any = 0;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    if constexpr (WF == FP8B200_E4M3) any |= ((q[i] & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;  // 0x7F / 0xFF
+    else any |= ((q[i] & 0x7C7C7C7Cu) + 0x04040404u) & 0x80808080u;                              // exponent 31
+  }
+  return any;
+}
+
+// Convert row r of a raw weight half tile (64 bytes, 64-byte swizzle: unit c
+// at c ^ ((r >> 1) & 3)) into row r of the MMA half tile (64 16-bit values =
+// 128 bytes, 128-byte swizzle: unit j at j ^ (r & 7)). Both swizzles put the
+// 8 rows a quarter-warp touches in distinct 16-byte bank groups.
+template <int WF, bool TO_F16>
+__device__ __forceinline__ void convert_weight_row(uint32_t raw, uint32_t dst, int r) {
+  uint32_t q[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; c++)  // all four 16-byte units of the row in flight at once
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(q[c][0]), "=r"(q[c][1]), "=r"(q[c][2]), "=r"(q[c][3])
+                 : "r"(raw + (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) * 16))));
+  uint32_t o[4][8];
+  const bool special = (fp8_unit_special<WF, TO_F16>(q[0]) | fp8_unit_special<WF, TO_F16>(q[1]) |
+                        fp8_unit_special<WF, TO_F16>(q[2]) | fp8_unit_special<WF, TO_F16>(q[3])) != 0u;
+  if (!special) {
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        o[c][2 * i] = fp8x2_fast<WF, TO_F16>(q[c][i], 0x4140u, 0x1404u);
+        o[c][2 * i + 1] = fp8x2_fast<WF, TO_F16>(q[c][i], 0x4342u, 0x3424u);
+      }
+  } else {  // NaN / inf present: conversion instructions
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t lo = fp8x2_to_f16x2<WF>(q[c][i] & 0xFFFFu), hi = fp8x2_to_f16x2<WF>(q[c][i] >> 16);
+        o[c][2 * i] = TO_F16 ? lo : f16x2_to_bf16x2(lo);
+        o[c][2 * i + 1] = TO_F16 ? hi : f16x2_to_bf16x2(hi);
+      }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j++)  // output unit j = codes 8j .. 8j+7
+    st_shared_v4(dst + (uint32_t)(r * 128 + ((j ^ (r & 7)) * 16)), o[j >> 1][4 * (j & 1)],
+                 o[j >> 1][4 * (j & 1) + 1], o[j >> 1][4 * (j & 1) + 2], o[j >> 1][4 * (j & 1) + 3]);
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LW_THREADS, 1)
+linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                   const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  // load slot s: [x 16 KiB | raw weights 8 KiB]; then the converted-weight slots (16 KiB); same offsets in both CTAs
+  auto sx = [&](int s) { return base + (uint32_t)(s * LW_LOAD_BYTES); };
+  auto sraw = [&](int s) { return sx(s) + (uint32_t)LW_A_BYTES; };
+  auto sw = [&](int c) { return base + (uint32_t)(LW_LOADS * LW_LOAD_BYTES + c * LW_W_BYTES); };
+  float *s_scale = reinterpret_cast<float *>(smem + LW_LOADS * LW_LOAD_BYTES + LW_CONVS * LW_W_BYTES);
+  float *s_bias = s_scale + PAIR_BN;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s_bias + PAIR_BN);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };                                // x of both CTAs (leader)
+  auto empty_bar = [&](int s) { return bar_base + 8u * (LW_LOADS + s); };                  // x slot read
+  auto conv_bar = [&](int c) { return bar_base + 8u * (2 * LW_LOADS + c); };               // both halves converted (leader)
+  auto cempty_bar = [&](int c) { return bar_base + 8u * (2 * LW_LOADS + LW_CONVS + c); };  // converted slot read
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * LW_LOADS + 2 * LW_CONVS + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * LW_LOADS + 2 * LW_CONVS + 2 + b); };
+  auto rfull_bar = [&](int s) { return bar_base + 8u * (2 * LW_LOADS + 2 * LW_CONVS + 4 + s); };  // raw weights (own)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * LW_LOADS + 2 * LW_CONVS + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = (int)cluster_id_x();
+  const int npairs = (int)num_clusters_x();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < LW_LOADS; s++) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+      mbar_init(rfull_bar(s), 1);
+    }
+    for (int c = 0; c < LW_CONVS; c++) {
+      mbar_init(conv_bar(c), 2 * LW_CONV_WARPS / LW_GROUPS);  // the warps of one group in each CTA
+      mbar_init(cempty_bar(c), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 8);  // four epilogue warps in each CTA
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs): this CTA's 128 rows of x
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        const int xrow = tm * (2 * BM) + (int)rank * BM;
+        const int wrow = tn * PAIR_BN + (int)rank * HALF_B;
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (p.debug_skip_first_load) { ok = false; break; }
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * LW_A_BYTES);
+          tma_load_2d_pair(sx(stage), &tmap_x, leader_full, kb * LW_BK, xrow);
+          mbar_expect_tx(rfull_bar(stage), LW_RAW_BYTES);
+          tma_load_2d(sraw(stage), &tmap_w, rfull_bar(stage), kb * LW_BK, wrow);
+          if (++stage == LW_LOADS) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only)
+    if (rank == 0 && lane == 0) {
+      int stage = 0, cs = 0;
+      uint32_t phase = 0, cphase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * PAIR_BN);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          if (!mbar_wait(conv_bar(cs), cphase, p.timeout_ns, 7)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128_kmajor(sx(stage));
+          const uint64_t bdesc = sdesc_sw128_kmajor(sw(cs));
+#pragma unroll
+          for (int k = 0; k < LW_BK / 16; k++)  // K = 16 per MMA: +32 bytes along the swizzled row
+            umma_f16_pair(d_tmem, adesc + (uint64_t)((k * 32) >> 4), bdesc + (uint64_t)((k * 32) >> 4), p.idesc,
+                          (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(empty_bar(stage));  // x slot free in both CTAs
+          umma_commit_pair(cempty_bar(cs));    // converted slot free in both CTAs
+          if (++stage == LW_LOADS) { stage = 0; phase ^= 1u; }
+          if (++cs == LW_CONVS) { cs = 0; cphase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------- weight converters (both CTAs): LW_GROUPS groups take
+    // k-blocks in turn, so that several k-blocks' conversions and their
+    // fence + arrival latencies overlap; within a group each thread converts
+    // rows ctid, ctid + LW_GROUP_THREADS, ... Slots and phases follow a running
+    // k-block counter.
+    const int group = (threadIdx.x - 192) / LW_GROUP_THREADS;
+    const int ctid = threadIdx.x - 192 - group * LW_GROUP_THREADS;
+    const uint32_t leader_conv0 = map_to_rank(conv_bar(0), 0);
+    uint32_t it = 0;  // k-blocks seen so far (both groups count all of them)
+    bool ok = true;
+    for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
+      for (int kb = 0; kb < p.num_kb; kb++, it++) {
+        if ((int)(it % LW_GROUPS) != group) continue;
+        const int stage = (int)(it % LW_LOADS), cs = (int)(it % LW_CONVS);
+        const uint32_t phase = (it / LW_LOADS) & 1u, cphase = (it / LW_CONVS) & 1u;
+        int got = 0;
+        if (lane == 0)
+          got = mbar_wait(rfull_bar(stage), phase, p.timeout_ns, 5) && mbar_wait(cempty_bar(cs), cphase ^ 1u, p.timeout_ns, 6)
+                    ? 1 : 0;
+        got = __shfl_sync(0xFFFFFFFFu, got, 0);
+        if (!got) { ok = false; break; }
+#pragma unroll
+        for (int r = ctid; r < HALF_B; r += LW_GROUP_THREADS) {
+          if (p.act_f16) {
+            if (p.w_fp8 == FP8B200_E4M3) convert_weight_row<FP8B200_E4M3, true>(sraw(stage), sw(cs), r);
+            else convert_weight_row<FP8B200_E5M2, true>(sraw(stage), sw(cs), r);
+          } else {
+            if (p.w_fp8 == FP8B200_E4M3) convert_weight_row<FP8B200_E4M3, false>(sraw(stage), sw(cs), r);
+            else convert_weight_row<FP8B200_E5M2, false>(sraw(stage), sw(cs), r);
+          }
+        }
+        fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_conv0 + 8u * (uint32_t)cs);
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of the pair tile
+    const int quarter = warp & 3;
+    const int etid = threadIdx.x - 64;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const float sb_t = p.sb_rowwise ? 0.0f : __ldg(p.sb);
+    const float sr = p.scale_result ? __ldg(p.scale_result) : 1.0f;
+    for (int tile = pair; tile < p.num_tiles; tile += npairs) {
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      epilogue_sync();
+      stage_columns(p, tn * PAIR_BN, sb_t, s_scale, s_bias, etid);
+      epilogue_sync();
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      drain_accumulator(p, tmem_base + (uint32_t)(acc * PAIR_BN), tm * (2 * BM) + (int)rank * BM, tn * PAIR_BN,
+                        quarter, lane, 1.0f, s_scale, s_bias, sr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still touch its shared memory
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -1601,4 +1934,86 @@ extern "C" int fp8b200_gemm_set_path(int path) {
   if (path < 0 || path > 4) return set_error(FP8B200_EINVAL, "gemm path must be 0 (auto), 1, 2, 3 or 4");
   g_path = path;
   return FP8B200_OK;
+}
+
+namespace fp8b200 {
+namespace gemm {
+// 2-D tensor map of `outer` rows x `inner` elements (row pitch ld_bytes) with
+// the given box and swizzle; no caching (used by the fp8-weight linear).
+int make_map_2d(CUtensorMap *m, const void *ptr, CUtensorMapDataType dt, int64_t inner, int64_t outer,
+                int64_t ld_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FP8B200_EINVAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FP8B200_OK;
+}
+}  // namespace gemm
+}  // namespace fp8b200
+
+extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, const void *w, int w_dtype, int64_t ldw,
+                                   int64_t M, int64_t N, int64_t K, const float *w_scale, int w_scale_layout,
+                                   const void *bias, int bias_dtype, void *D, int out_dtype, int64_t ldd,
+                                   void *stream) {
+  if (x_dtype != FP8B200_BF16 && x_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: activations must be bf16 or f16");
+  if (w_dtype != FP8B200_E4M3 && w_dtype != FP8B200_E5M2)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: weights must be e4m3fn or e5m2");
+  if (out_dtype != FP8B200_F32 && out_dtype != FP8B200_BF16 && out_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: output must be f32, bf16 or f16");
+  if (M < 0 || N < 0 || K < 0) return set_error(FP8B200_EINVAL, "linear_fp8w: negative size");
+  if (M == 0 || N == 0) return FP8B200_OK;
+  if (K == 0) return set_error(FP8B200_EINVAL, "linear_fp8w: K must be positive");
+  if (M > 0x7FFFFFFFLL || N > 0x7FFFFFFFLL || K > 0x7FFFFFFFLL)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: dimension too large");
+  if (ldx < K || ldw < K || ldx % 8 || ldw % 16)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: row strides must be >= K and 16-byte multiples");
+  if (ldd < N) return set_error(FP8B200_EINVAL, "linear_fp8w: output row stride < N");
+  if (!x || !w || !D || !w_scale) return set_error(FP8B200_EINVAL, "linear_fp8w: null pointer");
+  if (!aligned16(x) || !aligned16(w)) return set_error(FP8B200_EINVAL, "linear_fp8w: x and w must be 16-byte aligned");
+  if (w_scale_layout != FP8B200_SCALE_TENSOR && w_scale_layout != FP8B200_SCALE_ROWWISE)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: unknown weight-scale layout");
+  if (bias && bias_dtype != FP8B200_F32 && bias_dtype != FP8B200_BF16 && bias_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "linear_fp8w: bias must be f32/bf16/f16");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  static bool attr_done[64] = {};
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(linear_fp8w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LW_SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  CUtensorMap mx, mw;
+  if (int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, M, ldx * 2, LW_BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, LW_BK, HALF_B, CU_TENSOR_MAP_SWIZZLE_64B))
+    return rc;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.num_kb = (int)((K + LW_BK - 1) / LW_BK);
+  p.tiles_m = (int)((M + 2 * BM - 1) / (2 * BM));
+  p.tiles_n = (int)((N + PAIR_BN - 1) / PAIR_BN);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.sa = nullptr; p.sa_rowwise = 0;
+  p.sb = w_scale; p.sb_rowwise = w_scale_layout == FP8B200_SCALE_ROWWISE;
+  p.bias = bias; p.bias_dtype = bias_dtype;
+  p.scale_result = nullptr;
+  p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
+  p.vec_store = aligned16(D) && ((ldd * dtype_size(out_dtype)) % 16 == 0);
+  p.w_fp8 = w_dtype;
+  p.act_f16 = x_dtype == FP8B200_F16;
+  const uint32_t fmt = p.act_f16 ? 0u : 1u;  // kind::f16 operand type: 0 = f16, 1 = bf16
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(PAIR_BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+  p.timeout_ns = g_timeout_ns;
+  p.debug_skip_first_load = g_debug_skip_first_load;
+  const int clusters = std::min(p.num_tiles, current_sm_count() / 2);
+  linear_fp8w_kernel<<<2 * clusters, LW_THREADS, LW_SMEM_BYTES, (cudaStream_t)stream>>>(mx, mw, p);
+  count_launch();
+  return check_launch("linear_fp8w");
 }

@@ -294,6 +294,58 @@ def fp4_quantize(input):
 
 
 # ----------------------------------------------------------------- scaled GEMM
+def fp8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+               bias: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """y = x @ (weight * weight_scale)^T [+ bias] with float8 weights that are
+    dequantised on load inside the GEMM (never written out in a wider type):
+    the reference's dequantise-then-matmul path (fp8_mps_native.py:129-159)
+    for float8 weights and bf16/f16 activations. x: (..., K) bf16 or f16;
+    weight: (N, K) float8_e4m3fn / float8_e5m2 (rows contiguous along K);
+    weight_scale: 1 value or N values (one per output channel); bias: N values.
+    Returns (..., N) in out_dtype (default x.dtype)."""
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(f"fp8_linear: activations must be bfloat16 or float16, got {x.dtype}")
+    if weight.dtype not in _FP8 or weight.dim() != 2:
+        raise RuntimeError("fp8_linear: weight must be a 2-D float8_e4m3fn / float8_e5m2 tensor")
+    N, K = weight.shape
+    if x.shape[-1] != K:
+        raise RuntimeError(f"fp8_linear: x has {x.shape[-1]} features, weight expects {K}")
+    dev = x.device
+    if weight.device != dev:
+        raise RuntimeError("fp8_linear: x and weight on different devices")
+    odt = out_dtype or x.dtype
+    if odt not in (torch.float32, torch.bfloat16, torch.float16):
+        raise RuntimeError(f"fp8_linear: unsupported output dtype {odt}")
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+        if K % 8:  # row starts must stay 16-byte aligned: pad the row pitch
+            xp = torch.zeros(x2.shape[0], (K + 7) // 8 * 8, dtype=x.dtype, device=dev)
+            xp[:, :K] = x2
+            x2 = xp
+    w = weight
+    if w.stride(1) != 1 or w.stride(0) % 16 or w.data_ptr() % 16:
+        wp = torch.zeros(N, (K + 15) // 16 * 16, dtype=torch.uint8, device=dev)
+        wp[:, :K] = weight.view(torch.uint8)
+        w = wp.view(weight.dtype)
+    ws = weight_scale.to(device=dev, dtype=torch.float32).contiguous()
+    if ws.numel() not in (1, N):
+        raise RuntimeError(f"fp8_linear: weight_scale has {ws.numel()} values, expected 1 or {N}")
+    if bias is not None:
+        bias = bias.to(dev).contiguous()
+        if bias.numel() != N or bias.dtype not in _FLOAT:
+            raise RuntimeError("fp8_linear: bias must hold N float values")
+    M = x2.shape[0]
+    out = torch.empty((M, N), dtype=odt, device=dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().fp8b200_linear_fp8w(
+            x2.data_ptr(), L.dtype_code(x.dtype), x2.stride(0), w.data_ptr(), L.dtype_code(weight.dtype), w.stride(0),
+            M, N, K, ws.data_ptr(), L.SCALE_TENSOR if ws.numel() == 1 else L.SCALE_ROWWISE,
+            None if bias is None else bias.data_ptr(), 0 if bias is None else L.dtype_code(bias.dtype),
+            out.data_ptr(), L.dtype_code(odt), N, L.stream_of(x2)), "fp8_linear")
+    return out.reshape(*x.shape[:-1], N)
+
+
 def scaled_mm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
               bias: torch.Tensor | None = None, scale_result: torch.Tensor | None = None,
               out_dtype: torch.dtype = torch.bfloat16,

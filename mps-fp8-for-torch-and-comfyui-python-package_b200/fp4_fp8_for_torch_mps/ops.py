@@ -26,6 +26,8 @@ from __future__ import annotations
 import os
 import warnings
 
+from typing import Optional
+
 import torch
 import torch.library
 
@@ -450,6 +452,20 @@ def fp4_quantize(input: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 @fp4_quantize.register_fake
 def _(input):
     return (input.new_empty(input.numel() // 2, dtype=torch.uint8), input.new_empty((1,), dtype=torch.float32))
+
+
+@torch.library.custom_op("fp8_mps::fp8_linear", mutates_args=())
+def fp8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+               bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x @ (weight * weight_scale)^T [+ bias], float8 weights dequantised on
+    load (an addition to the reference's seven ops)."""
+    from fp4_fp8_for_torch_mps.fp8_mps_native import fp8_linear as _linear
+    return _linear(x, weight, weight_scale, bias)
+
+
+@fp8_linear.register_fake
+def _(x, weight, weight_scale, bias=None):
+    return x.new_empty(tuple(x.shape[:-1]) + (weight.shape[0],))
 
 
 @torch.library.custom_op("fp8_mps::fp4_dequantize", mutates_args=())

@@ -86,6 +86,9 @@ def test_fake_impls_match_reference_schemas():
         p, sc2 = torch.ops.fp8_mps.fp4_quantize(x)
         assert p.shape == (12,) and sc2.shape == (1,)
         assert torch.ops.fp8_mps.fp4_dequantize(p, sc2).shape == (24,)
+        xb = torch.empty(2, 3, 32, dtype=torch.bfloat16)
+        w8 = torch.empty(16, 32, dtype=torch.float8_e4m3fn)
+        assert torch.ops.fp8_mps.fp8_linear(xb, w8, s).shape == (2, 3, 16)   # addition to the seven
 
 
 def test_no_aten_overrides_without_cuda():

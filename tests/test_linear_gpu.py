@@ -1,0 +1,138 @@
+"""Device parity of the float8-weight linear with dequant-on-load
+(fp8b200_linear_fp8w, fp8_mps::fp8_linear) against a float64 reference
+x @ (decode(w) * s)^T + bias.
+
+Tolerance (the GEMM tests' bound): |out - r| <= ulp_out(|r|) + 2^-20 * S with
+S = sum_k |x_k| |w_k s| (+ |bias| 2^-4 when a bias is added): one output ulp
+plus the float32 accumulation bound. The products x_k * w_k are exact (the
+weights enter the tensor cores unrounded), so this is the same bar as the
+fp8 x fp8 GEMM.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+E4, E5 = torch.float8_e4m3fn, torch.float8_e5m2
+FMT = {E4: O.E4M3, E5: O.E5M2}
+ACC_TOL = 2.0 ** -20
+
+
+@pytest.fixture(scope="module")
+def nat(device):
+    from fp4_fp8_for_torch_mps import fp8_mps_native
+    return fp8_mps_native
+
+
+def ulp(x, dtype):
+    mant = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}[dtype]
+    ax = np.maximum(np.abs(x), 2.0 ** -126)
+    u = 2.0 ** (np.floor(np.log2(ax)) - mant)
+    if dtype == torch.float16:
+        u = np.maximum(u, 2.0 ** -24)
+    return u
+
+
+def reference(x, w, scale, bias=None):
+    xv = x.float().cpu().double().numpy()
+    wv = O.fp8_table_f64(FMT[w.dtype])[w.view(torch.uint8).cpu().numpy()]
+    sv = scale.float().cpu().double().numpy().reshape(1, -1)
+    W = wv * sv.reshape(-1, 1) if sv.size > 1 else wv * sv.item()
+    r = xv @ W.T
+    S = np.abs(xv) @ np.abs(W).T
+    if bias is not None:
+        bv = bias.float().cpu().double().numpy().reshape(1, -1)
+        r = r + bv
+        S = S + np.abs(bv) * 2.0 ** -4
+    return r, S
+
+
+def check(out, r, S, what):
+    o = out.float().cpu().double().numpy()
+    tol = ulp(r, out.dtype) + ACC_TOL * S
+    bad = np.abs(o - r) > tol
+    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} outside tolerance"
+
+
+def rand_w(shape, dtype, gen):
+    w = (torch.randn(*shape, generator=gen) * 30).clamp(-400, 400).to(dtype)
+    return w
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (17, 300, 200), (128, 256, 64), (129, 512, 72),
+                                   (300, 528, 1040), (1000, 1008, 2000), (64, 4096, 4096)])
+def test_shapes(nat, M, N, K):
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = rand_w((N, K), E4, g)
+    s = torch.tensor(0.0123)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    assert out.shape == (M, N) and out.dtype == torch.bfloat16
+    r, S = reference(x, w, s)
+    check(out, r, S, f"{M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("wdt", [E4, E5])
+@pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("bias_dt", [None, torch.float32, torch.bfloat16])
+def test_dtypes_scales_bias(nat, xdt, wdt, odt, bias_dt):
+    M, N, K = 200, 320, 384
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(M, K, generator=g) * 2).to(xdt)
+    w = rand_w((N, K), wdt, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3          # per output channel
+    bias = None if bias_dt is None else (torch.randn(N, generator=g) * 5).to(bias_dt)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda(), None if bias is None else bias.cuda(), out_dtype=odt)
+    assert out.dtype == odt
+    r, S = reference(x, w, s, bias)
+    check(out, r, S, f"{xdt} {wdt} {odt} bias={bias_dt}")
+
+
+@pytest.mark.parametrize("wdt", [E4, E5])
+def test_every_finite_weight_code(nat, wdt):
+    """Each of the finite codes appears in every column position of K: the
+    conversion inside shared memory is exact for all of them (a one-hot x
+    row picks out single weight values)."""
+    codes = torch.arange(256, dtype=torch.uint8)
+    vals = codes.view(wdt).float()
+    finite = codes[torch.isfinite(vals)]
+    K = 128
+    w = finite.repeat(256 * K // finite.numel() + 1)[: 256 * K].reshape(256, K).view(wdt)
+    x = torch.eye(K, dtype=torch.bfloat16)                 # row i selects column i of every weight row
+    out = nat.fp8_linear(x.cuda(), w.cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32)
+    want = w.float().T                                     # (K, 256): exact values
+    assert torch.equal(out.cpu(), want)
+
+
+def test_nan_weight_propagates(nat):
+    x = torch.ones(4, 64, dtype=torch.bfloat16)
+    w = torch.zeros(256, 64, dtype=torch.uint8)
+    w[3, 5] = 0x7F                                          # e4m3 NaN
+    out = nat.fp8_linear(x.cuda(), w.view(E4).cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32).cpu()
+    assert torch.isnan(out[:, 3]).all() and not torch.isnan(out[:, [0, 1, 2, 4]]).any()
+
+
+def test_leading_dims_custom_op_and_unaligned(nat):
+    """(..., K) activations, the fp8_mps::fp8_linear op, and K not a multiple
+    of 8 (the launcher pads the row pitch)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 5, 100, generator=g).to(torch.bfloat16)
+    w = rand_w((64, 100), E4, g)
+    s = torch.tensor(0.02)
+    out = torch.ops.fp8_mps.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    assert out.shape == (2, 5, 64)
+    r, S = reference(x.reshape(-1, 100), w, s)
+    check(out.reshape(-1, 64), r, S, "leading dims")
+
+
+def test_rejects_bad_input(nat):
+    x = torch.zeros(4, 32, device="cuda")
+    w = torch.zeros(8, 32, dtype=E4, device="cuda")
+    with pytest.raises(RuntimeError, match="bfloat16 or float16"):
+        nat.fp8_linear(x, w, torch.tensor(1.0))
+    with pytest.raises(RuntimeError, match="weight_scale"):
+        nat.fp8_linear(x.bfloat16(), w, torch.ones(3))
