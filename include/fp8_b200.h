@@ -228,6 +228,21 @@ int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, const void *w, 
                         void *stream);
 
 /*
+ * 16-bit GEMM: D = A @ B^T * scale_b [+ bias] -> out_dtype (F32/BF16/F16),
+ * A: M x K and B: N x K of the same type (FP8B200_BF16 or FP8B200_F16), row
+ * strides lda / ldb elements (multiples of 8), 16-byte aligned; scale_b one
+ * float or N floats (per output column); D 16-byte aligned rows.
+ * The CTA-pair 256x512 tcgen05 kernel of fp8b200_scaled_mm with kind::f16
+ * MMAs. It serves the large-M path of the float8-weight linear (weights
+ * decoded once to the activation type, scale applied here); the reference
+ * has no counterpart beyond its f16 matmul call (fp8_mps_native.py:150-155).
+ */
+int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64_t lda, int64_t ldb,
+                       int64_t M, int64_t N, int64_t K, const float *scale_b, int scale_b_layout,
+                       const void *bias, int bias_dtype, void *D, int out_dtype, int64_t ldd,
+                       void *stream);
+
+/*
  * Device-side status of the scaled GEMM on the current device: 0 if no
  * bounded wait has timed out, else FP8B200_ETIMEOUT with *status_out holding
  * the site code. Synchronises the device. `reset` clears the word.

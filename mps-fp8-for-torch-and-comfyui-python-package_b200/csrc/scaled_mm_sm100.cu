@@ -67,6 +67,7 @@ struct Params {
   int sk_mt, sk_stages, sk_cs, sk_tmem_cols;  // small-M kernel: rows per tile, ring depth, split-K cluster, TMEM
   int tma_store;                              // epilogue stores through the output tensor map
   int w_fp8;                                  // fp8-weight linear: weight format (FP8B200_E4M3 / E5M2)
+  int kb_elems;                               // elements per 128-byte k-block (128 fp8, 64 16-bit)
   int act_f16;                                // fp8-weight linear: activations f16 (1) or bf16 (0)
 };
 
@@ -806,6 +807,24 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   }
 }
 
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// One CTA-pair MMA of the kind the kernel is built for; the descriptors step
+// through the 128-byte swizzled rows 32 bytes per MMA in both cases.
+template <int KIND>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  if constexpr (KIND == 0) umma_f8f6f4_pair(tmem_d, adesc, bdesc, idesc, accumulate);
+  else umma_f16_pair(tmem_d, adesc, bdesc, idesc, accumulate);
+}
+
 // ------------------------------------------------------------------ CTA-pair wide kernel
 // 256 x 512 output tile per pair. Each K step issues two
 // tcgen05.mma.cta_group::2 (M=256, N=256) that share the A tile, so a k-block
@@ -823,6 +842,7 @@ constexpr int W_THREADS = 64 + 32 * W_EPI_WARPS;     // producer warp, MMA warp,
 constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + W_EPI_WARPS * W_STG_BYTES /*epilogue staging*/ +
                              1024 /*align*/ + 2 * WIDE_BN * 4 /*column tables*/ + 256;
 
+template <int KIND>  // 0: kind::f8f6f4 (fp8 operands, K = 32 per MMA), 1: kind::f16 (16-bit operands, K = 16)
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W_THREADS, 1)
 scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_d, const Params p) {
@@ -890,9 +910,10 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
           if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * W_STAGE_BYTES);
           const uint32_t st = stage_a(stage);
-          tma_load_2d_pair(st, &tmap_a, leader_full, kb * BK, arow);
-          tma_load_2d_pair(st + A2_BYTES, &tmap_b, leader_full, kb * BK, brow0);
-          tma_load_2d_pair(st + A2_BYTES + B2_BYTES, &tmap_b, leader_full, kb * BK, brow0 + PAIR_BN);
+          const int kx = kb * p.kb_elems;  // tensor-map coordinate of the k-block
+          tma_load_2d_pair(st, &tmap_a, leader_full, kx, arow);
+          tma_load_2d_pair(st + A2_BYTES, &tmap_b, leader_full, kx, brow0);
+          tma_load_2d_pair(st + A2_BYTES + B2_BYTES, &tmap_b, leader_full, kx, brow0 + PAIR_BN);
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -924,7 +945,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; k++) {
               const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-              umma_f8f6f4_pair(tmem_base, adesc + koff, b0desc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
             }
             if (++st == W_STAGES) { st = 0; ph ^= 1u; }
           }
@@ -939,7 +960,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_f8f6f4_pair(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc,
+            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc,
                              (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(empty_bar(stage));
@@ -955,8 +976,8 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_f8f6f4_pair(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
-            umma_f8f6f4_pair(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc, 1u);
+            umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
+            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc, 1u);
           }
           umma_commit_pair(empty_bar(stage));
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
@@ -976,7 +997,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     const int etid = threadIdx.x - 64;
     const uint32_t buf = stg_base + (uint32_t)(e * W_STG_BYTES);
     uint32_t acc_phase = 0;
-    const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
+    const float sa_t = p.sa_rowwise ? 0.0f : (p.sa != nullptr ? __ldg(p.sa) : 1.0f);
     const float sb_t = p.sb_rowwise ? 0.0f : __ldg(p.sb);
     const float sr = p.scale_result ? __ldg(p.scale_result) : 1.0f;
     for (int tile = pair; tile < p.num_tiles; tile += npairs) {
@@ -1410,15 +1431,6 @@ __device__ __forceinline__ void convert_weight_row(uint32_t raw, uint32_t dst, i
                  o[j >> 1][4 * (j & 1) + 1], o[j >> 1][4 * (j & 1) + 2], o[j >> 1][4 * (j & 1) + 3]);
 }
 
-__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LW_THREADS, 1)
 linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -1707,7 +1719,7 @@ int pair_clusters(int dev, bool wide) {
     cfg.blockDim = dim3(wide ? W_THREADS : THREADS, 1, 1);
     cfg.dynamicSmemBytes = wide ? W_SMEM_BYTES : SMEM2_BYTES;
     int n = 0;
-    const cudaError_t e = wide ? cudaOccupancyMaxActiveClusters(&n, scaled_mm_wide_kernel, &cfg)
+    const cudaError_t e = wide ? cudaOccupancyMaxActiveClusters(&n, scaled_mm_wide_kernel<0>, &cfg)
                                : cudaOccupancyMaxActiveClusters(&n, scaled_mm_pair_kernel, &cfg);
     if (e != cudaSuccess || n < 1) n = current_sm_count() / 2;
     c = n;
@@ -1821,7 +1833,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(scaled_mm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
+      e = cudaFuncSetAttribute(scaled_mm_wide_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
   }
@@ -1862,6 +1874,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.timeout_ns = g_timeout_ns;
   p.debug_skip_first_load = g_debug_skip_first_load;
   p.sk_mt = mt;
+  p.kb_elems = BK;
   p.sk_stages = p.sk_cs = p.sk_tmem_cols = 0;
   p.tma_store = 0;
   CUtensorMap md;
@@ -1899,7 +1912,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel, ma, mb, p);
   } else if (wide) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
-    scaled_mm_wide_kernel<<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
+    scaled_mm_wide_kernel<0><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
   } else if (pair) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, false));
     scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
@@ -2016,4 +2029,68 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
   linear_fp8w_kernel<<<2 * clusters, LW_THREADS, LW_SMEM_BYTES, (cudaStream_t)stream>>>(mx, mw, p);
   count_launch();
   return check_launch("linear_fp8w");
+}
+
+extern "C" int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64_t lda, int64_t ldb, int64_t M,
+                                  int64_t N, int64_t K, const float *scale_b, int scale_b_layout, const void *bias,
+                                  int bias_dtype, void *D, int out_dtype, int64_t ldd, void *stream) {
+  if (dtype != FP8B200_BF16 && dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: operands must be bf16 or f16");
+  if (out_dtype != FP8B200_F32 && out_dtype != FP8B200_BF16 && out_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: output must be f32, bf16 or f16");
+  if (M < 0 || N < 0 || K < 0) return set_error(FP8B200_EINVAL, "gemm_16bit: negative size");
+  if (M == 0 || N == 0) return FP8B200_OK;
+  if (K == 0) return set_error(FP8B200_EINVAL, "gemm_16bit: K must be positive");
+  if (M > 0x7FFFFFFFLL || N > 0x7FFFFFFFLL || K > 0x7FFFFFFFLL)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: dimension too large");
+  if (lda < K || ldb < K || lda % 8 || ldb % 8)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: row strides must be >= K and multiples of 8 elements");
+  if (ldd < N) return set_error(FP8B200_EINVAL, "gemm_16bit: output row stride < N");
+  if (!A || !B || !D || !scale_b) return set_error(FP8B200_EINVAL, "gemm_16bit: null pointer");
+  if (!aligned16(A) || !aligned16(B)) return set_error(FP8B200_EINVAL, "gemm_16bit: operands must be 16-byte aligned");
+  const int esz = dtype_size(out_dtype);
+  if (!aligned16(D) || (ldd * esz) % 16)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: output rows must be 16-byte aligned");
+  if (scale_b_layout != FP8B200_SCALE_TENSOR && scale_b_layout != FP8B200_SCALE_ROWWISE)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: unknown scale layout");
+  if (bias && bias_dtype != FP8B200_F32 && bias_dtype != FP8B200_BF16 && bias_dtype != FP8B200_F16)
+    return set_error(FP8B200_EINVAL, "gemm_16bit: bias must be f32/bf16/f16");
+  int dev;
+  if (int rc = check_device(&dev)) return rc;
+  static bool attr_done[64] = {};
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(scaled_mm_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         W_SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "gemm_16bit: smem attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  CUtensorMap ma, mb, md;
+  if (int rc = make_map_2d(&ma, A, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, M, lda * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_map_2d(&mb, B, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, N, ldb * 2, 64, HALF_B,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_out_map(&md, D, M, N, ldd, esz)) return rc;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.kb_elems = 64;
+  p.num_kb = (int)((K + 63) / 64);
+  p.tiles_m = (int)((M + 2 * BM - 1) / (2 * BM));
+  p.tiles_n = (int)((N + WIDE_BN - 1) / WIDE_BN);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.sa = nullptr; p.sa_rowwise = 0;
+  p.sb = scale_b; p.sb_rowwise = scale_b_layout == FP8B200_SCALE_ROWWISE;
+  p.bias = bias; p.bias_dtype = bias_dtype;
+  p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
+  p.vec_store = 1;
+  p.tma_store = 1;
+  const uint32_t fmt = dtype == FP8B200_BF16 ? 1u : 0u;
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(PAIR_BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+  p.timeout_ns = g_timeout_ns;
+  p.debug_skip_first_load = g_debug_skip_first_load;
+  const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
+  scaled_mm_wide_kernel<1><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
+  count_launch();
+  return check_launch("gemm_16bit");
 }

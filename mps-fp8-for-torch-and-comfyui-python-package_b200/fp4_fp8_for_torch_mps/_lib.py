@@ -59,6 +59,7 @@ def _declare(L):
         "fp8b200_scaled_mm": [vp, i32, i64, vp, i32, i64, i64, i64, i64,
                               vp, i32, vp, i32, vp, i32, vp, vp, i32, i64, vp],
         "fp8b200_linear_fp8w": [vp, i32, i64, vp, i32, i64, i64, i64, i64, vp, i32, vp, i32, vp, i32, i64, vp],
+        "fp8b200_gemm_16bit": [vp, vp, i32, i64, i64, i64, i64, i64, vp, i32, vp, i32, vp, i32, i64, vp],
         "fp8b200_gemm_status": [ctypes.POINTER(ctypes.c_uint32), i32],
         "fp8b200_debug_gemm": [i32, ctypes.c_ulonglong],
         "fp8b200_gemm_set_path": [i32],

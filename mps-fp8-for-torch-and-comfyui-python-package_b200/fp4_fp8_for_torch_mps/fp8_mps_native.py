@@ -294,6 +294,50 @@ def fp4_quantize(input):
 
 
 # ----------------------------------------------------------------- scaled GEMM
+# Rows of x from which fp8_linear decodes the weights once and runs the 16-bit
+# GEMM instead of dequantising them on load inside the GEMM.
+LINEAR_DECODE_ONCE_M = 1024
+
+
+def gemm_16bit(a: torch.Tensor, b_nk: torch.Tensor, scale_b: torch.Tensor, bias: torch.Tensor | None = None,
+               out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """D = a @ b_nk^T * scale_b [+ bias] for bf16 or f16 a (M, K) and b_nk
+    (N, K) of the same type on the tensor cores (CTA-pair tcgen05 kind::f16).
+    scale_b: 1 value or N values."""
+    if a.dtype not in (torch.bfloat16, torch.float16) or b_nk.dtype != a.dtype:
+        raise RuntimeError("gemm_16bit: operands must both be bfloat16 or both float16")
+    if a.dim() != 2 or b_nk.dim() != 2 or a.shape[1] != b_nk.shape[1]:
+        raise RuntimeError("gemm_16bit: shapes must be (M, K) and (N, K)")
+    M, K = a.shape
+    N = b_nk.shape[0]
+    dev = a.device
+    odt = out_dtype or a.dtype
+
+    def aligned(t):
+        return t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+
+    if not aligned(a) or not aligned(b_nk):
+        kp = (K + 7) // 8 * 8
+        if not aligned(a):
+            a = torch.nn.functional.pad(a, (0, kp - K)) if kp != K else a.contiguous()
+        if not aligned(b_nk):
+            b_nk = torch.nn.functional.pad(b_nk, (0, kp - K)) if kp != K else b_nk.contiguous()
+    sb = scale_b.to(device=dev, dtype=torch.float32).contiguous()
+    if sb.numel() not in (1, N):
+        raise RuntimeError(f"gemm_16bit: scale_b has {sb.numel()} values, expected 1 or {N}")
+    if bias is not None:
+        bias = bias.to(dev).contiguous()
+    npad = (N + 7) // 8 * 8                 # 16-byte aligned output rows
+    out = torch.empty((M, npad), dtype=odt, device=dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().fp8b200_gemm_16bit(
+            a.data_ptr(), b_nk.data_ptr(), L.dtype_code(a.dtype), a.stride(0), b_nk.stride(0), M, N, K,
+            sb.data_ptr(), L.SCALE_TENSOR if sb.numel() == 1 else L.SCALE_ROWWISE,
+            None if bias is None else bias.data_ptr(), 0 if bias is None else L.dtype_code(bias.dtype),
+            out.data_ptr(), L.dtype_code(odt), npad, L.stream_of(a)), "gemm_16bit")
+    return out[:, :N]
+
+
 def fp8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
                bias: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """y = x @ (weight * weight_scale)^T [+ bias] with float8 weights that are
@@ -337,6 +381,17 @@ def fp8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor
             raise RuntimeError("fp8_linear: bias must hold N float values")
     M = x2.shape[0]
     out = torch.empty((M, N), dtype=odt, device=dev)
+    if M >= LINEAR_DECODE_ONCE_M and (N * out.element_size()) % 16 == 0:
+        # many rows: decode the weights once (exact; N*K values against M*N*K
+        # products) and run the 16-bit CTA-pair GEMM with the scale in its epilogue
+        wd = decode_fp8(w.view(torch.uint8), weight.dtype, x.dtype)
+        with torch.cuda.device(dev):
+            L.check(L.lib().fp8b200_gemm_16bit(
+                x2.data_ptr(), wd.data_ptr(), L.dtype_code(x.dtype), x2.stride(0), wd.stride(0), M, N, K,
+                ws.data_ptr(), L.SCALE_TENSOR if ws.numel() == 1 else L.SCALE_ROWWISE,
+                None if bias is None else bias.data_ptr(), 0 if bias is None else L.dtype_code(bias.dtype),
+                out.data_ptr(), L.dtype_code(odt), N, L.stream_of(x2)), "fp8_linear")
+        return out.reshape(*x.shape[:-1], N)
     with torch.cuda.device(dev):
         L.check(L.lib().fp8b200_linear_fp8w(
             x2.data_ptr(), L.dtype_code(x.dtype), x2.stride(0), w.data_ptr(), L.dtype_code(weight.dtype), w.stride(0),

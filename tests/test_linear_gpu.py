@@ -136,3 +136,37 @@ def test_rejects_bad_input(nat):
         nat.fp8_linear(x, w, torch.tensor(1.0))
     with pytest.raises(RuntimeError, match="weight_scale"):
         nat.fp8_linear(x.bfloat16(), w, torch.ones(3))
+
+
+# ---------------------------------------------------------------- many rows: decode once + 16-bit GEMM
+@pytest.mark.parametrize("M,N,K", [(1024, 512, 256), (2048, 1024, 512), (1500, 776, 333), (1100, 100, 64)])
+@pytest.mark.parametrize("wdt", [E4, E5])
+def test_many_rows_path(nat, M, N, K, wdt):
+    """M >= LINEAR_DECODE_ONCE_M: weights decoded once, 16-bit CTA-pair GEMM
+    (N = 100: output rows not 16-byte aligned, dequant-on-load kernel)."""
+    assert M >= nat.LINEAR_DECODE_ONCE_M
+    g = torch.Generator().manual_seed(M + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = rand_w((N, K), wdt, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    bias = torch.randn(N, generator=g)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda(), bias.cuda())
+    r, S = reference(x, w, s, bias)
+    check(out, r, S, f"{M}x{N}x{K} {wdt}")
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 64), (300, 520, 200), (1024, 1536, 1024)])
+def test_gemm_16bit(nat, dt, odt, M, N, K):
+    g = torch.Generator().manual_seed(M * N + K)
+    a = torch.randn(M, K, generator=g).to(dt)
+    b = torch.randn(N, K, generator=g).to(dt)
+    s = torch.rand(N, generator=g) + 0.5
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    out = nat.gemm_16bit(a.cuda(), b.cuda(), s.cuda(), bias.cuda(), out_dtype=odt)
+    av, bv = a.double().numpy(), b.double().numpy()
+    sv, bb = s.double().numpy(), bias.float().double().numpy()
+    r = (av @ bv.T) * sv[None, :] + bb[None, :]
+    S = (np.abs(av) @ np.abs(bv).T) * sv[None, :] + np.abs(bb)[None, :] * 2.0 ** -4
+    check(out, r, S, f"gemm_16bit {dt} {odt} {M}x{N}x{K}")
