@@ -1125,6 +1125,25 @@ __device__ __forceinline__ void store_quad(const Params &p, long long row, int c
   }
 }
 
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int WF, bool TO_F16>
+__device__ __forceinline__ void convert_weight_row(uint32_t raw, uint32_t dst, int r);
+
+// W8 = false: fp8 x fp8 (kind::f8f6f4). W8 = true: float8 weights dequantised
+// on load against 16-bit activations (kind::f16): each stage also holds the
+// raw 128 x 64-byte weight tile (64-byte swizzle), and the epilogue warps,
+// idle until the accumulator is ready, convert it into the MMA's A tile in
+// two groups taking alternate k-blocks (CTA-local barriers only).
+template <bool W8>
 __global__ void __launch_bounds__(THREADS, 1)
 scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const Params p) {
@@ -1134,14 +1153,16 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
   uint8_t *smem = smem_raw + (base - raw_addr);
   const int MT = p.sk_mt, S = p.sk_stages, CS = p.sk_cs;
   const uint32_t a_bytes = (uint32_t)MT * BK;
-  const uint32_t stage_bytes = SK_B_BYTES + a_bytes;
+  // stage: [weights as the MMA's A (16 KiB) | rows of x (MT x 128 bytes) | W8: raw weights (8 KiB)]
+  const uint32_t stage_bytes = SK_B_BYTES + a_bytes + (W8 ? SK_B_BYTES / 2 : 0u);
   float *s_rs = reinterpret_cast<float *>(smem + S * stage_bytes);  // row scales of this tile's MT rows
   uint64_t *bars = reinterpret_cast<uint64_t *>(s_rs + SK_MAX_MT);
   const uint32_t bar_base = smem_u32(bars);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (S + s); };
   const uint32_t tfull = bar_base + 8u * (2 * S);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
+  auto conv_bar = [&](int s) { return bar_base + 8u * (2 * S + 1 + s); };  // W8: A tile converted
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
   float *part = reinterpret_cast<float *>(smem);  // partial tile [MT][128] fp32, over the drained ring
 
   const int warp = threadIdx.x >> 5;
@@ -1157,6 +1178,8 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(tfull, 1);
+    if (W8)
+      for (int s = 0; s < S; s++) mbar_init(conv_bar(s), 2);  // the two warps of one converter group
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
@@ -1181,10 +1204,16 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       for (int kb = kb0; kb < kb1; kb++) {
         if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) break;
         if (p.debug_skip_first_load) break;  // test hook: never fill stage 0
-        mbar_expect_tx(full_bar(stage), stage_bytes);
         const uint32_t st = base + (uint32_t)stage * stage_bytes;
-        tma_load_2d(st, &tmap_b, full_bar(stage), kb * BK, tn * SK_BN);
-        tma_load_2d(st + SK_B_BYTES, &tmap_a, full_bar(stage), kb * BK, tm * MT);
+        const int kx = kb * p.kb_elems;  // tensor-map coordinate of the k-block
+        if (W8) {
+          mbar_expect_tx(full_bar(stage), a_bytes + SK_B_BYTES / 2);
+          tma_load_2d(st + SK_B_BYTES + a_bytes, &tmap_b, full_bar(stage), kx, tn * SK_BN);  // raw weights
+        } else {
+          mbar_expect_tx(full_bar(stage), stage_bytes);
+          tma_load_2d(st, &tmap_b, full_bar(stage), kx, tn * SK_BN);
+        }
+        tma_load_2d(st + SK_B_BYTES, &tmap_a, full_bar(stage), kx, tm * MT);
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
     }
@@ -1195,15 +1224,21 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       uint32_t phase = 0;
       bool fine = true;
       for (int kb = kb0; kb < kb1; kb++) {
-        if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { fine = false; break; }
+        // W8: the converters saw the stage land before converting it
+        if (!mbar_wait(W8 ? conv_bar(stage) : full_bar(stage), phase, p.timeout_ns, 3)) { fine = false; break; }
         tc_fence_after();
         const uint32_t st = base + (uint32_t)stage * stage_bytes;
         const uint64_t wdesc = sdesc_sw128_kmajor(st);
         const uint64_t xdesc = sdesc_sw128_kmajor(st + SK_B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / UMMA_K; k++)
-          umma_f8f6f4(tmem_base, wdesc + (uint64_t)((k * UMMA_K) >> 4), xdesc + (uint64_t)((k * UMMA_K) >> 4),
-                      p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < BK / UMMA_K; k++) {  // 4 MMAs of 32 bytes of K (fp8: K=32, 16-bit: K=16)
+          if (W8)
+            umma_f16(tmem_base, wdesc + (uint64_t)((k * UMMA_K) >> 4), xdesc + (uint64_t)((k * UMMA_K) >> 4), p.idesc,
+                     (kb > kb0 || k > 0) ? 1u : 0u);
+          else
+            umma_f8f6f4(tmem_base, wdesc + (uint64_t)((k * UMMA_K) >> 4), xdesc + (uint64_t)((k * UMMA_K) >> 4),
+                        p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        }
         umma_commit(empty_bar(stage));
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
@@ -1214,7 +1249,38 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
     // every CTA copies its fp32 tile (a partial sum when cs > 1) from TMEM
     // into its drained shared-memory ring as part[row][128 columns]
     const int etid = threadIdx.x - 64;
-    const float sa_t = p.sa_rowwise ? 0.0f : __ldg(p.sa);
+    if (W8) {
+      // ---------------- weight converters during the mainloop: two groups of
+      // two warps take alternate k-blocks; each thread converts rows gt, gt + 64
+      const int group = (warp - 2) >> 1;
+      const int gt = etid - group * 64;
+      bool cok = true;
+      for (int kb = kb0 + group; kb < kb1 && cok; kb += 2) {
+        const int i = kb - kb0;
+        const int stage = i % S;
+        const uint32_t phase = (uint32_t)(i / S) & 1u;
+        int got = 0;
+        if (lane == 0) got = mbar_wait(full_bar(stage), phase, p.timeout_ns, 5) ? 1 : 0;
+        got = __shfl_sync(0xFFFFFFFFu, got, 0);
+        if (!got) { cok = false; break; }
+        const uint32_t st = base + (uint32_t)stage * stage_bytes;
+        const uint32_t raw = st + SK_B_BYTES + a_bytes;
+#pragma unroll
+        for (int r = gt; r < SK_BN; r += 64) {
+          if (p.act_f16) {
+            if (p.w_fp8 == FP8B200_E4M3) convert_weight_row<FP8B200_E4M3, true>(raw, st, r);
+            else convert_weight_row<FP8B200_E5M2, true>(raw, st, r);
+          } else {
+            if (p.w_fp8 == FP8B200_E4M3) convert_weight_row<FP8B200_E4M3, false>(raw, st, r);
+            else convert_weight_row<FP8B200_E5M2, false>(raw, st, r);
+          }
+        }
+        fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(conv_bar(stage));
+      }
+    }
+    const float sa_t = p.sa_rowwise ? 0.0f : (p.sa != nullptr ? __ldg(p.sa) : 1.0f);
     for (int t = etid; t < MT; t += 128) {
       const long long row = (long long)tm * MT + t;
       s_rs[t] = p.sa_rowwise ? (row < p.M ? __ldg(p.sa + row) : 0.0f) : sa_t;
@@ -1741,6 +1807,7 @@ bool prefer_wide(int dev, int64_t M, int64_t N) {
 
 // Resident clusters of `cs` CTAs of the small-M kernel with `smem` bytes of
 // dynamic shared memory on device `dev` (cs == 1: resident CTAs).
+template <bool W8>
 int skinny_resident(int dev, int cs, int smem) {
   struct Entry { int dev, cs, smem, n; };
   static Entry cache[64];
@@ -1752,7 +1819,7 @@ int skinny_resident(int dev, int cs, int smem) {
   int n = 0;
   if (cs == 1) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scaled_mm_skinny_kernel, THREADS, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scaled_mm_skinny_kernel<W8>, THREADS, smem) != cudaSuccess)
       per_sm = 1;
     n = std::max(per_sm, 1) * current_sm_count();
   } else {
@@ -1767,7 +1834,7 @@ int skinny_resident(int dev, int cs, int smem) {
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, scaled_mm_skinny_kernel, &cfg) != cudaSuccess) n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, scaled_mm_skinny_kernel<W8>, &cfg) != cudaSuccess) n = 0;
     cudaGetLastError();  // an unsupported cluster size only disqualifies that size
   }
   if (used < 64) cache[used++] = Entry{dev, cs, smem, n};
@@ -1777,12 +1844,13 @@ int skinny_resident(int dev, int cs, int smem) {
 // Split-K cluster size for `tiles` output tiles of `num_kb` k-blocks: the
 // size that keeps the most CTAs busy per wave; a larger cluster must gain at
 // least 15 % over the best smaller one (the partial reduction is not free).
+template <bool W8>
 int skinny_cluster_size(int dev, long long tiles, int num_kb, int smem) {
   int best_cs = 1;
   double best = 0.0;
   for (int cs = 1; cs <= 8; cs *= 2) {
     if (cs > num_kb) break;
-    const int n = skinny_resident(dev, cs, smem);
+    const int n = skinny_resident<W8>(dev, cs, smem);
     if (n < 1) continue;
     const long long waves = (tiles + n - 1) / n;
     const double score = (double)(tiles * cs) / (double)waves;
@@ -1831,7 +1899,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(scaled_mm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
+      e = cudaFuncSetAttribute(scaled_mm_skinny_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_wide_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
@@ -1896,7 +1964,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   }
 
   if (skinny) {
-    p.sk_cs = skinny_cluster_size(dev, p.num_tiles, p.num_kb, sk_smem);
+    p.sk_cs = skinny_cluster_size<false>(dev, p.num_tiles, p.num_kb, sk_smem);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1909,7 +1977,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
     cfg.numAttrs = p.sk_cs > 1 ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel, ma, mb, p);
+    cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel<false>, ma, mb, p);
   } else if (wide) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
     scaled_mm_wide_kernel<0><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
@@ -2000,6 +2068,70 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     cudaError_t e = cudaFuncSetAttribute(linear_fp8w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LW_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
+  }
+  if (M <= SK_MAX_MT) {
+    // few rows: the small-M kernel with weights dequantised on load (128
+    // weight rows per tile on the MMA's M, K split over a cluster)
+    static bool sk_attr[64] = {};
+    if (dev < 64 && !sk_attr[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(scaled_mm_skinny_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           SK_SMEM_MAX);
+      if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
+      sk_attr[dev] = true;
+    }
+    const int mt = (int)((M + 15) / 16 * 16);
+    CUtensorMap mx, mw;
+    if (int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, M, ldx * 2, LW_BK, mt, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, LW_BK, SK_BN, CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.M = (int)M; p.N = (int)N; p.K = (int)K;
+    p.kb_elems = LW_BK;
+    p.num_kb = (int)((K + LW_BK - 1) / LW_BK);
+    p.tiles_m = 1;
+    p.tiles_n = (int)((N + SK_BN - 1) / SK_BN);
+    p.num_tiles = p.tiles_n;
+    p.sa = nullptr; p.sa_rowwise = 0;
+    p.sb = w_scale; p.sb_rowwise = w_scale_layout == FP8B200_SCALE_ROWWISE;
+    p.bias = bias; p.bias_dtype = bias_dtype;
+    p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
+    p.vec_store = aligned16(D) && ((ldd * dtype_size(out_dtype)) % 16 == 0);
+    p.w_fp8 = w_dtype;
+    p.act_f16 = x_dtype == FP8B200_F16;
+    const uint32_t fmt = p.act_f16 ? 0u : 1u;
+    p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(mt >> 3) << 17) | ((uint32_t)(SK_BN >> 4) << 24);
+    p.timeout_ns = g_timeout_ns;
+    p.debug_skip_first_load = g_debug_skip_first_load;
+    p.sk_mt = mt;
+    const int stage_bytes = SK_B_BYTES + mt * BK + SK_B_BYTES / 2;
+    // This path is bound by the converters' hand-off latency, not by ring
+    // depth: a ring of about 104 KiB lets two CTAs share an SM (more k-block
+    // streams at once), as long as it still holds the fp32 partial tile.
+    const int need = (mt * SK_BN * 4 + stage_bytes - 1) / stage_bytes;
+    p.sk_stages = std::max(need, std::min(SK_MAX_STAGES, (104 * 1024) / stage_bytes));
+    p.sk_stages = std::max(p.sk_stages, 2);
+    int cols = 32;
+    while (cols < mt) cols *= 2;
+    p.sk_tmem_cols = cols;
+    const int sk_smem = p.sk_stages * stage_bytes + 1024 + SK_MAX_MT * 4 + 256;
+    p.sk_cs = skinny_cluster_size<true>(dev, p.num_tiles, p.num_kb, sk_smem);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.sk_cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(p.num_tiles * p.sk_cs), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)sk_smem;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.sk_cs > 1 ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel<true>, mx, mw, p);
+    count_launch();
+    return check_launch("linear_fp8w");
   }
   CUtensorMap mx, mw;
   if (int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, M, ldx * 2, LW_BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
