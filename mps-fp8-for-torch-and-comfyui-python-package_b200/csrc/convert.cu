@@ -194,6 +194,15 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
 constexpr long long kBulkSpinLimit = 1ll << 24;
 __device__ int g_bulk_status;
 
+// Programmatic dependent launch: the bulk converters let the next kernel in
+// the stream launch as soon as every CTA of this one has started, and wait
+// for the previous kernel's completion (and memory) only before their first
+// global access, so launch and prologue overlap the previous kernel's tail.
+// Both are no-ops for launches without the programmatic-serialization
+// attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 template <int KIND>
 __global__ void __launch_bounds__(kDecThreads)
 decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t nbytes, int fmt, int odt,
@@ -204,12 +213,16 @@ decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   uint8_t *in_ring = smem_raw + C::kLutBytes;
   uint8_t *out_ring = in_ring + kStages * C::kIn;
   uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * kOutChunk);
-  const float s = load_scale(scale, mode);
   const int64_t nch = nbytes / C::kIn;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  pdl_launch_dependents();
+  pdl_wait_prior();  // nothing in global memory is read or written before this
+  const float s = load_scale(scale, mode);
+  if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
       const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
       if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
@@ -471,12 +484,16 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   uint8_t *in_ring = smem_raw;
   uint8_t *out_ring = in_ring + kStages * C::kIn;
   uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * C::kOut);
-  const bool scaled = scale != nullptr;
-  const float s = scaled ? __ldg(scale) : 1.0f;
   const int64_t nch = n / kEncElems;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  pdl_launch_dependents();
+  pdl_wait_prior();  // nothing in global memory is read or written before this
+  const bool scaled = scale != nullptr;
+  const float s = scaled ? __ldg(scale) : 1.0f;
+  if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
       const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
       if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
@@ -908,6 +925,22 @@ int resident_per_sm(const void *kernel, int smem_bytes, int threads = kThreads) 
   return n;
 }
 
+// Launch with programmatic stream serialization (see pdl_wait_prior).
+template <typename... Params, typename... Args>
+void launch_pdl(void (*kernel)(Params...), int grid, int threads, int smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3((unsigned)threads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <int KIND>
 void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt, const float *scale, int mode,
                    cudaStream_t st) {
@@ -915,8 +948,8 @@ void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt,
   const int per_sm = resident_per_sm((const void *)decode_bulk_kernel<KIND>, smem, kDecThreads);
   const int64_t nch = nbytes / Dec<KIND>::kIn;
   const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)current_sm_count() * per_sm));
-  decode_bulk_kernel<KIND><<<g, kDecThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, nbytes, fmt, odt, scale,
-                                                        mode);
+  launch_pdl(decode_bulk_kernel<KIND>, g, kDecThreads, smem, st, (const uint8_t *)src, (uint8_t *)dst, nbytes, fmt,
+             odt, scale, mode);
 }
 
 template <int SRC, int FMT>
@@ -926,7 +959,7 @@ void launch_encode(const void *src, void *dst, int64_t n, const float *scale, cu
     const int per_sm = resident_per_sm((const void *)encode_bulk_kernel<SRC, FMT>, smem, kDecThreads);
     const int64_t nch = n / kEncElems;
     const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)current_sm_count() * per_sm));
-    encode_bulk_kernel<SRC, FMT><<<g, kDecThreads, smem, st>>>((const uint8_t *)src, (uint8_t *)dst, n, scale);
+    launch_pdl(encode_bulk_kernel<SRC, FMT>, g, kDecThreads, smem, st, (const uint8_t *)src, (uint8_t *)dst, n, scale);
   } else {  // unaligned: element-wise (the kernel's scalar loop)
     const int g = grid_for(std::max<int64_t>(n, 1), kThreads, resident_per_sm((const void *)encode_kernel<SRC, FMT>, 0));
     encode_kernel<SRC, FMT><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, 0, scale);
