@@ -1194,6 +1194,11 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+  // programmatic dependent launch: the next kernel may launch once every CTA
+  // is here; this kernel touches global memory only after the previous one
+  // has completed (both no-ops without the launch attribute)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   int ok = 1;
   if (warp == 0) {
@@ -1966,17 +1971,19 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   if (skinny) {
     p.sk_cs = skinny_cluster_size<false>(dev, p.num_tiles, p.num_kb, sk_smem);
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)p.sk_cs;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.sk_cs;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(p.num_tiles * p.sk_cs), 1, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
     cfg.dynamicSmemBytes = (size_t)sk_smem;
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
-    cfg.numAttrs = p.sk_cs > 1 ? 1 : 0;
+    cfg.numAttrs = p.sk_cs > 1 ? 2 : 1;
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel<false>, ma, mb, p);
   } else if (wide) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
@@ -2118,17 +2125,19 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     const int sk_smem = p.sk_stages * stage_bytes + 1024 + SK_MAX_MT * 4 + 256;
     p.sk_cs = skinny_cluster_size<true>(dev, p.num_tiles, p.num_kb, sk_smem);
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)p.sk_cs;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.sk_cs;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(p.num_tiles * p.sk_cs), 1, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
     cfg.dynamicSmemBytes = (size_t)sk_smem;
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
-    cfg.numAttrs = p.sk_cs > 1 ? 1 : 0;
+    cfg.numAttrs = p.sk_cs > 1 ? 2 : 1;
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel<true>, mx, mw, p);
     count_launch();
     return check_launch("linear_fp8w");
