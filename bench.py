@@ -476,7 +476,7 @@ class ScaledMMSmallM:
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
         self.L = L
         _, N, K = ROWWISE_SHAPES[args.shape]
-        M = args.m
+        M = args.m or 16
         aq, bq, sa, sb = rowwise_operands(M, N, K, seed=rank)
         self.M, self.N, self.K = M, N, K
         self.profile = f"{self.name}_{M}x{N}x{K}"
@@ -556,7 +556,7 @@ class LinearFp8W:
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
         self.L, self.nat = L, nat
         _, N, K = ROWWISE_SHAPES[args.shape]
-        M = args.m if args.m != 16 else 16384
+        M = args.m or 16384
         g = torch.Generator().manual_seed(rank)
         self.x_host = torch.randn(M, K, generator=g).to(torch.bfloat16)
         _, wq, _, sw = rowwise_operands(1, N, K, seed=rank)
@@ -564,12 +564,18 @@ class LinearFp8W:
         self.M, self.N, self.K = M, N, K
         self.profile = f"{self.name}_{M}x{N}x{K}"
         self.x, self.w, self.s = self.x_host.cuda(), wq.cuda(), self.s_host.cuda()
+        foot = M * K * 2 + N * K + M * N * 2
+        # weight sets rotate when one step's operands would fit in L2 (decode-sized M)
+        self.nsets = 1 if foot > 300_000_000 else max(2, min(32, -(-300_000_000 // (N * K))))
+        self.ws = [self.w] + [self.w.clone() for _ in range(self.nsets - 1)]
+        self.i = 0
         self.out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
         self.work = 2.0 * M * N * K
         self.h2d, self.d2h = M * K * 2, M * N * 2
         self.config = {"workload": self.name, "M": M, "N": N, "K": K, "weights": "e4m3, per-channel scale",
                        "activations": "bf16", "out": "bf16",
-                       "l2": "x+w+y {:.0f} MiB".format((M * K * 2 + N * K + M * N * 2) / 2**20)}
+                       "l2": ("x+w+y {:.0f} MiB > L2".format(foot / 2**20) if self.nsets == 1 else
+                              f"{self.nsets} rotating weight sets, {self.nsets * N * K / 2**20:.0f} MiB > L2")}
         self.stream = torch.cuda.current_stream()
         self.lib = L.lib()
         self.h_x = self.x_host.pin_memory()
@@ -578,7 +584,9 @@ class LinearFp8W:
 
     def step(self):
         L = self.L
-        rc = self.lib.fp8b200_linear_fp8w(self.x.data_ptr(), L.BF16, self.K, self.w.data_ptr(), L.E4M3, self.K,
+        w = self.ws[self.i % self.nsets]
+        self.i += 1
+        rc = self.lib.fp8b200_linear_fp8w(self.x.data_ptr(), L.BF16, self.K, w.data_ptr(), L.E4M3, self.K,
                                           self.M, self.N, self.K, self.s.data_ptr(), L.SCALE_ROWWISE, None, 0,
                                           self.out.data_ptr(), L.BF16, self.N, self.stream.cuda_stream)
         if rc:
@@ -586,7 +594,9 @@ class LinearFp8W:
 
     def e2e_step(self):
         self.d_x.copy_(self.h_x, non_blocking=True)
-        y = torch.ops.fp8_mps.fp8_linear(self.d_x, self.w, self.s)
+        w = self.ws[self.i % self.nsets]
+        self.i += 1
+        y = torch.ops.fp8_mps.fp8_linear(self.d_x, w, self.s)
         self.h_out.copy_(y, non_blocking=True)
 
     def check(self):
@@ -737,7 +747,7 @@ def reference_line(args):
         w = LinearFp8W.__new__(LinearFp8W)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
         _, N, K = ROWWISE_SHAPES[args.shape]
-        M = args.m if args.m != 16 else 16384
+        M = args.m or 16384
         w.x_host = torch.randn(256, K, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
         _, w.w_host, _, sw = rowwise_operands(1, N, K)
         w.s_host = sw.reshape(-1)
@@ -749,12 +759,13 @@ def reference_line(args):
         w = ScaledMMSmallM.__new__(ScaledMMSmallM)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
         _, N, K = ROWWISE_SHAPES[args.shape]
-        w.a_host, w.b_host, w.sa_host, w.sb_host = rowwise_operands(args.m, N, K)
-        w.M, w.N, w.K = args.m, N, K
-        w.work = float(N * K + args.m * K + 2 * args.m * N)
+        m = args.m or 16
+        w.a_host, w.b_host, w.sa_host, w.sb_host = rowwise_operands(m, N, K)
+        w.M, w.N, w.K = m, N, K
+        w.work = float(N * K + m * K + 2 * m * N)
         vals = [w.cpu_run() for _ in range(max(args.steps, 1))]
         unit, metric = "GB/s", "scaled_mm_small_m_GBps"
-        config = {"workload": args.workload, "M": args.m, "N": N, "K": K, "out": "bf16"}
+        config = {"workload": args.workload, "M": m, "N": N, "K": K, "out": "bf16"}
     else:
         w = ScaledMM.__new__(ScaledMM)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands, scaled_mm_operands
@@ -785,7 +796,8 @@ def main():
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--shape", type=int, default=0, choices=[0, 1, 2])
     ap.add_argument("--layers", type=int, default=0, help="llama_fp8: number of layers (default 32)")
-    ap.add_argument("--m", type=int, default=16, help="scaled_mm_small_m: activation rows")
+    ap.add_argument("--m", type=int, default=0,
+                    help="rows of A / x: scaled_mm_small_m (default 16), linear_fp8w (default 16384)")
     args = ap.parse_args()
     rank, local, ws = rank_info()
 
