@@ -859,9 +859,9 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   const uint32_t bar_base = smem_u32(bars);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (W_STAGES + s); };
-  const uint32_t tfull = bar_base + 8u * (2 * W_STAGES);
-  auto tempty_bar = [&](int h) { return bar_base + 8u * (2 * W_STAGES + 1 + h); };  // accumulator half h drained
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * W_STAGES + 3);
+  auto tfull_bar = [&](int h) { return bar_base + 8u * (2 * W_STAGES + h); };       // accumulator half h complete
+  auto tempty_bar = [&](int h) { return bar_base + 8u * (2 * W_STAGES + 2 + h); };  // accumulator half h drained
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * W_STAGES + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -874,7 +874,8 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       mbar_init(full_bar(s), 1);   // used in the leader only
       mbar_init(empty_bar(s), 1);  // one multicast commit per use
     }
-    mbar_init(tfull, 1);
+    mbar_init(tfull_bar(0), 1);
+    mbar_init(tfull_bar(1), 1);
     mbar_init(tempty_bar(0), 2 * W_EPI_WARPS);  // every epilogue warp of both CTAs (leader's barriers)
     mbar_init(tempty_bar(1), 2 * W_EPI_WARPS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -966,7 +967,11 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           umma_commit_pair(empty_bar(stage));
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
         }
-        for (int kb = head; kb < p.num_kb; kb++) {
+        // the last `tail` k-blocks run in two passes as well: all their half-0
+        // MMAs, then half 0 is reported complete (its drain starts), then their
+        // half-1 MMAs (stages still resident), then half 1 is complete
+        const int tail = min(W_STAGES, p.num_kb - head);
+        for (int kb = head; kb < p.num_kb - tail; kb++) {
           if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = stage_a(stage);
@@ -983,7 +988,38 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit_pair(tfull);
+        {
+          int st = stage;
+          uint32_t ph = phase;
+          for (int t = 0; t < tail; t++) {
+            if (!mbar_wait(full_bar(st), ph, p.timeout_ns, 3)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = stage_a(st);
+            const uint64_t adesc = sdesc_sw128_kmajor(sa);
+            const uint64_t b0desc = sdesc_sw128_kmajor(sa + A2_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; k++) {
+              const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
+              umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
+            }
+            if (++st == W_STAGES) { st = 0; ph ^= 1u; }
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(0));
+        for (int t = 0; t < tail; t++) {  // same stages, already full
+          const uint32_t sa = stage_a(stage);
+          const uint64_t adesc = sdesc_sw128_kmajor(sa);
+          const uint64_t b1desc = sdesc_sw128_kmajor(sa + A2_BYTES + B2_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; k++) {
+            const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
+            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc, 1u);
+          }
+          umma_commit_pair(empty_bar(stage));
+          if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        umma_commit_pair(tfull_bar(1));
         acc_phase ^= 1u;
       }
     }
@@ -1011,24 +1047,21 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         s_bias[j] = (in && p.bias != nullptr) ? load_bias(p.bias, p.bias_dtype, col) : 0.0f;
       }
       wide_epilogue_sync();
-      int ok = 0;
-      if (lane == 0) ok = mbar_wait(tfull, acc_phase, p.timeout_ns, 4) ? 1 : 0;
-      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
       const int row0 = tm * (2 * BM) + (int)rank * BM;
+      int ok = 1;
 #pragma unroll 1
-      for (int h = 0; h < 2; h++) {  // release each half as soon as it is read
-        if (p.tma_store)
-          drain_accumulator_tma(p, &tmap_d, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN,
-                                quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, buf, sub, 2);
-        else
-          drain_accumulator(p, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN, quarter, lane,
-                            sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, sub, 2);
+      for (int h = 0; h < 2 && ok; h++) {  // drain each half once it is complete; release it once read
+        if (lane == 0) ok = mbar_wait(tfull_bar(h), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        if (!ok) break;
+        tc_fence_after();
+        drain_accumulator_tma(p, &tmap_d, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN,
+                              quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, buf, sub, 2);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(h), 0));
       }
+      if (!ok) break;
       acc_phase ^= 1u;
     }
     if (lane == 0) bulk_wait_all();  // this warp's stores are done before its staging memory goes away
