@@ -42,7 +42,7 @@ def test_decode_all_codes(nat, golden, fmt, odt):
     assert np.array_equal(bits(dst), golden[f"decode_f{fmt}_o{odt}"])
 
 
-@pytest.mark.parametrize("n", [0, 1, 15, 16, 17, 255, 4097, 1000003])
+@pytest.mark.parametrize("n", [0, 1, 15, 16, 17, 255, 4097, 1000003, 16777216 + 4096 + 48 + 5])
 @pytest.mark.parametrize("offset", [0, 1, 3, 16])
 def test_decode_ragged_and_unaligned(nat, n, offset):
     g = torch.Generator().manual_seed(n + offset)
@@ -115,7 +115,7 @@ def test_encode_planted_edges_and_reference_known_answers(nat, golden, fmt):
             assert np.array_equal(torch.ops.fp8_mps.encode(v).cpu().numpy(), golden[f"kat_{k}_e4m3"]), k
 
 
-@pytest.mark.parametrize("n", [0, 1, 15, 16, 17, 1000003])
+@pytest.mark.parametrize("n", [0, 1, 15, 16, 17, 1000003, 4096 * 444 * 3 + 16 * 7 + 9])
 @pytest.mark.parametrize("offset", [0, 1, 8])
 @pytest.mark.parametrize("sdt", [0, 1, 2])
 def test_encode_ragged_and_unaligned(nat, n, offset, sdt):
@@ -230,7 +230,7 @@ def test_fp4_decode_workload_full_size(nat, odt):
     assert np.array_equal(bits(out), ref)
 
 
-@pytest.mark.parametrize("n", [0, 1, 15, 17, 1000003])
+@pytest.mark.parametrize("n", [0, 1, 15, 17, 1000003, 4096 * 296 * 5 + 16 * 3 + 11])
 @pytest.mark.parametrize("offset", [0, 1, 16])
 def test_fp4_decode_ragged_unaligned(nat, n, offset):
     g = torch.Generator().manual_seed(n)
