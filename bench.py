@@ -75,6 +75,8 @@ def peaks():
 def profile_traffic(name: str):
     """DRAM bytes per launch from an ncu capture summarised in
     profiles/<name>.md (a line `dram_bytes_per_launch: <int>`), or None."""
+    if not name:
+        return None
     p = os.path.join(ROOT, "profiles", name + ".md")
     if not os.path.exists(p):
         return None
@@ -185,6 +187,26 @@ def timed_region(step, steps: int, stream, dist_on: bool):
     return ms
 
 
+def gather_line(w, ws, rank, reps=10):
+    """Replicated-output mode of the row-sharded GEMM, timed on its own: each
+    rank contributes its block of M/ws output rows and
+    parallel.gather_rows (one NCCL all_gather_into_tensor over
+    NVLink/NVSwitch) assembles the full M x N result on every rank."""
+    from fp4_fp8_for_torch_mps.parallel import gather_rows, shard_rows
+    M = w.out.shape[0]
+    s, e = shard_rows(M, ws, rank)
+    local = w.out[s:e]
+    for _ in range(3):
+        full = gather_rows(local, M)
+    torch.cuda.synchronize()
+    ms = timed_region(lambda: gather_rows(local, M), reps, torch.cuda.current_stream(), True) / reps
+    nbytes = full.numel() * full.element_size()
+    return {"ms": round(ms, 4), "bytes_per_rank": local.numel() * local.element_size(), "bytes_total": nbytes,
+            "algbw_GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "busbw_GBps": round(nbytes * (ws - 1) / ws / (ms * 1e-3) / 1e9, 1),
+            "op": "parallel.gather_rows -> NCCL all_gather_into_tensor", "timed": "separately, not in value"}
+
+
 def chunked_e2e(chunks, streams, body):
     """Run body(i, stream_index) for every chunk on rotating streams, joined
     to the current stream (so events on it bracket the whole pipeline)."""
@@ -272,28 +294,49 @@ class Fp4Decode:
 
 
 class Fp8RoundTrip:
+    """FP8 round trip: encode `--src` (f32, bf16 or f16) to `--fmt` (e4m3fn
+    or e5m2), decode back to the source dtype. Default 4096x4096 f32 ->
+    e4m3fn -> f32; `--elems` sets the element count (the 4096x4096 planted
+    input is tiled; e.g. 1073741824 for a 1 Gi-element sweep)."""
     name = "fp8_roundtrip"
     metric = "fp8_roundtrip_GBps"
     unit, bound, kernels_per_step = "GB/s", "hbm", 2
     profile = "fp8_encode_decode_4096x4096"
-    dtype = "f32->e4m3->f32"
-    SETS = 4
+    SRC = {"f32": (torch.float32, 0, 4), "bf16": (torch.bfloat16, 1, 2), "f16": (torch.float16, 2, 2)}
+    FMT = {"e4m3": ("e4m3fn", 0, torch.float8_e4m3fn), "e5m2": ("e5m2", 1, torch.float8_e5m2)}
 
     def __init__(self, rank, args):
         from fp4_fp8_for_torch_mps import _lib as L
         from fp4_fp8_for_torch_mps import fp8_mps_native as nat
         from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
         self.L, self.nat = L, nat
-        self.x_host = fp8_roundtrip_input(seed=rank)
-        n = self.x_host.numel()
+        src, fmt = getattr(args, "src", "f32"), getattr(args, "fmt", "e4m3")
+        self.src, self.fmt_key = src, fmt
+        self.tdt, self.sdt, eb = self.SRC[src]
+        self.fmt_name, self.fmt, self.fp8 = self.FMT[fmt]
+        self.l_sdt = (L.F32, L.BF16, L.F16)[self.sdt]
+        self.l_fmt = (L.E4M3, L.E5M2)[self.fmt]
+        base = fp8_roundtrip_input(seed=rank)
+        n = getattr(args, "elems", 0) or base.numel()
+        flat = base.view(-1)
+        if n > flat.numel():
+            flat = flat.repeat((n + flat.numel() - 1) // flat.numel())
+        self.x_host = flat[:n].to(self.tdt).reshape(base.shape if n == base.numel() else (n,))
+        self.dtype = f"{src}->{self.fmt_name}->{src}"
+        if (src, fmt, n) != ("f32", "e4m3", base.numel()):
+            self.profile = None  # the committed ncu summary covers the default case only
+        step_bytes = n * (2 * eb + 2)
+        self.SETS = 4 if step_bytes < (1 << 30) else 1
         self.xs = [self.x_host.cuda() for _ in range(self.SETS)]
         self.codes = [torch.empty(n, dtype=torch.uint8, device="cuda") for _ in range(self.SETS)]
-        self.back = [torch.empty(n, dtype=torch.float32, device="cuda") for _ in range(self.SETS)]
+        self.back = [torch.empty(n, dtype=self.tdt, device="cuda") for _ in range(self.SETS)]
         self.i = 0
-        self.work = n * 10                       # encode 5 B/elt + decode 5 B/elt
-        self.h2d, self.d2h = n * 4, n * 4
-        self.config = {"workload": "fp8_roundtrip", "shape": list(self.x_host.shape), "fp8": "e4m3fn",
-                       "l2": f"{self.SETS} rotating buffer sets (576 MiB) > L2"}
+        self.work = step_bytes                   # encode (eb + 1) B/elt + decode (1 + eb) B/elt
+        self.h2d, self.d2h = n * eb, n * eb
+        self.config = {"workload": "fp8_roundtrip", "shape": list(self.x_host.shape), "src": src,
+                       "fp8": self.fmt_name,
+                       "l2": (f"{self.SETS} rotating buffer sets ({self.SETS * step_bytes / 2**20:.0f} MiB) > L2"
+                              if self.SETS > 1 else f"one buffer set of {step_bytes / 2**20:.0f} MiB > L2")}
         self.stream = torch.cuda.current_stream()
         self.lib = L.lib()
         self.h_in = self.x_host.pin_memory()
@@ -302,19 +345,19 @@ class Fp8RoundTrip:
         self.streams = [torch.cuda.Stream() for _ in range(3)]
         cn = n // self.chunks
         self.cn = cn
-        self.d_in = [torch.empty(cn, dtype=torch.float32, device="cuda") for _ in self.streams]
+        self.d_in = [torch.empty(cn, dtype=self.tdt, device="cuda") for _ in self.streams]
         self.d_mid = [torch.empty(cn, dtype=torch.uint8, device="cuda") for _ in self.streams]
-        self.d_out = [torch.empty(cn, dtype=torch.float32, device="cuda") for _ in self.streams]
+        self.d_out = [torch.empty(cn, dtype=self.tdt, device="cuda") for _ in self.streams]
 
     graph = None
     graph_launches = 0  # kernels in the captured graph
 
     def _launch(self, k, s):
         n = self.codes[k].numel()
-        rc = self.lib.fp8b200_encode_fp8(self.xs[k].data_ptr(), self.L.F32, self.codes[k].data_ptr(),
-                                         self.L.E4M3, n, None, s)
-        rc = rc or self.lib.fp8b200_decode_fp8(self.codes[k].data_ptr(), self.L.E4M3, self.back[k].data_ptr(),
-                                               self.L.F32, n, None, 0, s)
+        rc = self.lib.fp8b200_encode_fp8(self.xs[k].data_ptr(), self.l_sdt, self.codes[k].data_ptr(),
+                                         self.l_fmt, n, None, s)
+        rc = rc or self.lib.fp8b200_decode_fp8(self.codes[k].data_ptr(), self.l_fmt, self.back[k].data_ptr(),
+                                               self.l_sdt, n, None, 0, s)
         if rc:
             self.L.check(rc, "fp8 round trip")
 
@@ -349,32 +392,40 @@ class Fp8RoundTrip:
 
         def body(i, j):
             self.d_in[j].copy_(hin[i * c:(i + 1) * c], non_blocking=True)
-            self.nat.encode_fp8(self.d_in[j], torch.float8_e4m3fn, out=self.d_mid[j])
-            self.nat.decode_fp8(self.d_mid[j], torch.float8_e4m3fn, torch.float32, out=self.d_out[j])
+            self.nat.encode_fp8(self.d_in[j], self.fp8, out=self.d_mid[j])
+            self.nat.decode_fp8(self.d_mid[j], self.fp8, self.tdt, out=self.d_out[j])
             hout[i * c:(i + 1) * c].copy_(self.d_out[j], non_blocking=True)
         chunked_e2e(self.chunks, self.streams, body)
 
     def check(self):
         import numpy as np
         from oracle import oracle as O
-        xb = self.x_host.view(-1)[:1 << 16].view(torch.int32).numpy().view(np.uint32)
-        ref = O.decode_fp8(O.encode_fp8(xb, 0, 0), 0, 0)
-        got = self.h_out.view(-1)[:1 << 16].view(torch.int32).numpy().view(np.uint32)
+        npu = np.uint32 if self.sdt == 0 else np.uint16
+        ity = torch.int32 if self.sdt == 0 else torch.int16
+        xb = self.x_host.view(-1)[:1 << 16].view(ity).numpy().view(npu)
+        ref = O.decode_fp8(O.encode_fp8(xb, self.sdt, self.fmt), self.fmt, self.sdt)
+        got = self.h_out.view(-1)[:1 << 16].view(ity).numpy().view(npu)
         return bool(np.array_equal(ref, got))
 
+    def cpu_run(self):
+        return Fp8RoundTrip.cpu_run_for(src=self.src, fmt=self.fmt_key)
+
     @staticmethod
-    def cpu_run(rows=4096, reps=3):
+    def cpu_run_for(rows=4096, reps=3, src="f32", fmt="e4m3"):
         import numpy as np
         from oracle import oracle as O
         from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
-        xb = fp8_roundtrip_input(0).view(torch.int32).numpy().view(np.uint32).reshape(-1)
-        xb = xb[: rows * 4096]
+        tdt, sdt, eb = Fp8RoundTrip.SRC[src]
+        f = Fp8RoundTrip.FMT[fmt][1]
+        x = fp8_roundtrip_input(0).view(-1)[: rows * 4096].to(tdt)
+        xb = x.view(torch.int32 if sdt == 0 else torch.int16).numpy().view(np.uint32 if sdt == 0 else np.uint16)
         threads = os.cpu_count() or 1
         t0 = time.perf_counter()
         for _ in range(reps):
-            O.decode_fp8(O.encode_fp8(xb, 0, 0, threads=threads), 0, 0, threads=threads)
+            O.decode_fp8(O.encode_fp8(xb, sdt, f, threads=threads), f, sdt, threads=threads)
         dt = (time.perf_counter() - t0) / reps
-        return xb.size * 10 / dt / 1e9, threads, f"{rows}x4096 f32 encode+decode per pass (oracle, C)"
+        return xb.size * (2 * eb + 2) / dt / 1e9, threads, \
+            f"{rows}x4096 {src} encode to {Fp8RoundTrip.FMT[fmt][0]} + decode per pass (oracle, C)"
 
 
 class ScaledMM:
@@ -739,9 +790,11 @@ def reference_line(args):
         unit, metric = "GB/s", "fp4_decode_GBps"
         config = {"workload": "fp4_decode", "shape": [16384, 8192], "out": "bf16", "scale": 0.37}
     elif args.workload == "fp8_roundtrip":
-        vals = [Fp8RoundTrip.cpu_run(rows=4096, reps=1) for _ in range(max(args.steps, 1))]
+        vals = [Fp8RoundTrip.cpu_run_for(rows=4096, reps=1, src=args.src, fmt=args.fmt) for _ in range(max(args.steps, 1))]
         unit, metric = "GB/s", "fp8_roundtrip_GBps"
-        config = {"workload": "fp8_roundtrip", "shape": [4096, 4096], "fp8": "e4m3fn"}
+        config = {"workload": "fp8_roundtrip", "shape": [args.elems] if args.elems else [4096, 4096],
+                  "src": args.src, "fp8": Fp8RoundTrip.FMT[args.fmt][0],
+                  "sample": "4096x4096 elements per step" if args.elems else "full size"}
     elif args.workload == "linear_fp8w":
         w = LinearFp8W.__new__(LinearFp8W)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
@@ -795,6 +848,12 @@ def main():
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--shape", type=int, default=0, choices=[0, 1, 2])
     ap.add_argument("--layers", type=int, default=0, help="llama_fp8: number of layers (default 32)")
+    ap.add_argument("--elems", type=int, default=0,
+                    help="fp8_roundtrip: elements per step (default 4096x4096; 1073741824 for the 1 Gi sweep)")
+    ap.add_argument("--src", default="f32", choices=["f32", "bf16", "f16"], help="fp8_roundtrip: source dtype")
+    ap.add_argument("--fmt", default="e4m3", choices=["e4m3", "e5m2"], help="fp8_roundtrip: fp8 format")
+    ap.add_argument("--gather", action="store_true",
+                    help="scaled_mm at N > 1: also time the replicated-output all-gather of the M-sharded result")
     ap.add_argument("--m", type=int, default=0,
                     help="rows of A / x: scaled_mm_small_m (default 16), linear_fp8w (default 16384)")
     args = ap.parse_args()
@@ -847,6 +906,7 @@ def main():
     e2e_steps = max(3, min(args.steps, 10))
     e2e_ms = timed_region(w.e2e_step, e2e_steps, torch.cuda.current_stream(), dist_on)
     ok = w.check()
+    gather = gather_line(w, ws, rank) if (args.gather and dist_on and hasattr(w, "out")) else None
 
     pk, pk_kind = peaks()
     per_step_s = ms / args.steps * 1e-3
@@ -892,6 +952,8 @@ def main():
         "clocks": clocks,
         "result_check": ok,
     }
+    if gather is not None:
+        line["gather"] = gather
     print(json.dumps(line))
     return 0
 

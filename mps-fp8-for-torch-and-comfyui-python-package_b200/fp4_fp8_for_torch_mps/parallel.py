@@ -49,6 +49,14 @@ def gather_rows(local: torch.Tensor, total_rows: int, group=None) -> torch.Tenso
     for d in tail:
         row_bytes *= d
     lb = local.contiguous().view(torch.uint8).reshape(local.shape[0], row_bytes)
+    if total_rows % ws == 0:  # equal blocks: gather straight into the result, no padding or concatenation
+        full = torch.empty((total_rows,) + tail, dtype=dt, device=local.device)
+        fb = full.view(torch.uint8).reshape(total_rows, row_bytes)
+        if dist.get_backend(group) == "nccl":
+            dist.all_gather_into_tensor(fb, lb, group=group)
+        else:
+            dist.all_gather(list(fb.chunk(ws)), lb, group=group)
+        return full
     padded = torch.zeros((rows_max, row_bytes), dtype=torch.uint8, device=local.device)
     padded[: lb.shape[0]] = lb
     out = torch.empty((ws * rows_max, row_bytes), dtype=torch.uint8, device=local.device)
