@@ -790,26 +790,72 @@ __device__ __forceinline__ uint32_t silu_mul_bf16(uint32_t g, uint32_t u) {
   return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(silu_bf16(gf) * uf));
 }
 
-// The float silu(x) value that silu_bf16 rounds (fast or exact, whichever
-// rounds to the formula's bf16), for two values at once packed to bf16x2.
-__device__ __forceinline__ float silu_pre(float x) {
-  if (fabsf(x) <= 16.0f) {
-    const float s = __fdividef(x, 1.0f + __expf(-x));
-    const int d = (int)(__float_as_uint(s) & 0xFFFFu) - 0x8000;
-    if (d > 64 || d < -64) return s;
-  }
-  return x / (1.0f + expf(-x));
+// Packed two-lane f32 arithmetic (sm_100 f32x2: one instruction for two
+// IEEE round-to-nearest operations, bit-identical to two scalar ones).
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// Two bf16(silu(g)) * u products from packed bf16x2 words g and u. The
-// product of two bf16 values is exact in float, so one bf16x2 multiply
-// (round to nearest even, no contraction) equals PyTorch's float product
-// rounded to bf16.
+// Two bf16(silu(g)) * u products from packed bf16x2 words g and u. The fast
+// silu value x * 1/(1 + 2^(-x log2 e)) comes from the hardware ex2 and rcp
+// approximations (on |x| <= 16 neither sees a subnormal, so their
+// flush-to-zero forms are exact-range safe) with paired f32x2 arithmetic; as
+// in silu_bf16, the formula itself is evaluated whenever a value of the pair is
+// within 64 ulp of a bf16 rounding midpoint (low 16 bits 0x7FC0..0x8040), or
+// |x| > 16, or x is not finite. The product of two bf16 values is exact in
+// float, so one bf16x2 multiply (round to nearest even, no contraction) equals
+// PyTorch's float product rounded to bf16.
 __device__ __forceinline__ uint32_t silu_mul_bf16x2(uint32_t g, uint32_t u) {
-  const __nv_bfloat162 s2 = __floats2bfloat162_rn(silu_pre(u2f(g << 16)), silu_pre(u2f(g & 0xFFFF0000u)));
+  const float x0 = u2f(g << 16), x1 = u2f(g & 0xFFFF0000u);
+  const unsigned long long xx = f2pack(x0, x1);
+  float t0, t1, d0, d1, s0, s1;
+  f2unpack(mul_f32x2(xx, f2pack(-1.4426950408889634f, -1.4426950408889634f)), t0, t1);
+  f2unpack(add_f32x2(f2pack(ex2_approx_ftz(t0), ex2_approx_ftz(t1)), f2pack(1.0f, 1.0f)), d0, d1);
+  f2unpack(mul_f32x2(xx, f2pack(rcp_approx_ftz(d0), rcp_approx_ftz(d1))), s0, s1);
+  const bool near0 = ((__float_as_uint(s0) - 0x7FC0u) & 0xFFFFu) <= 128u;
+  const bool near1 = ((__float_as_uint(s1) - 0x7FC0u) & 0xFFFFu) <= 128u;
+  if (!(fabsf(x0) <= 16.0f) || !(fabsf(x1) <= 16.0f) || near0 || near1) {  // rare
+    s0 = x0 / (1.0f + expf(-x0));
+    s1 = x1 / (1.0f + expf(-x1));
+  }
+  const __nv_bfloat162 s2 = __floats2bfloat162_rn(s0, s1);
   uint32_t y;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t *>(&s2)), "r"(u));
   return y;
+}
+
+// Running max of |y| over bf16x2 words, NaN-propagating: for non-NaN values
+// the result equals an integer max of the magnitude bits; any NaN makes the
+// lane NaN (the row's scale then takes its NaN branch either way).
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t m, uint32_t y) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(y & 0x7FFF7FFFu));
+  return r;
 }
 
 // Eight bf16 values (one 16-byte vector) -> eight fp8 codes of value * s,
@@ -840,6 +886,20 @@ __device__ __forceinline__ uint2 encode8_bf16(uint4 v, float s) {
   return make_uint2(o[0], o[1]);
 }
 
+// encode8_bf16 for a row whose amax and scale are finite: then every
+// |value * s| <= fmax (1 + 2^-23), below the first value that rounds past the
+// largest finite code, so the cvt pairs alone give CPU PyTorch's codes.
+template <int FMT>
+__device__ __forceinline__ uint2 encode8_bf16_finite(uint4 v, float s) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const unsigned long long ss = f2pack(s, s);
+  float x[8];
+#pragma unroll
+  for (int q = 0; q < 4; q++) f2unpack(mul_f32x2(f2pack(u2f(w[q] << 16), u2f(w[q] & 0xFFFF0000u)), ss), x[2 * q], x[2 * q + 1]);
+  return make_uint2(cvt_pair<FMT>(x[0], x[1]) | (cvt_pair<FMT>(x[2], x[3]) << 16),
+                    cvt_pair<FMT>(x[4], x[5]) | (cvt_pair<FMT>(x[6], x[7]) << 16));
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kRowThreads)
 silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *__restrict__ dst, int64_t ld_dst,
@@ -847,11 +907,12 @@ silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *_
   extern __shared__ __align__(16) uint16_t ybuf[];  // F bf16 values of the current row
   __shared__ uint32_t warp_max[kRowThreads / 32];
   __shared__ float row_scale;
+  __shared__ int row_finite;  // amax and scale finite: the cvt pairs need no fix-up
   const int64_t nvec = vec ? F / 8 : 0;  // 8 bf16 per 16-byte vector
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const uint16_t *g = gu + r * ld, *u = g + F;
     const uint4 *g4 = reinterpret_cast<const uint4 *>(g), *u4 = reinterpret_cast<const uint4 *>(u);
-    uint32_t m_lo = 0, m_hi = 0;  // amax bits of the low and high bf16 halves
+    uint32_t m2 = 0;  // |y| max of the low and high bf16 lanes
     int64_t v = threadIdx.x;
     for (; v + kRowThreads < nvec; v += 2 * kRowThreads) {  // two vectors of g and u in flight
       const uint4 ga = g4[v], ua = u4[v], gb = g4[v + kRowThreads], ub = u4[v + kRowThreads];
@@ -861,7 +922,7 @@ silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *_
                                   silu_mul_bf16x2(gb.z, ub.z), silu_mul_bf16x2(gb.w, ub.w));
       const uint32_t ys[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
 #pragma unroll
-      for (int q = 0; q < 8; q++) { m_lo = max(m_lo, ys[q] & 0x7FFFu); m_hi = max(m_hi, ys[q] & 0x7FFF0000u); }
+      for (int q = 0; q < 8; q++) m2 = absmax_bf16x2(m2, ys[q]);
       reinterpret_cast<uint4 *>(ybuf)[v] = ya;
       reinterpret_cast<uint4 *>(ybuf)[v + kRowThreads] = yb;
     }
@@ -871,15 +932,15 @@ silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *_
                                   silu_mul_bf16x2(ga.z, ua.z), silu_mul_bf16x2(ga.w, ua.w));
       const uint32_t ys[4] = {ya.x, ya.y, ya.z, ya.w};
 #pragma unroll
-      for (int q = 0; q < 4; q++) { m_lo = max(m_lo, ys[q] & 0x7FFFu); m_hi = max(m_hi, ys[q] & 0x7FFF0000u); }
+      for (int q = 0; q < 4; q++) m2 = absmax_bf16x2(m2, ys[q]);
       reinterpret_cast<uint4 *>(ybuf)[v] = ya;
     }
     for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads) {
       const uint32_t y = silu_mul_bf16(g[i], u[i]);
-      m_lo = max(m_lo, y & 0x7FFFu);
+      m2 = absmax_bf16x2(m2, y & 0xFFFFu);
       ybuf[i] = (uint16_t)y;
     }
-    uint32_t m = max(m_lo << 16, m_hi);
+    uint32_t m = max(m2 << 16, m2 & 0xFFFF0000u);
     m = __reduce_max_sync(0xFFFFFFFFu, m);
     if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
     __syncthreads();
@@ -889,13 +950,18 @@ silu_mul_quantize_kernel(const uint16_t *__restrict__ gu, int64_t ld, uint8_t *_
       const double a = (double)u2f(t);
       const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
       row_scale = (float)sd;
+      row_finite = t < 0x7F800000u && __float_as_uint((float)sd) < 0x7F800000u;
       inv_scale[r] = (float)(1.0 / sd);
     }
     __syncthreads();
     const float s = row_scale;
     uint8_t *rd = dst + r * ld_dst;
-    for (int64_t w = threadIdx.x; w < nvec; w += kRowThreads)  // 8 elements -> 8 bytes
-      reinterpret_cast<uint2 *>(rd)[w] = encode8_bf16<FMT>(reinterpret_cast<const uint4 *>(ybuf)[w], s);
+    if (row_finite)
+      for (int64_t w = threadIdx.x; w < nvec; w += kRowThreads)  // 8 elements -> 8 bytes
+        reinterpret_cast<uint2 *>(rd)[w] = encode8_bf16_finite<FMT>(reinterpret_cast<const uint4 *>(ybuf)[w], s);
+    else
+      for (int64_t w = threadIdx.x; w < nvec; w += kRowThreads)
+        reinterpret_cast<uint2 *>(rd)[w] = encode8_bf16<FMT>(reinterpret_cast<const uint4 *>(ybuf)[w], s);
     for (int64_t i = nvec * 8 + threadIdx.x; i < F; i += kRowThreads)
       rd[i] = (uint8_t)encode_one<FP8B200_BF16, FMT>(ybuf[i], true, s);
     __syncthreads();  // ybuf / warp_max / row_scale are reused by the next row
@@ -911,14 +977,24 @@ int resident_per_sm(const void *kernel, int smem_bytes, int threads = kThreads) 
   struct Entry { const void *k; int dev; int smem; int n; };
   static Entry cache[128];
   static int used = 0;
+  struct Limit { const void *k; int dev; int smem; };  // dynamic shared memory limit set so far
+  static Limit limits[64];
+  static int nlimits = 0;
   static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
+  if (smem_bytes > 48 * 1024) {  // the limit only ever rises, so every size seen before still launches
+    int i = 0;
+    while (i < nlimits && !(limits[i].k == kernel && limits[i].dev == dev)) i++;
+    if (i == nlimits || limits[i].smem < smem_bytes) {
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+      if (i == nlimits && nlimits < 64) limits[nlimits++] = Limit{kernel, dev, smem_bytes};
+      else if (i < nlimits) limits[i].smem = smem_bytes;
+    }
+  }
   for (int i = 0; i < used; i++)
     if (cache[i].k == kernel && cache[i].dev == dev && cache[i].smem == smem_bytes) return cache[i].n;
-  if (smem_bytes > 48 * 1024)
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem_bytes) != cudaSuccess || n < 1) n = 1;
   if (used < 128) cache[used++] = Entry{kernel, dev, smem_bytes, n};
@@ -1227,11 +1303,11 @@ extern "C" int fp8b200_silu_mul_quantize_rows_fp8(const void *gate_up, int64_t r
   const int vec = aligned16(gate_up) && f % 8 == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0 &&
                   ld_dst % 8 == 0;
   const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
+  cudaStream_t st = (cudaStream_t)stream;
   const void *k = fp8_dtype == FP8B200_E4M3 ? (const void *)silu_mul_quantize_kernel<FP8B200_E4M3>
                                             : (const void *)silu_mul_quantize_kernel<FP8B200_E5M2>;
   const int per_sm = resident_per_sm(k, (int)smem, kRowThreads);
   const int g = (int)std::min<int64_t>(rows, (int64_t)current_sm_count() * per_sm);
-  cudaStream_t st = (cudaStream_t)stream;
   if (fp8_dtype == FP8B200_E4M3)
     silu_mul_quantize_kernel<FP8B200_E4M3><<<g, kRowThreads, smem, st>>>((const uint16_t *)gate_up, ld, (uint8_t *)dst,
                                                                         ld_dst, rows, f, vec, fmax, inv_scale);

@@ -31,7 +31,8 @@ def assert_same(a, b):
 
 
 @pytest.mark.parametrize("fmt", FP8)
-@pytest.mark.parametrize("rows,f", [(0, 64), (1, 1), (3, 7), (5, 8), (17, 1000), (257, 14336), (2, 24577)])
+@pytest.mark.parametrize("rows,f", [(0, 64), (1, 1), (3, 7), (5, 8), (17, 1000), (257, 14336), (2, 24577),
+                                    (3, 38912), (2, 38920), (1000, 4096), (7, 2048 * 3 + 8), (600, 14336)])
 def test_matches_unfused(nat, fmt, rows, f):
     g = torch.Generator(device="cuda").manual_seed(rows * 131 + f)
     gu = (torch.randn(rows, 2 * f, generator=g, device="cuda") * 3).to(torch.bfloat16)
@@ -48,6 +49,25 @@ def test_every_bf16_gate_value(nat, fmt):
                           device="cuda").to(torch.bfloat16)):
         gu = torch.cat([g, u])[None]
         assert_same(nat.silu_mul_quantize_rows_fp8(gu, fmt), unfused(nat, gu, fmt))
+
+
+@pytest.mark.parametrize("fmt", FP8)
+def test_every_bf16_gate_value_in_short_rows(nat, fmt):
+    """All 65536 bf16 patterns as g in 4 rows of F = 16384 (vectorised
+    path), against random u."""
+    g = torch.arange(65536, dtype=torch.int32, device="cuda").to(torch.int16).view(torch.bfloat16).reshape(4, -1)
+    u = torch.randn(4, 16384, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda").to(torch.bfloat16)
+    gu = torch.cat([g, u], dim=1)
+    assert_same(nat.silu_mul_quantize_rows_fp8(gu, fmt), unfused(nat, gu, fmt))
+
+
+def test_row_lengths_up_and_down(nat):
+    """Alternating large and small rows: every launch still gets the shared
+    memory it needs (the per-kernel limit only rises)."""
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    for f in (24576, 1000, 24576, 64, 38912, 8, 24576):
+        gu = (torch.randn(9, 2 * f, generator=gen, device="cuda") * 2).to(torch.bfloat16)
+        assert_same(nat.silu_mul_quantize_rows_fp8(gu), unfused(nat, gu, torch.float8_e4m3fn))
 
 
 @pytest.mark.parametrize("fmt", FP8)
