@@ -410,6 +410,89 @@ __device__ __forceinline__ void encode_unit(const EncIn<SRC> &e, uint8_t *out, b
   st_u128(out, o[0], o[1], o[2], o[3]);
 }
 
+// Packed two-lane f32 arithmetic (sm_100 f32x2: one instruction for two
+// IEEE round-to-nearest operations, bit-identical to two scalar ones).
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// max |x| bits (as f32 bit patterns) over one 16-value unit
+template <int SRC>
+__device__ __forceinline__ uint32_t unit_absmax(const EncIn<SRC> &e) {
+  uint32_t m = 0, sg;
+#pragma unroll
+  for (int h = 0; h < (SRC == FP8B200_F32 ? 2 : 1); h++) {
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      if constexpr (SRC == FP8B200_F32) m = max(m, e.a[h].w[j] & 0x7FFFFFFFu);
+      else {
+        m = max(m, f2u(widen<SRC>(e.a[h].w[j] & 0xFFFFu, sg)) & 0x7FFFFFFFu);
+        m = max(m, f2u(widen<SRC>(e.a[h].w[j] >> 16, sg)) & 0x7FFFFFFFu);
+      }
+    }
+  }
+  return m;
+}
+
+// Per-row scale from the row's amax bits t: scale = fmax / amax (1 when amax
+// is 0 or NaN), computed in double and rounded to float; inv = 1 / scale.
+// Returns whether amax and the scale are finite (encode_unit_finite applies).
+__device__ __forceinline__ int row_scale_of(uint32_t t, float fmax, float &scale, float *inv) {
+  const double a = (double)u2f(t);
+  const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+  scale = (float)sd;
+  *inv = (float)(1.0 / sd);
+  return t < 0x7F800000u && __float_as_uint(scale) < 0x7F800000u;
+}
+
+// encode_unit for rows whose amax and scale are finite: |x * s| <= fmax (1 +
+// 2^-23) for every element, so no element needs the fix-up and the products
+// run as f32x2 pairs (the same IEEE roundings as one multiply each).
+template <int SRC, int FMT>
+__device__ __forceinline__ void encode_unit_finite(const EncIn<SRC> &e, uint8_t *out, float s) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  float x[16];
+  const unsigned long long ss = f2pack(s, s);
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    uint32_t sg;
+    float lo, hi;
+    if constexpr (EB == 4) { lo = u2f(e.a[j >> 2].w[2 * (j & 3)]); hi = u2f(e.a[j >> 2].w[2 * (j & 3) + 1]); }
+    else { lo = widen<SRC>(e.a[0].w[j] & 0xFFFFu, sg); hi = widen<SRC>(e.a[0].w[j] >> 16, sg); }
+    f2unpack(mul_f32x2(f2pack(lo, hi), ss), x[2 * j], x[2 * j + 1]);
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++)
+    o[q] = cvt_pair<FMT>(x[4 * q], x[4 * q + 1]) | (cvt_pair<FMT>(x[4 * q + 2], x[4 * q + 3]) << 16);
+  st_u128(out, o[0], o[1], o[2], o[3]);
+}
+
 // vec: source 32-byte and destination 16-byte aligned; otherwise every
 // element goes through the scalar loop (still on the GPU).
 template <int SRC, int FMT>
@@ -711,6 +794,7 @@ quantize_rows_reg_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_
   constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
   __shared__ uint32_t warp_max[kRowThreads / 32];
   __shared__ float row_scale;
+  __shared__ int row_finite;
   const int nunits = (int)(cols / 16);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const uint8_t *rs = src + r * ld_src * EB;
@@ -721,42 +805,75 @@ quantize_rows_reg_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_
       const int u = threadIdx.x + k * kRowThreads;
       if (u < nunits) in[k] = load_enc<SRC>(rs + (int64_t)u * 16 * EB);
     }
-    uint32_t m = 0, sg;
+    uint32_t m = 0;
 #pragma unroll
-    for (int k = 0; k < KV; k++) {
-      if (threadIdx.x + k * kRowThreads < nunits) {
-#pragma unroll
-        for (int h = 0; h < EB / 2; h++) {
-#pragma unroll
-          for (int j = 0; j < 8; j++) {
-            if constexpr (EB == 4) m = max(m, f2u(widen<SRC>(in[k].a[h].w[j], sg)) & 0x7FFFFFFFu);
-            else {
-              m = max(m, f2u(widen<SRC>(in[k].a[h].w[j] & 0xFFFFu, sg)) & 0x7FFFFFFFu);
-              m = max(m, f2u(widen<SRC>(in[k].a[h].w[j] >> 16, sg)) & 0x7FFFFFFFu);
-            }
-          }
-        }
-      }
-    }
+    for (int k = 0; k < KV; k++)
+      if (threadIdx.x + k * kRowThreads < nunits) m = max(m, unit_absmax<SRC>(in[k]));
     m = __reduce_max_sync(0xFFFFFFFFu, m);
     if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
     __syncthreads();
     if (threadIdx.x == 0) {
       uint32_t t = 0;
       for (int w = 0; w < kRowThreads / 32; w++) t = max(t, warp_max[w]);
-      const double a = (double)u2f(t);
-      const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
-      row_scale = (float)sd;
-      inv_scale[r] = (float)(1.0 / sd);
+      float sc;
+      row_finite = row_scale_of(t, fmax, sc, inv_scale + r);
+      row_scale = sc;
     }
     __syncthreads();
     const float s = row_scale;
+    const bool finite = row_finite;
 #pragma unroll
     for (int k = 0; k < KV; k++) {
       const int u = threadIdx.x + k * kRowThreads;
-      if (u < nunits) encode_unit<SRC, FMT>(in[k], rd + (int64_t)u * 16, true, s);
+      if (u < nunits) {
+        if (finite) encode_unit_finite<SRC, FMT>(in[k], rd + (int64_t)u * 16, s);
+        else encode_unit<SRC, FMT>(in[k], rd + (int64_t)u * 16, true, s);
+      }
     }
     __syncthreads();  // warp_max / row_scale are reused by the next row
+  }
+}
+
+// Rows of at most 32 x KW units (16 values each; 4096 bf16 values at KW = 8)
+// are quantised one row per warp: the whole row sits in the warp's
+// registers, its amax is one warp reduction and no block barrier separates
+// the load, reduce and encode steps, so the SM's other warps keep their rows'
+// loads in flight meanwhile. Same results as quantize_rows_kernel.
+template <int SRC, int FMT, int KW>
+__global__ void __launch_bounds__(kRowThreads)
+quantize_rows_warp_kernel(const uint8_t *__restrict__ src, int64_t ld_src, uint8_t *__restrict__ dst, int64_t ld_dst,
+                          int64_t rows, int64_t cols, float fmax, float *__restrict__ inv_scale) {
+  constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (kRowThreads / 32);
+  const int nunits = (int)(cols / 16);
+  for (int64_t r = (int64_t)blockIdx.x * (kRowThreads / 32) + (threadIdx.x >> 5); r < rows; r += nwarps) {
+    const uint8_t *rs = src + r * ld_src * EB;
+    uint8_t *rd = dst + r * ld_dst;
+    EncIn<SRC> in[KW];
+#pragma unroll
+    for (int k = 0; k < KW; k++) {
+      const int u = lane + 32 * k;
+      if (u < nunits) in[k] = load_enc<SRC>(rs + (int64_t)u * 16 * EB);
+    }
+    uint32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < KW; k++)
+      if (lane + 32 * k < nunits) m = max(m, unit_absmax<SRC>(in[k]));
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    float s = 0.0f;
+    int finite = 0;
+    if (lane == 0) finite = row_scale_of(m, fmax, s, inv_scale + r);
+    s = __shfl_sync(0xFFFFFFFFu, s, 0);
+    finite = __shfl_sync(0xFFFFFFFFu, finite, 0);
+#pragma unroll
+    for (int k = 0; k < KW; k++) {
+      const int u = lane + 32 * k;
+      if (u < nunits) {
+        if (finite) encode_unit_finite<SRC, FMT>(in[k], rd + (int64_t)u * 16, s);
+        else encode_unit<SRC, FMT>(in[k], rd + (int64_t)u * 16, true, s);
+      }
+    }
   }
 }
 
@@ -788,37 +905,6 @@ __device__ __forceinline__ float silu_bf16(float x) {
 __device__ __forceinline__ uint32_t silu_mul_bf16(uint32_t g, uint32_t u) {
   const float gf = u2f(g << 16), uf = u2f(u << 16);
   return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(silu_bf16(gf) * uf));
-}
-
-// Packed two-lane f32 arithmetic (sm_100 f32x2: one instruction for two
-// IEEE round-to-nearest operations, bit-identical to two scalar ones).
-__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2unpack(unsigned long long v, float &lo, float &hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ float ex2_approx_ftz(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float rcp_approx_ftz(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
 }
 
 // Two bf16(silu(g)) * u products from packed bf16x2 words g and u. The fast
@@ -1234,6 +1320,38 @@ void launch_rows_reg_kv(int kv, const uint8_t *s, int64_t ld_src, uint8_t *d, in
   else launch_rows_reg_t<SRC, FMT, 8>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
 }
 
+template <int SRC, int FMT, int KW>
+void launch_rows_warp_t(const uint8_t *s, int64_t ld_src, uint8_t *d, int64_t ld_dst, int64_t rows, int64_t cols,
+                        float fmax, float *inv, cudaStream_t st) {
+  const void *k = (const void *)quantize_rows_warp_kernel<SRC, FMT, KW>;
+  const int64_t blocks = (rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
+  const int g = (int)std::min<int64_t>(blocks, (int64_t)current_sm_count() * resident_per_sm(k, 0, kRowThreads));
+  quantize_rows_warp_kernel<SRC, FMT, KW><<<g, kRowThreads, 0, st>>>(s, ld_src, d, ld_dst, rows, cols, fmax, inv);
+}
+
+template <int SRC, int FMT>
+void launch_rows_warp_kw(int kw, const uint8_t *s, int64_t ld_src, uint8_t *d, int64_t ld_dst, int64_t rows,
+                         int64_t cols, float fmax, float *inv, cudaStream_t st) {
+  if (kw == 1) launch_rows_warp_t<SRC, FMT, 1>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  else if (kw == 2) launch_rows_warp_t<SRC, FMT, 2>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  else if (kw == 4) launch_rows_warp_t<SRC, FMT, 4>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  else if constexpr (SRC != FP8B200_F32) launch_rows_warp_t<SRC, FMT, 8>(s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+}
+
+// One row per warp for rows of at most 32 x (8 units for 16-bit, 4 for f32).
+void launch_rows_warp(int src_dtype, int fp8_dtype, int kw, const uint8_t *s, int64_t ld_src, uint8_t *d,
+                      int64_t ld_dst, int64_t rows, int64_t cols, float fmax, float *inv, cudaStream_t st) {
+  if (fp8_dtype == FP8B200_E4M3) {
+    if (src_dtype == FP8B200_F32) launch_rows_warp_kw<FP8B200_F32, FP8B200_E4M3>(kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else if (src_dtype == FP8B200_BF16) launch_rows_warp_kw<FP8B200_BF16, FP8B200_E4M3>(kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else launch_rows_warp_kw<FP8B200_F16, FP8B200_E4M3>(kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  } else {
+    if (src_dtype == FP8B200_F32) launch_rows_warp_kw<FP8B200_F32, FP8B200_E5M2>(kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else if (src_dtype == FP8B200_BF16) launch_rows_warp_kw<FP8B200_BF16, FP8B200_E5M2>(kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+    else launch_rows_warp_kw<FP8B200_F16, FP8B200_E5M2>(kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv, st);
+  }
+}
+
 void launch_rows_reg(int src_dtype, int fp8_dtype, int kv, const uint8_t *s, int64_t ld_src, uint8_t *d,
                      int64_t ld_dst, int64_t rows, int64_t cols, float fmax, float *inv, cudaStream_t st) {
   if (fp8_dtype == FP8B200_E4M3) {
@@ -1265,7 +1383,13 @@ extern "C" int fp8b200_quantize_rows_fp8(const void *src, int src_dtype, int64_t
   const uint8_t *s = (const uint8_t *)src;
   uint8_t *d = (uint8_t *)dst;
   const int64_t nunits = cols / 16;
-  if (vec && cols % 16 == 0 && nunits <= 8 * kRowThreads) {  // whole row in registers
+  if (vec && cols % 16 == 0 && nunits <= 32 * (eb == 4 ? 4 : 8)) {  // whole row in one warp's registers
+    const int kw = nunits <= 32 ? 1 : nunits <= 64 ? 2 : nunits <= 128 ? 4 : 8;
+    launch_rows_warp(src_dtype, fp8_dtype, kw, s, ld_src, d, ld_dst, rows, cols, fmax, inv_scale, st);
+    count_launch();
+    return check_launch("quantize_rows");
+  }
+  if (vec && cols % 16 == 0 && nunits <= 8 * kRowThreads) {  // whole row in the block's registers
     const int kv = nunits <= kRowThreads ? 1 : nunits <= 2 * kRowThreads ? 2 : nunits <= 4 * kRowThreads ? 4 : 8;
     launch_rows_reg(src_dtype, fp8_dtype, kv, s, ld_src, d, ld_dst, rows, cols, fmax, inv_scale, st);
     count_launch();

@@ -275,7 +275,8 @@ def test_fp4_quantize_matches_reference_formula(nat):
 
 
 # ---------------------------------------------------------------- per-row quantize
-@pytest.mark.parametrize("rows,cols", [(1, 16), (3, 17), (64, 4096), (37, 14336), (5, 1000), (2, 70000)])
+@pytest.mark.parametrize("rows,cols", [(1, 16), (3, 17), (64, 4096), (37, 14336), (5, 1000), (2, 70000),
+                                       (300, 512), (1000, 2048), (9, 4080), (17, 1024), (40, 4112)])
 @pytest.mark.parametrize("sdt", [0, 1, 2])
 @pytest.mark.parametrize("fmt", [0, 1])
 def test_quantize_rows(nat, rows, cols, sdt, fmt):
@@ -284,6 +285,11 @@ def test_quantize_rows(nat, rows, cols, sdt, fmt):
     if rows > 2:
         x[1] = 0                                  # all-zero row -> scale 1
         x[2, cols // 2] = float("nan")            # NaN row -> scale 1, NaN code
+    if rows > 5:
+        x[3, cols - 1] = float("-inf")            # inf row -> scale 0, NaN / zero codes
+        x[4] = 0
+        x[4, 0] = 1e-40 if sdt != 2 else 6e-8     # tiny amax -> scale overflows to inf
+        x[5, 1] = 60000.0                          # large amax among ordinary values
     codes, inv = nat.quantize_rows_fp8(x.cuda(), FP8[fmt])
     assert codes.dtype == FP8[fmt] and codes.shape == (rows, cols) and inv.shape == (rows, 1)
     fmax = 448.0 if fmt == 0 else 57344.0
