@@ -299,7 +299,8 @@ def test_quantize_rows(nat, rows, cols, sdt, fmt):
     for r in range(rows):
         amax = np.float64(np.max(np.abs(xf[r])))
         sd = fmax / amax if amax > 0 else 1.0
-        assert gi[r] == np.float32(1.0 / sd), r
+        with np.errstate(divide="ignore"):        # inf row: scale 0, inverse inf
+            assert gi[r] == np.float32(1.0 / sd), r
         assert np.array_equal(got[r], O.encode_fp8_scaled(xf[r], np.float32(sd), fmt)), r
 
 
