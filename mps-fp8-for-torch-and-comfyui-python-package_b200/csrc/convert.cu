@@ -1446,55 +1446,58 @@ extern "C" int fp8b200_silu_mul_quantize_rows_fp8(const void *gate_up, int64_t r
 // Rotary position embedding of the q and k heads of a fused qkv projection,
 // with the roundings of PyTorch's bf16 expression
 //   cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
-// (each product of two bf16 values is exact in float and rounded to bf16; the
-// float difference / sum of those is rounded to bf16). One thread produces 8
+// (each product of two bf16 values rounded to bf16, then the float difference
+// / sum of those rounded to bf16). Both steps run as bf16x2 instructions
+// (mul/sub/add .rn.bf16x2, rounding once from the exact result): a product of
+// two bf16 values is exact in float, and for the sum and difference the float
+// intermediate rounding is innocuous because float carries 24 >= 2 x 8 + 2
+// significand bits, so one rounding from the exact value gives the same bf16
+// as PyTorch's float operation followed by rounding. One thread produces 8
 // outputs of each half of one head: 16-byte loads of x1, x2, cos and sin,
 // 16-byte stores. Rows of qkv are tokens (position = token % seq); q heads come
 // first, then k heads, head_dim contiguous elements each.
 namespace fp8b200 {
 namespace {
 
-__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 
+template <typename I>  // index type: 32-bit when the work fits, else 64-bit
 __global__ void __launch_bounds__(256)
-rope_kernel(const uint16_t *__restrict__ qkv, int64_t ld, int64_t tokens, int nq, int nk, int hd, int seq,
+rope_kernel(const uint16_t *__restrict__ qkv, int64_t ld, I tokens, I nq, I nk, I hd, I seq,
             const uint16_t *__restrict__ cosv, const uint16_t *__restrict__ sinv, uint16_t *__restrict__ oq,
             uint16_t *__restrict__ ok) {
-  const int half = hd / 2, groups = half / 8, heads = nq + nk;
-  const int64_t total = tokens * heads * groups;
-  for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (int64_t)gridDim.x * blockDim.x) {
-    const int g = (int)(w % groups);
-    const int64_t th = w / groups;
-    const int h = (int)(th % heads);
-    const int64_t t = th / heads;
-    const int pos = (int)(t % seq);
-    const uint16_t *x = qkv + t * ld + (int64_t)h * hd + g * 8;
+  const I half = hd / 2, groups = half / 8, heads = nq + nk;
+  const I total = tokens * heads * groups;
+  for (I w = (I)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (I)gridDim.x * blockDim.x) {
+    const I th = w / groups, g = w - th * groups;
+    const I t = th / heads, h = th - t * heads;
+    const I pos = t % seq;
+    const uint16_t *x = qkv + (int64_t)t * ld + (int64_t)h * hd + g * 8;
     const uint4 a = *reinterpret_cast<const uint4 *>(x);
     const uint4 b = *reinterpret_cast<const uint4 *>(x + half);
     const uint4 c = __ldg(reinterpret_cast<const uint4 *>(cosv + (int64_t)pos * half + g * 8));
     const uint4 s = __ldg(reinterpret_cast<const uint4 *>(sinv + (int64_t)pos * half + g * 8));
-    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-    const uint32_t cw[4] = {c.x, c.y, c.z, c.w}, sw[4] = {s.x, s.y, s.z, s.w};
-    uint32_t lo[4], hi[4];
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      float o1[2], o2[2];
-#pragma unroll
-      for (int e = 0; e < 2; e++) {
-        const float x1 = e ? bf16hi(aw[q]) : bf16lo(aw[q]), x2 = e ? bf16hi(bw[q]) : bf16lo(bw[q]);
-        const float cc = e ? bf16hi(cw[q]) : bf16lo(cw[q]), ss = e ? bf16hi(sw[q]) : bf16lo(sw[q]);
-        o1[e] = rbf(x1 * cc) - rbf(x2 * ss);
-        o2[e] = rbf(x2 * cc) + rbf(x1 * ss);
-      }
-      const __nv_bfloat162 p1 = __floats2bfloat162_rn(o1[0], o1[1]), p2 = __floats2bfloat162_rn(o2[0], o2[1]);
-      lo[q] = *reinterpret_cast<const uint32_t *>(&p1);
-      hi[q] = *reinterpret_cast<const uint32_t *>(&p2);
-    }
-    uint16_t *o = h < nq ? oq + (t * nq + h) * hd : ok + (t * nk + (h - nq)) * hd;
-    *reinterpret_cast<uint4 *>(o + g * 8) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4 *>(o + half + g * 8) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    const uint4 lo = make_uint4(bsub2(bmul2(a.x, c.x), bmul2(b.x, s.x)), bsub2(bmul2(a.y, c.y), bmul2(b.y, s.y)),
+                                bsub2(bmul2(a.z, c.z), bmul2(b.z, s.z)), bsub2(bmul2(a.w, c.w), bmul2(b.w, s.w)));
+    const uint4 hi = make_uint4(badd2(bmul2(b.x, c.x), bmul2(a.x, s.x)), badd2(bmul2(b.y, c.y), bmul2(a.y, s.y)),
+                                badd2(bmul2(b.z, c.z), bmul2(a.z, s.z)), badd2(bmul2(b.w, c.w), bmul2(a.w, s.w)));
+    uint16_t *o = h < nq ? oq + ((int64_t)t * nq + h) * hd : ok + ((int64_t)t * nk + (h - nq)) * hd;
+    *reinterpret_cast<uint4 *>(o + g * 8) = lo;
+    *reinterpret_cast<uint4 *>(o + half + g * 8) = hi;
   }
 }
 
@@ -1521,9 +1524,17 @@ extern "C" int fp8b200_rope_bf16(const void *qkv, int64_t tokens, int64_t ld, in
   if (int rc = check_device(&dev)) return rc;
   const int64_t work = tokens * (n_q_heads + n_k_heads) * (head_dim / 16);
   const int g = (int)std::min<int64_t>((work + 255) / 256, (int64_t)current_sm_count() * 8);
-  rope_kernel<<<g, 256, 0, (cudaStream_t)stream>>>((const uint16_t *)qkv, ld, tokens, n_q_heads, n_k_heads,
-                                                   head_dim, seq, (const uint16_t *)cos_table,
-                                                   (const uint16_t *)sin_table, (uint16_t *)out_q, (uint16_t *)out_k);
+  const int64_t total = tokens * (n_q_heads + n_k_heads) * (head_dim / 16);
+  if (total + (int64_t)g * 256 < ((int64_t)1 << 31) && tokens * (int64_t)(n_q_heads + n_k_heads) * head_dim < ((int64_t)1 << 31))
+    rope_kernel<int><<<g, 256, 0, (cudaStream_t)stream>>>((const uint16_t *)qkv, ld, (int)tokens, n_q_heads, n_k_heads,
+                                                          head_dim, seq, (const uint16_t *)cos_table,
+                                                          (const uint16_t *)sin_table, (uint16_t *)out_q,
+                                                          (uint16_t *)out_k);
+  else
+    rope_kernel<int64_t><<<g, 256, 0, (cudaStream_t)stream>>>((const uint16_t *)qkv, ld, tokens, n_q_heads,
+                                                              n_k_heads, head_dim, seq, (const uint16_t *)cos_table,
+                                                              (const uint16_t *)sin_table, (uint16_t *)out_q,
+                                                              (uint16_t *)out_k);
   count_launch();
   return check_launch("rope");
 }
