@@ -683,6 +683,7 @@ class LlamaFp8:
     profile = "scaled_mm_llama_fp8"
     dtype = "e4m3 linears (f32 acc), bf16 attention/norms"
     scaling = "strong"
+    sustained = True  # a step is ~0.1 s of GEMMs at the power cap
 
     def __init__(self, rank, args):
         from fp4_fp8_for_torch_mps.workloads import LLAMA, Fp8LlamaStack, llama_input
@@ -919,13 +920,17 @@ def main():
         achieved, gemm_ms, n_gemm = w.gemm_roofline()
         extra = {"gemm_ms_per_step": round(gemm_ms, 3), "gemm_launches_per_step": n_gemm,
                  "gemm_share": round(gemm_ms / (ms / args.steps), 4)}
+    # GEMMs timed inside a long step (seconds under the power cap) against the
+    # sustained GEMM peak, GEMMs timed on their own against the burst peak
+    bf16_key = "bf16_tflops_sustained" if getattr(w, "sustained", False) and "bf16_tflops_sustained" in pk \
+        else "bf16_tflops"
     if w.bound == "hbm":
         peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
     elif w.bound == "tensor_bf16":
-        peak, punit, psrc = pk["bf16_tflops"], "TFLOP/s", f"{pk_kind} bf16_tflops"
+        peak, punit, psrc = pk[bf16_key], "TFLOP/s", f"{pk_kind} {bf16_key}"
     else:
-        peak, punit = 2.0 * pk["bf16_tflops"], "TFLOP/s"
-        psrc = f"2 x {pk_kind} bf16_tflops (dense fp8 issue rate is twice bf16 on tcgen05)"
+        peak, punit = 2.0 * pk[bf16_key], "TFLOP/s"
+        psrc = f"2 x {pk_kind} {bf16_key} (dense fp8 issue rate is twice bf16 on tcgen05)"
     cpu = None
     if rank == 0:
         v, cores, sample = w.cpu_run() if hasattr(w, "cpu_run") else (None, None, None)
