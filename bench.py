@@ -428,6 +428,149 @@ class Fp8RoundTrip:
             f"{rows}x4096 {src} encode to {Fp8RoundTrip.FMT[fmt][0]} + decode per pass (oracle, C)"
 
 
+class Quantize:
+    """Dynamic quantisation rows of the path, each one bench line:
+    fp8_quantize  -- per-tensor e4m3 (amax pass, scale, encode pass) of the
+                     4096x4096 f32 FP8 round-trip input; bytes = in + out;
+    quantize_rows -- per-token e4m3 of 16384x4096 bf16 activations (the
+                     Llama-shaped stack's linear inputs); bytes = in + out + scales;
+    fp4_quantize  -- per-tensor FP4 (amax pass, scale, nibble encode) of
+                     16384x16384 bf16 (the FP4 decode output's shape)."""
+    unit, bound = "GB/s", "hbm"
+    profile = None
+
+    def __init__(self, rank, args, kind):
+        from fp4_fp8_for_torch_mps import _lib as L
+        from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
+        self.L, self.kind = L, kind
+        self.name, self.metric = kind, f"{kind}_GBps"
+        g = torch.Generator().manual_seed(rank)
+        if kind == "fp8_quantize":
+            self.x_host = fp8_roundtrip_input(seed=rank)
+            self.dtype, sets = "f32->e4m3 (per tensor)", 4
+        elif kind == "quantize_rows":
+            self.x_host = torch.randn(16384, 4096, generator=g).to(torch.bfloat16)
+            self.dtype, sets = "bf16->e4m3 (per row)", 2
+        else:
+            self.x_host = (torch.randn(16384, 16384, generator=g) * 3).to(torch.bfloat16)
+            self.dtype, sets = "bf16->fp4 e2m1 (per tensor)", 1
+        x = self.x_host
+        n, eb = x.numel(), x.element_size()
+        self.n, self.sets = n, sets
+        self.xs = [x.cuda() for _ in range(sets)]
+        out_n = n // 2 if kind == "fp4_quantize" else n
+        self.outs = [torch.empty(out_n, dtype=torch.uint8, device="cuda") for _ in range(sets)]
+        rows = x.shape[0]
+        self.scales = torch.empty(rows if kind == "quantize_rows" else 2, dtype=torch.float32, device="cuda")
+        self.scratch = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.work = n * eb + out_n + (4 * rows if kind == "quantize_rows" else 0)
+        self.h2d, self.d2h = n * eb, out_n + 4 * (rows if kind == "quantize_rows" else 1)
+        per_set = n * eb + out_n
+        self.config = {"workload": kind, "shape": list(x.shape), "src": str(x.dtype).replace("torch.", ""),
+                       "l2": (f"{sets} rotating buffer sets ({sets * per_set / 2**20:.0f} MiB) > L2" if sets > 1
+                              else f"{per_set / 2**20:.0f} MiB per step > L2")}
+        self.stream = torch.cuda.current_stream()
+        self.lib = L.lib()
+        self.i = 0
+        n0 = L.launch_count()
+        self.step()
+        torch.cuda.synchronize()
+        self.kernels_per_step = L.launch_count() - n0
+        self.h_in = x.pin_memory()
+        self.d_in = torch.empty_like(self.xs[0])
+        self.h_out = torch.empty(out_n, dtype=torch.uint8).pin_memory()
+        self.h_scales = torch.empty(self.scales.numel(), dtype=torch.float32).pin_memory()
+
+    def step(self):
+        k = self.i % self.sets
+        self.i += 1
+        L, x, o, st = self.L, self.xs[k], self.outs[k], self.stream.cuda_stream
+        if self.kind == "fp8_quantize":
+            rc = self.lib.fp8b200_quantize_fp8(x.data_ptr(), L.F32, o.data_ptr(), L.E4M3, self.n,
+                                               self.scales.data_ptr(), self.scratch.data_ptr(), st)
+        elif self.kind == "quantize_rows":
+            r, c = x.shape
+            rc = self.lib.fp8b200_quantize_rows_fp8(x.data_ptr(), L.BF16, r, c, c, o.data_ptr(), c, L.E4M3,
+                                                    self.scales.data_ptr(), st)
+        else:
+            rc = self.lib.fp8b200_quantize_fp4(x.data_ptr(), L.BF16, o.data_ptr(), self.n,
+                                               self.scales.data_ptr(), self.scratch.data_ptr(), st)
+        if rc:
+            L.check(rc, self.kind)
+
+    def e2e_step(self):
+        # public API on an input copied from pinned host memory, results read back
+        self.d_in.copy_(self.h_in, non_blocking=True)
+        if self.kind == "fp8_quantize":
+            q, s = torch.ops.fp8_mps.quantize(self.d_in)
+        elif self.kind == "quantize_rows":
+            from fp4_fp8_for_torch_mps import fp8_mps_native as nat
+            q, s = nat.quantize_rows_fp8(self.d_in)
+        else:
+            q, s = torch.ops.fp8_mps.fp4_quantize(self.d_in)
+        self.h_out.copy_(q.reshape(-1).view(torch.uint8), non_blocking=True)
+        self.h_scales[:s.numel()].copy_(s.reshape(-1), non_blocking=True)
+
+    def check(self):
+        import numpy as np
+        from oracle import oracle as O
+        got = self.h_out.numpy()
+        if self.kind == "quantize_rows":
+            xf = self.x_host[:16].float().numpy()
+            cols = xf.shape[1]
+            for r in range(16):
+                amax = np.float64(np.max(np.abs(xf[r])))
+                sd = 448.0 / amax if amax > 0 else 1.0
+                if self.h_scales[r].item() != np.float32(1.0 / sd):
+                    return False
+                if not np.array_equal(got[r * cols:(r + 1) * cols], O.encode_fp8_scaled(xf[r], np.float32(sd), 0)):
+                    return False
+            return True
+        amax = float(self.x_host.float().abs().max())
+        m = 1 << 16
+        xf = self.x_host.reshape(-1)[:m].float().numpy()
+        # the reference's rule: scale = fmax / amax if amax > 0 else 1 (a NaN amax gives 1)
+        if self.kind == "fp8_quantize":
+            scale = 448.0 / amax if amax > 0 else 1.0
+            ok = np.array_equal(got[:m], O.encode_fp8_scaled(xf, scale, 0))
+        else:
+            scale = 6.0 / amax if amax > 0 else 1.0
+            ok = np.array_equal(got[:m // 2], O.fp4_encode_ref(xf, scale))
+        return bool(ok and self.h_scales[0].item() == np.float32(1.0 / scale))
+
+    def cpu_run(self):
+        return Quantize.cpu_run_for(self.kind)
+
+    @staticmethod
+    def cpu_run_for(kind, reps=1):
+        """The oracle (C, one thread) on a 1024-row sample: amax, scale, encode."""
+        import numpy as np
+        from oracle import oracle as O
+        from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
+        g = torch.Generator().manual_seed(0)
+        if kind == "fp8_quantize":
+            x = fp8_roundtrip_input(0)[:1024].numpy()
+            eb, outb = 4, 1.0
+        elif kind == "quantize_rows":
+            x = torch.randn(1024, 4096, generator=g).to(torch.bfloat16).float().numpy()
+            eb, outb = 2, 1.0
+        else:
+            x = (torch.randn(1024, 16384, generator=g) * 3).to(torch.bfloat16).float().numpy()
+            eb, outb = 2, 0.5
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            if kind == "quantize_rows":
+                for r in range(x.shape[0]):
+                    a = float(np.max(np.abs(x[r])))
+                    O.encode_fp8_scaled(x[r], np.float32(448.0 / a if a > 0 else 1.0), 0)
+            elif kind == "fp8_quantize":
+                O.encode_fp8_scaled(x, 448.0 / float(np.max(np.abs(x))), 0)
+            else:
+                O.fp4_encode_ref(x, 6.0 / float(np.max(np.abs(x))))
+        dt = (time.perf_counter() - t0) / reps
+        return x.size * (eb + outb) / dt / 1e9, 1, f"{x.shape[0]}x{x.shape[1]} {kind} per pass (oracle, C, 1 thread)"
+
+
 class ScaledMM:
     name = "scaled_mm"
     unit, bound, kernels_per_step = "TFLOP/s", "tensor", 1
@@ -776,7 +919,10 @@ def llama_cpu_tokens_per_s(layers: int, reps: int = 1, seq: int = 256):
 WORKLOADS = {"fp4_decode": Fp4Decode, "fp8_roundtrip": Fp8RoundTrip, "llama_fp8": LlamaFp8,
              "scaled_mm": lambda r, a: ScaledMM(r, a, False),
              "scaled_mm_rowwise": lambda r, a: ScaledMM(r, a, True), "scaled_mm_small_m": ScaledMMSmallM,
-             "linear_fp8w": LinearFp8W}
+             "linear_fp8w": LinearFp8W,
+             "fp8_quantize": lambda r, a: Quantize(r, a, "fp8_quantize"),
+             "quantize_rows": lambda r, a: Quantize(r, a, "quantize_rows"),
+             "fp4_quantize": lambda r, a: Quantize(r, a, "fp4_quantize")}
 
 
 # ---------------------------------------------------------------- reference arm
@@ -796,6 +942,11 @@ def reference_line(args):
         config = {"workload": "fp8_roundtrip", "shape": [args.elems] if args.elems else [4096, 4096],
                   "src": args.src, "fp8": Fp8RoundTrip.FMT[args.fmt][0],
                   "sample": "4096x4096 elements per step" if args.elems else "full size"}
+    elif args.workload in ("fp8_quantize", "quantize_rows", "fp4_quantize"):
+        vals = [Quantize.cpu_run_for(args.workload) for _ in range(max(args.steps, 1))]
+        unit, metric = "GB/s", f"{args.workload}_GBps"
+        shape = {"fp8_quantize": [4096, 4096], "quantize_rows": [16384, 4096], "fp4_quantize": [16384, 16384]}
+        config = {"workload": args.workload, "shape": shape[args.workload], "sample": "1024 rows per step"}
     elif args.workload == "linear_fp8w":
         w = LinearFp8W.__new__(LinearFp8W)
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands

@@ -558,10 +558,26 @@ __device__ __forceinline__ uint32_t encode4(const uint8_t *in, int idx, bool sca
   return o;
 }
 
+// Scale of a per-tensor quantisation from the amax bits left by amax_kernel:
+// fmax / amax in double rounded to float (1 if amax is 0 or NaN); block 0
+// also publishes {scale, 1/scale} to scale_out.
+__device__ __forceinline__ float scale_from_amax(const uint32_t *amax_bits, float fmax, float *scale_out) {
+  const double a = (double)u2f(__ldg(amax_bits));
+  const double sd = (a > 0.0) ? (double)fmax / a : 1.0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    scale_out[0] = (float)sd;
+    scale_out[1] = (float)(1.0 / sd);
+  }
+  return (float)sd;
+}
+
+// scale: multiply by *scale; or amax_bits: the scale of a per-tensor
+// quantisation (scale_from_amax); neither: plain encode.
 template <int SRC, int FMT>
 __global__ void __launch_bounds__(kDecThreads)
 encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t n,
-                   const float *__restrict__ scale) {
+                   const float *__restrict__ scale, const uint32_t *__restrict__ amax_bits, float fmax,
+                   float *__restrict__ scale_out) {
   using C = Enc<SRC>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint8_t *in_ring = smem_raw;
@@ -574,8 +590,8 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   }
   pdl_launch_dependents();
   pdl_wait_prior();  // nothing in global memory is read or written before this
-  const bool scaled = scale != nullptr;
-  const float s = scaled ? __ldg(scale) : 1.0f;
+  const bool scaled = scale != nullptr || amax_bits != nullptr;
+  const float s = amax_bits ? scale_from_amax(amax_bits, fmax, scale_out) : scale ? __ldg(scale) : 1.0f;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
       const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
@@ -625,12 +641,52 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
 // The reference's nearest-of-8 threshold encoder (shaders/fp8_matmul.metal:
 // 88-102): not round-to-nearest-even at ties (0.25 -> 0.5, 1.25 -> 1.5), NaN
 // -> +6, -0.0 -> +0. Element 2i goes to the low nibble (:271-273).
+// The threshold chain v < 0.25 -> 0, < 0.75 -> 1, < 1.25 -> 2, < 1.75 -> 3,
+// < 2.5 -> 4, < 3.5 -> 5, < 5 -> 6, else 7 (sign bit from v < 0, so NaN and
+// -0 give positive codes) on the float's bits: the e2m1 values from 1.0 up
+// (1, 1.5, 2, 3, 4, 6) are the floats with one mantissa bit, so adding half
+// of their spacing (float bit 21) and truncating rounds |v| half up, and
+// (bits >> 22) - 252 numbers them 2..7 (8.0 and above, inf and NaN clamp to
+// 7); the two compares supply codes 1 ([0.25, 0.75)) and 2 ([0.75, 1)).
+// Equal to the chain for all 2^32 float bit patterns (checked exhaustively).
 __device__ __forceinline__ uint32_t fp4_code(float v) {
-  uint32_t sign = 0;
-  if (v < 0.0f) { sign = 8u; v = -v; }
-  const uint32_t c = (v < 0.25f) ? 0u : (v < 0.75f) ? 1u : (v < 1.25f) ? 2u : (v < 1.75f) ? 3u
-                   : (v < 2.5f) ? 4u : (v < 3.5f) ? 5u : (v < 5.0f) ? 6u : 7u;
-  return sign | c;
+  const uint32_t sign = (v < 0.0f) ? 8u : 0u;
+  const uint32_t m = __float_as_uint(v) & 0x7FFFFFFFu;
+  const int low = (int)(m >= 0x3E800000u) + (int)(m >= 0x3F400000u);
+  const int c = min(max((int)((m + 0x00200000u) >> 22) - 252, low), 7);
+  return sign | (uint32_t)c;
+}
+
+// Packed byte (lo in the low nibble) from cvt.rn.satfinite.e2m1x2. Over all
+// 2^32 float inputs it differs from fp4_code only at +-0.25, +-1.25, +-2.5,
+// +-5 (round-to-nearest-even takes the lower neighbour at these ties; the
+// reference thresholds take the upper) and at -0 (sign kept; the reference
+// gives +0); NaN and inf already agree. Callers add +0.0 first (-0 becomes
+// +0, every other value is unchanged) and repair the ties: a tie is a
+// rounding boundary, so the code of the next float up in magnitude (bits + 1)
+// differs from it, and at a tie that code is the reference's. Where the two
+// conversions differ the value is either such a tie or one ulp below a tie
+// that rounds up; only the former has its low 21 bits clear, so those
+// nibbles take the next-up code (fp4_fix_ties). Checked against the
+// thresholds on the device for all 2^32 inputs.
+__device__ __forceinline__ uint32_t fp4x2_cvt(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float fp4_next_up(float x) { return __uint_as_float(__float_as_uint(x) + 1u); }
+
+// o, up: packed codes of x[0..N) and of their next-up floats; returns o with
+// the nibbles of exact ties (low 21 bits clear, finite) taken from up.
+template <int N>
+__device__ __forceinline__ uint32_t fp4_fix_ties(uint32_t o, uint32_t up, const float (&x)[N]) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int e = 0; e < N; e++) {
+    const uint32_t b = __float_as_uint(x[e]);
+    if ((b & 0x1FFFFFu) == 0u && (b & 0x7F800000u) != 0x7F800000u) m |= 0xFu << (4 * e);
+  }
+  return (o & ~m) | (up & m);
 }
 
 template <int SRC>
@@ -680,6 +736,113 @@ fp4_encode_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, in
   }
 }
 
+// FP4 encode in the bulk-copy pipeline of the fp8 encoders: chunks of
+// kEncElems elements (16 or 8 KiB of input) encode to kEncElems / 2 packed
+// bytes; each thread step reads 16 bytes of shared memory (4 f32 or 8 16-bit
+// values) and writes their 2 or 4 packed bytes. Scale options as for
+// encode_bulk_kernel.
+template <int SRC>
+struct Fp4Enc {
+  static constexpr int kEB = SRC == FP8B200_F32 ? 4 : 2;
+  static constexpr int kPer = 16 / kEB;  // elements per thread step
+  static constexpr int kIn = kEncElems * kEB;
+  static constexpr int kOut = kEncElems / 2;
+  static constexpr int kSteps = kEncElems / kPer / kDecThreads;
+  static constexpr int kSmem = kStages * (kIn + kOut) + 64;
+};
+
+template <int SRC>
+__global__ void __launch_bounds__(kDecThreads)
+fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t n,
+                       const float *__restrict__ scale, const uint32_t *__restrict__ amax_bits, float fmax,
+                       float *__restrict__ scale_out) {
+  using C = Fp4Enc<SRC>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint8_t *in_ring = smem_raw;
+  uint8_t *out_ring = in_ring + kStages * C::kIn;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * C::kOut);
+  const int64_t nch = n / kEncElems;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  pdl_launch_dependents();
+  pdl_wait_prior();  // nothing in global memory is read or written before this
+  const bool scaled = scale != nullptr || amax_bits != nullptr;
+  const float s = amax_bits ? scale_from_amax(amax_bits, fmax, scale_out) : scale ? __ldg(scale) : 1.0f;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; i++) {
+      const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
+      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
+    }
+  }
+  __syncthreads();
+  for (int64_t i = 0;; i++) {
+    const int64_t c = blockIdx.x + i * gridDim.x;
+    if (c >= nch) break;
+    const int st = (int)(i % kStages);
+    const uint32_t ph = (uint32_t)((i / kStages) & 1);
+    int timed_out = 0;
+    for (long long k = 0; !mbar_try(smem_addr(bar + st), ph);)
+      if (++k > kBulkSpinLimit) { timed_out = 1; break; }
+    if (__syncthreads_or(timed_out)) {
+      if (threadIdx.x == 0) atomicExch(&g_bulk_status, 1);
+      break;
+    }
+    if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStages - 1) : "memory");
+    __syncthreads();
+    const uint4 *in = reinterpret_cast<const uint4 *>(in_ring + st * C::kIn);
+    uint8_t *out = out_ring + st * C::kOut;
+    const unsigned long long ss = f2pack(s, s);
+#pragma unroll
+    for (int j = 0; j < C::kSteps; j++) {
+      const int idx = threadIdx.x + j * kDecThreads;
+      const uint4 v = in[idx];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      constexpr int NX = C::kPer;  // 4 (f32) or 8 (16-bit) values
+      float x[NX];
+      uint32_t sg;
+#pragma unroll
+      for (int q = 0; q < NX / 2; q++) {
+        float a, b;
+        if constexpr (SRC == FP8B200_F32) { a = u2f(w[2 * q]); b = u2f(w[2 * q + 1]); }
+        else { a = widen<SRC>(w[q] & 0xFFFFu, sg); b = widen<SRC>(w[q] >> 16, sg); }
+        unsigned long long ab = f2pack(a, b);
+        if (scaled) ab = mul_f32x2(ab, ss);
+        f2unpack(add_f32x2(ab, 0ull), a, b);  // + 0.0: -0 -> +0
+        x[2 * q] = a;
+        x[2 * q + 1] = b;
+      }
+      uint32_t o = 0, up = 0;
+#pragma unroll
+      for (int q = 0; q < NX / 2; q++) {
+        o |= fp4x2_cvt(x[2 * q], x[2 * q + 1]) << (8 * q);
+        up |= fp4x2_cvt(fp4_next_up(x[2 * q]), fp4_next_up(x[2 * q + 1])) << (8 * q);
+      }
+      if (o != up) o = fp4_fix_ties<NX>(o, up, x);  // a value at or one ulp below a rounding boundary
+      if constexpr (SRC == FP8B200_F32) reinterpret_cast<uint16_t *>(out)[idx] = (uint16_t)o;
+      else reinterpret_cast<uint32_t *>(out)[idx] = o;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + c * C::kOut),
+                   "r"(smem_addr(out)), "r"(C::kOut)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      const int64_t c2 = blockIdx.x + (i + kStages) * gridDim.x;
+      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + c2 * C::kIn, C::kIn, smem_addr(bar + st));
+    }
+  }
+  if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (blockIdx.x == gridDim.x - 1)
+    for (int64_t p = nch * (kEncElems / 2) + threadIdx.x; p < n / 2; p += kDecThreads) {
+      float lo = load_elem<SRC>(src, 2 * p), hi = load_elem<SRC>(src, 2 * p + 1);
+      if (scaled) { lo = __fmul_rn(lo, s); hi = __fmul_rn(hi, s); }
+      dst[p] = (uint8_t)(fp4_code(lo) | (fp4_code(hi) << 4));
+    }
+}
+
 // ------------------------------------------------------------------ amax / quantize
 // max |x| as float bits (NaN sorts above inf, so a NaN anywhere wins).
 // nunits: 32-byte chunks read vectorised (0 for an unaligned source); the
@@ -691,8 +854,7 @@ amax_kernel(const uint8_t *__restrict__ src, int64_t n, int64_t nunits, uint32_t
   constexpr int PER = 32 / EB;
   uint32_t m = 0, sg;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < nunits; u += nthreads) {
-    const U8x32 a = ld_u256(src + u * 32);
+  auto fold = [&](const U8x32 &a) {
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       if constexpr (EB == 4) m = max(m, f2u(widen<SRC>(a.w[j], sg)) & 0x7FFFFFFFu);
@@ -701,7 +863,16 @@ amax_kernel(const uint8_t *__restrict__ src, int64_t n, int64_t nunits, uint32_t
         m = max(m, f2u(widen<SRC>(a.w[j] >> 16, sg)) & 0x7FFFFFFFu);
       }
     }
+  };
+  int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; u + 3 * nthreads < nunits; u += 4 * nthreads) {  // four 32-byte loads in flight per thread
+    U8x32 a[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) a[k] = ld_u256(src + (u + k * nthreads) * 32);
+#pragma unroll
+    for (int k = 0; k < 4; k++) fold(a[k]);
   }
+  for (; u < nunits; u += nthreads) fold(ld_u256(src + u * 32));
   for (int64_t i = nunits * PER + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nthreads)
     m = max(m, f2u(load_elem<SRC>(src, i)) & 0x7FFFFFFFu);
   m = __reduce_max_sync(0xFFFFFFFFu, m);
@@ -1114,34 +1285,50 @@ void launch_decode(const void *src, void *dst, int64_t nbytes, int fmt, int odt,
              odt, scale, mode);
 }
 
+// amax_bits (per-tensor quantisation): the kernel derives the scale from the
+// amax and publishes it to scale_out; the bulk path only (callers check
+// alignment first).
 template <int SRC, int FMT>
-void launch_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+void launch_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st,
+                   const uint32_t *amax_bits = nullptr, float fmax = 0.0f, float *scale_out = nullptr) {
   if (aligned16(src) && aligned16(dst)) {
     constexpr int smem = Enc<SRC>::kSmem;
     const int per_sm = resident_per_sm((const void *)encode_bulk_kernel<SRC, FMT>, smem, kDecThreads);
     const int64_t nch = n / kEncElems;
     const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)current_sm_count() * per_sm));
-    launch_pdl(encode_bulk_kernel<SRC, FMT>, g, kDecThreads, smem, st, (const uint8_t *)src, (uint8_t *)dst, n, scale);
+    launch_pdl(encode_bulk_kernel<SRC, FMT>, g, kDecThreads, smem, st, (const uint8_t *)src, (uint8_t *)dst, n, scale,
+               amax_bits, fmax, scale_out);
   } else {  // unaligned: element-wise (the kernel's scalar loop)
     const int g = grid_for(std::max<int64_t>(n, 1), kThreads, resident_per_sm((const void *)encode_kernel<SRC, FMT>, 0));
     encode_kernel<SRC, FMT><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, n, 0, scale);
   }
 }
 
-void launch_encode_any(int sdt, int fmt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+void launch_encode_any(int sdt, int fmt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st,
+                       const uint32_t *amax_bits = nullptr, float fmax = 0.0f, float *scale_out = nullptr) {
   if (fmt == FP8B200_E4M3) {
-    if (sdt == FP8B200_F32) launch_encode<FP8B200_F32, FP8B200_E4M3>(src, dst, n, scale, st);
-    else if (sdt == FP8B200_BF16) launch_encode<FP8B200_BF16, FP8B200_E4M3>(src, dst, n, scale, st);
-    else launch_encode<FP8B200_F16, FP8B200_E4M3>(src, dst, n, scale, st);
+    if (sdt == FP8B200_F32) launch_encode<FP8B200_F32, FP8B200_E4M3>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
+    else if (sdt == FP8B200_BF16) launch_encode<FP8B200_BF16, FP8B200_E4M3>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
+    else launch_encode<FP8B200_F16, FP8B200_E4M3>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
   } else {
-    if (sdt == FP8B200_F32) launch_encode<FP8B200_F32, FP8B200_E5M2>(src, dst, n, scale, st);
-    else if (sdt == FP8B200_BF16) launch_encode<FP8B200_BF16, FP8B200_E5M2>(src, dst, n, scale, st);
-    else launch_encode<FP8B200_F16, FP8B200_E5M2>(src, dst, n, scale, st);
+    if (sdt == FP8B200_F32) launch_encode<FP8B200_F32, FP8B200_E5M2>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
+    else if (sdt == FP8B200_BF16) launch_encode<FP8B200_BF16, FP8B200_E5M2>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
+    else launch_encode<FP8B200_F16, FP8B200_E5M2>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
   }
 }
 
 template <int SRC>
-void launch_fp4_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
+void launch_fp4_encode(const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st,
+                       const uint32_t *amax_bits = nullptr, float fmax = 0.0f, float *scale_out = nullptr) {
+  if (aligned16(src) && aligned16(dst)) {
+    constexpr int smem = Fp4Enc<SRC>::kSmem;
+    const int per_sm = resident_per_sm((const void *)fp4_encode_bulk_kernel<SRC>, smem, kDecThreads);
+    const int64_t nch = n / kEncElems;
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)current_sm_count() * per_sm));
+    launch_pdl(fp4_encode_bulk_kernel<SRC>, g, kDecThreads, smem, st, (const uint8_t *)src, (uint8_t *)dst, n, scale,
+               amax_bits, fmax, scale_out);
+    return;
+  }
   const int64_t npairs = n / 2;
   const int64_t nunits = (aligned32(src) && aligned16(dst)) ? n / 32 : 0;
   const int g = grid_for(std::max<int64_t>(nunits ? nunits : npairs, 1), kThreads,
@@ -1149,10 +1336,11 @@ void launch_fp4_encode(const void *src, void *dst, int64_t n, const float *scale
   fp4_encode_kernel<SRC><<<g, kThreads, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, npairs, nunits, scale);
 }
 
-void launch_fp4_encode_any(int sdt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st) {
-  if (sdt == FP8B200_F32) launch_fp4_encode<FP8B200_F32>(src, dst, n, scale, st);
-  else if (sdt == FP8B200_BF16) launch_fp4_encode<FP8B200_BF16>(src, dst, n, scale, st);
-  else launch_fp4_encode<FP8B200_F16>(src, dst, n, scale, st);
+void launch_fp4_encode_any(int sdt, const void *src, void *dst, int64_t n, const float *scale, cudaStream_t st,
+                           const uint32_t *amax_bits = nullptr, float fmax = 0.0f, float *scale_out = nullptr) {
+  if (sdt == FP8B200_F32) launch_fp4_encode<FP8B200_F32>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
+  else if (sdt == FP8B200_BF16) launch_fp4_encode<FP8B200_BF16>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
+  else launch_fp4_encode<FP8B200_F16>(src, dst, n, scale, st, amax_bits, fmax, scale_out);
 }
 
 bool is_float_dtype(int dt) { return dt == FP8B200_F32 || dt == FP8B200_BF16 || dt == FP8B200_F16; }
@@ -1168,8 +1356,11 @@ int check_scale_mode(int mode, const float *scale, int odt) {
   return FP8B200_OK;
 }
 
+// Per-tensor quantisation, first half: clear the scratch and reduce max|x|
+// into it; with `with_scale` also run the one-thread scale kernel (for the
+// element-wise encoders; the bulk encoders derive the scale themselves).
 int launch_amax_and_scale(const void *src, int src_dtype, int64_t n, float fmax, float *scale_out,
-                          uint32_t *amax_scratch, cudaStream_t st) {
+                          uint32_t *amax_scratch, cudaStream_t st, bool with_scale = true) {
   if (cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t), st) != cudaSuccess)
     return check_launch("quantize amax clear");
   if (n > 0) {
@@ -1183,6 +1374,7 @@ int launch_amax_and_scale(const void *src, int src_dtype, int64_t n, float fmax,
     count_launch();
     if (int rc = check_launch("quantize amax")) return rc;
   }
+  if (!with_scale) return FP8B200_OK;
   quant_scale_kernel<<<1, 1, 0, st>>>(amax_scratch, fmax, scale_out);
   count_launch();
   return check_launch("quantize scale");
@@ -1263,9 +1455,11 @@ extern "C" int fp8b200_quantize_fp8(const void *src, int src_dtype, void *dst, i
   if (int rc = check_device(&dev)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   const float fmax = fp8_dtype == FP8B200_E4M3 ? 448.0f : 57344.0f;
-  if (int rc = launch_amax_and_scale(src, src_dtype, n, fmax, scale_out, amax_scratch, st)) return rc;
+  const bool bulk = n > 0 && aligned16(src) && aligned16(dst);  // the encoder derives the scale from the amax
+  if (int rc = launch_amax_and_scale(src, src_dtype, n, fmax, scale_out, amax_scratch, st, !bulk)) return rc;
   if (n > 0) {
-    launch_encode_any(src_dtype, fp8_dtype, src, dst, n, scale_out, st);
+    if (bulk) launch_encode_any(src_dtype, fp8_dtype, src, dst, n, nullptr, st, amax_scratch, fmax, scale_out);
+    else launch_encode_any(src_dtype, fp8_dtype, src, dst, n, scale_out, st);
     count_launch();
     return check_launch("quantize encode");
   }
@@ -1294,9 +1488,11 @@ extern "C" int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, i
   int dev;
   if (int rc = check_device(&dev)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  if (int rc = launch_amax_and_scale(src, src_dtype, n, 6.0f, scale_out, amax_scratch, st)) return rc;
+  const bool bulk = n > 0 && aligned16(src) && aligned16(dst);  // the encoder derives the scale from the amax
+  if (int rc = launch_amax_and_scale(src, src_dtype, n, 6.0f, scale_out, amax_scratch, st, !bulk)) return rc;
   if (n > 0) {
-    launch_fp4_encode_any(src_dtype, src, dst, n, scale_out, st);
+    if (bulk) launch_fp4_encode_any(src_dtype, src, dst, n, nullptr, st, amax_scratch, 6.0f, scale_out);
+    else launch_fp4_encode_any(src_dtype, src, dst, n, scale_out, st);
     count_launch();
     return check_launch("fp4 quantize encode");
   }

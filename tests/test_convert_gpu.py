@@ -253,7 +253,7 @@ def test_fp4_aten_routes(nat):
     assert torch.equal(dst.view(torch.uint8), f4.view(torch.uint8))
 
 
-@pytest.mark.parametrize("n", [2, 30, 32, 34, 100002])
+@pytest.mark.parametrize("n", [2, 30, 32, 34, 100002, 4096 * 300 + 4098])
 @pytest.mark.parametrize("sdt", [0, 1, 2])
 def test_fp4_encode_reference_thresholds(nat, n, sdt):
     special = np.array([0.0, -0.0, 0.24, 0.25, 0.74, 0.75, 1.25, 1.74, 1.75, 2.49, 2.5, 3.49, 3.5,
@@ -265,13 +265,60 @@ def test_fp4_encode_reference_thresholds(nat, n, sdt):
     assert np.array_equal(enc, O.fp4_encode_ref(x.float().numpy()))
 
 
-def test_fp4_quantize_matches_reference_formula(nat):
-    x = torch.randn(4098, generator=torch.Generator().manual_seed(5)) * 3
+@pytest.mark.parametrize("n", [4098, (1 << 20) + 6])
+@pytest.mark.parametrize("sdt", [0, 1, 2])
+def test_fp4_quantize_matches_reference_formula(nat, n, sdt):
+    x = (torch.randn(n, generator=torch.Generator().manual_seed(5)) * 3).to(OUT[sdt])
     enc, inv = torch.ops.fp8_mps.fp4_quantize(x.cuda())
-    amax = x.abs().max().item()
+    xf = x.float()
+    amax = xf.abs().max().item()
     scale = 6.0 / amax
-    assert np.array_equal(enc.cpu().numpy(), O.fp4_encode_ref(x.numpy(), scale))
-    assert inv.item() == np.float32(1.0 / scale) and enc.shape == (2049,)
+    assert np.array_equal(enc.cpu().numpy(), O.fp4_encode_ref(xf.numpy(), scale))
+    assert inv.item() == np.float32(1.0 / scale) and enc.shape == (n // 2,)
+
+
+@pytest.mark.parametrize("sdt", [1, 2])
+def test_fp4_encode_every_16bit_pattern(nat, sdt):
+    """All 65536 bf16 / f16 bit patterns (NaNs, infs, signed zeros,
+    subnormals), unscaled and scaled, against the reference thresholds."""
+    x = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(OUT[sdt])
+    for scale in (None, 0.37):
+        dev = x.cuda()
+        out = torch.empty(32768, dtype=torch.uint8, device="cuda")
+        sc = None if scale is None else torch.tensor([scale], dtype=torch.float32, device="cuda")
+        from fp4_fp8_for_torch_mps import _lib as L
+        L.check(L.lib().fp8b200_encode_fp4(dev.data_ptr(), sdt, out.data_ptr(), 65536,
+                                           None if sc is None else sc.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream), "fp4 encode")
+        assert np.array_equal(out.cpu().numpy(), O.fp4_encode_ref(x.float().numpy(), scale)), scale
+
+
+def test_fp4_encode_every_f32_pattern(nat):
+    """All 2^32 float bit patterns, in 16 slices, against the reference
+    thresholds (the bulk encoder converts with cvt.rn.satfinite.e2m1x2 and
+    falls back to the thresholds for the inputs where the two differ)."""
+    out = torch.empty(1 << 27, dtype=torch.uint8, device="cuda")
+    from fp4_fp8_for_torch_mps import _lib as L
+    for k in range(16):
+        lo = k << 28
+        bits = np.arange(lo, lo + (1 << 28), dtype=np.uint64).astype(np.uint32)
+        dev = torch.arange(lo, lo + (1 << 28), dtype=torch.int64, device="cuda").to(torch.int32)
+        L.check(L.lib().fp8b200_encode_fp4(dev.data_ptr(), 0, out.data_ptr(), 1 << 28, None,
+                                           torch.cuda.current_stream().cuda_stream), "fp4 encode")
+        assert np.array_equal(out.cpu().numpy(), O.fp4_encode_ref(bits.view(np.float32))), hex(lo)
+
+
+def test_fp4_encode_f32_near_every_threshold(nat):
+    """f32 values within 4096 ulps of each threshold (0.25 ... 5) and of the
+    e2m1 values, both signs, plus 2^22 random bit patterns."""
+    marks = np.array([0.25, 0.5, 0.75, 1.0, 1.25, 1.5, 1.75, 2.0, 2.5, 3.0, 3.5, 4.0, 5.0, 6.0, 8.0], np.float32)
+    near = (marks.view(np.uint32)[:, None] + np.arange(-4096, 4096, dtype=np.int64)[None, :]).astype(np.uint32)
+    rnd = np.random.default_rng(9).integers(0, 1 << 32, size=1 << 22, dtype=np.uint64).astype(np.uint32)
+    bits = np.concatenate([near.reshape(-1), near.reshape(-1) | np.uint32(0x80000000), rnd])
+    bits = bits[: bits.size // 2 * 2]
+    x = torch.from_numpy(bits.view(np.int32).copy()).view(torch.float32)
+    enc = torch.ops.fp8_mps.fp4_encode(x.cuda()).cpu().numpy()
+    assert np.array_equal(enc, O.fp4_encode_ref(bits.view(np.float32)))
 
 
 # ---------------------------------------------------------------- per-row quantize
