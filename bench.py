@@ -737,7 +737,9 @@ class LinearFp8W:
     """FP8-weight linear with dequant-on-load: y = x @ (w * s)^T, x bf16
     (M, K) N(0,1), w e4m3 quantised per output channel from N(0, 0.02),
     Llama shapes (N, K from --shape, M from --m, default 16384). Compute in
-    bf16 on the tensor cores: the roofline peak is the measured bf16 rate."""
+    bf16 on the tensor cores: the roofline peak is the measured bf16 rate;
+    for M <= 256 the weight bytes bound it and the line reports GB/s (weights
+    + x + y) against HBM."""
     name = "linear_fp8w"
     metric = "linear_fp8w_TFLOPS"
     unit, bound, kernels_per_step = "TFLOP/s", "tensor_bf16", 1
@@ -764,6 +766,9 @@ class LinearFp8W:
         self.i = 0
         self.out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
         self.work = 2.0 * M * N * K
+        if M <= 256:  # decode-sized M: the weight bytes bound it, so report bytes against HBM
+            self.metric, self.unit, self.bound = "linear_fp8w_GBps", "GB/s", "hbm"
+            self.work = float(N * K + M * K * 2 + M * N * 2)
         self.h2d, self.d2h = M * K * 2, M * N * 2
         self.config = {"workload": self.name, "M": M, "N": N, "K": K, "weights": "e4m3, per-channel scale",
                        "activations": "bf16", "out": "bf16",
@@ -804,16 +809,20 @@ class LinearFp8W:
         return bool(np.all(np.abs(got - ref) <= O.bf16_ulp(ref) + 2.0 ** -20 * S))
 
     def cpu_run(self, reps=1):
-        """float32 matmul of a 256-row slice against the dequantised weights (CPU torch)."""
+        """float32 matmul of a (at most) 256-row slice against the dequantised
+        weights (CPU torch); in GB/s of the step's bytes for M <= 256."""
         threads = torch.get_num_threads()
         W = self.w_host.float() * self.s_host.reshape(-1, 1)
-        A = self.x_host[:256].float()
+        rows = min(256, self.M)
+        A = self.x_host[:rows].float()
         t0 = time.perf_counter()
         for _ in range(reps):
             (A @ W.t()).to(torch.bfloat16)
         dt = (time.perf_counter() - t0) / reps
-        return 2.0 * 256 * self.N * self.K / dt / 1e12, threads, \
-            f"256x{self.N}x{self.K} f32 matmul, weights dequantised beforehand (CPU torch, {threads} threads)"
+        sample = f"{rows}x{self.N}x{self.K} f32 matmul, weights dequantised beforehand (CPU torch, {threads} threads)"
+        if self.M <= 256:
+            return (self.N * self.K + rows * self.K * 2 + rows * self.N * 2) / dt / 1e9, threads, sample
+        return 2.0 * rows * self.N * self.K / dt / 1e12, threads, sample
 
 
 class LlamaFp8:
@@ -952,12 +961,12 @@ def reference_line(args):
         from fp4_fp8_for_torch_mps.workloads import ROWWISE_SHAPES, rowwise_operands
         _, N, K = ROWWISE_SHAPES[args.shape]
         M = args.m or 16384
-        w.x_host = torch.randn(256, K, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+        w.x_host = torch.randn(min(256, M), K, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
         _, w.w_host, _, sw = rowwise_operands(1, N, K)
         w.s_host = sw.reshape(-1)
-        w.N, w.K = N, K
+        w.M, w.N, w.K = M, N, K
         vals = [w.cpu_run() for _ in range(max(args.steps, 1))]
-        unit, metric = "TFLOP/s", "linear_fp8w_TFLOPS"
+        unit, metric = ("GB/s", "linear_fp8w_GBps") if M <= 256 else ("TFLOP/s", "linear_fp8w_TFLOPS")
         config = {"workload": args.workload, "M": M, "N": N, "K": K, "out": "bf16"}
     elif args.workload == "scaled_mm_small_m":
         w = ScaledMMSmallM.__new__(ScaledMMSmallM)

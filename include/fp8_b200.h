@@ -215,9 +215,11 @@ int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda,
  * w: N x K float8 weight codes, row stride ldw bytes (multiple of 16); x and w
  * 16-byte aligned. w_scale: one float (FP8B200_SCALE_TENSOR) or N floats, one
  * per output channel (FP8B200_SCALE_ROWWISE); bias: N values or NULL.
- * The weights are converted to x's type inside shared memory (exact) and the
- * products are accumulated in float32 on the tensor cores (kind::f16); the
- * scale and bias are applied to the float32 sums.
+ * The weights are converted to x's type (exact) and the products are
+ * accumulated in float32 on the tensor cores; the scale and bias are applied
+ * to the float32 sums. M <= 16 with K a multiple of 128: weights converted in
+ * registers for warp-level m16n8k16 MMAs, K split over a cluster; otherwise
+ * converted in shared memory for tcgen05 kind::f16 MMAs.
  * Replaces the reference's dequantise-then-matmul path: fp8_scaled_mm_fast
  * (fp8_mps_native.py:129-159), which decodes both operands to f16 and calls
  * an MPS f16 matmul, for the case where only the weights are float8.
@@ -266,6 +268,8 @@ int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
  * SMs idle in the last wave; else the single-CTA kernel with 128x256 tiles),
  * 1 = always single-CTA, 2 = always CTA-pair 256x256, 3 = always small-M
  * (tiles of 256 rows of A when M > 256), 4 = always CTA-pair 256x512.
+ * Path 3 also sends fp8b200_linear_fp8w calls with M <= 16 to its tcgen05
+ * small-M kernel instead of the warp-level MMA kernel.
  * Process-wide; for tests and tuning.
  */
 int fp8b200_gemm_set_path(int path);

@@ -1807,6 +1807,196 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
   return FP8B200_OK;
 }
 
+// ------------------------------------------------------------------ few-row float8-weight linear
+// For M <= 16 activation rows the float8-weight linear is a matrix-vector
+// product bound by the weight bytes: every weight is used by at most 16
+// rows, so the tcgen05 path's shared-memory hand-off of converted weights
+// costs more than the math. This kernel converts weights in registers and
+// feeds them straight to the warp-level tensor-core instruction
+// mma.sync.m16n8k16 computing D^T = W x^T: 16 weight rows as the A operand,
+// 8 x rows as B (NT = 1 or 2 tiles, zero rows past M), float32 accumulators.
+//   CTA: 4 warps, 64 output channels (16 weight rows per warp);
+//   cluster: ks CTAs splitting K, partial sums reduced through distributed
+//   shared memory (each CTA reduces and stores 64 / ks columns), so no
+//   global scratch and a fixed summation order.
+//   k-loop: 128-value blocks; lane (g, t) copies 32 weight bytes of rows g
+//   and 8 + g per block into a GV_STAGES-deep shared-memory ring with
+//   cp.async (its own slots only, so no barrier), and reads 32 x values of
+//   x row g (and g + 8) with read-only loads (the x rows are shared by every
+//   warp and CTA of a column and stay in L1 / L2). Within a block the lane's
+//   32 physical k positions 32t .. 32t+31 are the logical positions {2t,
+//   2t+1, 2t+8, 2t+9} of eight consecutive m16n8k16 steps (four positions
+//   per step), the same permutation for A and B, which leaves the sum
+//   unchanged, and makes both operands' register pairs come straight from
+//   the conversions and the 16-byte loads.
+constexpr int GV_WARPS = 4;
+constexpr int GV_BN = 16 * GV_WARPS;  // 64 output channels per CTA
+constexpr int GV_BK = 128;
+constexpr int GV_STAGES = 4;  // weight blocks in flight per lane (cp.async ring)
+
+template <int WF, bool F16>
+__device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o)[16]) {
+  const uint32_t q[2][4] = {{raw[0].x, raw[0].y, raw[0].z, raw[0].w}, {raw[1].x, raw[1].y, raw[1].z, raw[1].w}};
+  if ((fp8_unit_special<WF, F16>(q[0]) | fp8_unit_special<WF, F16>(q[1])) == 0u) {
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        o[8 * h + 2 * i] = fp8x2_fast<WF, F16>(q[h][i], 0x4140u, 0x1404u);
+        o[8 * h + 2 * i + 1] = fp8x2_fast<WF, F16>(q[h][i], 0x4342u, 0x3424u);
+      }
+  } else {  // NaN / inf codes: conversion instructions
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t lo = fp8x2_to_f16x2<WF>(q[h][i] & 0xFFFFu), hi = fp8x2_to_f16x2<WF>(q[h][i] >> 16);
+        o[8 * h + 2 * i] = F16 ? lo : f16x2_to_bf16x2(lo);
+        o[8 * h + 2 * i + 1] = F16 ? hi : f16x2_to_bf16x2(hi);
+      }
+  }
+}
+
+template <bool F16>
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  if constexpr (F16)
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int WF, bool F16, int NT>  // NT: 8-row tiles of x (1 for M <= 8, 2 for M <= 16)
+__global__ void __launch_bounds__(32 * GV_WARPS)
+linear_fp8w_gemv_kernel(const uint16_t *__restrict__ x, int64_t ldx, const uint8_t *__restrict__ w, int64_t ldw,
+                        int M, int N, int kslice, const Params p) {
+  extern __shared__ __align__(16) uint8_t gv_smem[];
+  const uint32_t ring = smem_u32(gv_smem);  // GV_STAGES x GV_WARPS x 2 KiB of raw weights
+  float *part = reinterpret_cast<float *>(gv_smem + GV_STAGES * GV_WARPS * 2048);  // [16][GV_BN]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t rank = cluster_rank(), ks = p.sk_cs;
+  const int n0 = blockIdx.y * GV_BN;
+  const int64_t k0 = (int64_t)rank * kslice;
+  const int nblk = kslice / GV_BK;
+
+  // this lane's weight rows: channel n0 + 16 warp + 8 h + g, h = 0, 1; its 32 bytes of each
+  // 128-value block land in the ring at chunk i = 2h + half: warp slot + i * 512 + lane * 16, so
+  // that the lane reads back exactly what it copied (no barrier) and a warp's 16-byte reads of
+  // one chunk are contiguous
+  const uint8_t *wrow[2];
+  uint32_t wbytes[2];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int n = n0 + 16 * warp + 8 * h + g;
+    wbytes[h] = n < N ? 16u : 0u;
+    wrow[h] = w + (int64_t)(n < N ? n : 0) * ldw + k0 + 32 * t;
+  }
+  const uint32_t slot = ring + (uint32_t)(warp * 2048 + lane * 16);
+  auto issue = [&](int kb) {
+    if (kb < nblk) {
+      const uint32_t st = slot + (uint32_t)((kb % GV_STAGES) * GV_WARPS * 2048);
+#pragma unroll
+      for (int c = 0; c < 4; c++) cp_async16(st + c * 512, wrow[c >> 1] + (int64_t)kb * GV_BK + 16 * (c & 1), wbytes[c >> 1]);
+    }
+    cp_async_commit();  // one group per block, empty past the end, so the wait count stays uniform
+  };
+#pragma unroll
+  for (int s = 0; s < GV_STAGES - 1; s++) issue(s);
+
+  // D^T = W x^T per warp: the warp's 16 weight rows are the m16n8k16 A operand (rows g, g + 8),
+  // x rows the 8-column B operand (NT tiles: rows 0-7, 8-15). A lane needs x row g (+ 8).
+  float acc[NT][4] = {};
+  const uint4 *xr[NT];
+  bool xin[NT];
+#pragma unroll
+  for (int u = 0; u < NT; u++) {
+    xin[u] = 8 * u + g < M;
+    xr[u] = reinterpret_cast<const uint4 *>(x + (xin[u] ? (int64_t)(8 * u + g) * ldx : 0) + k0 + 32 * t);
+  }
+#pragma unroll 1
+  for (int kb = 0; kb < nblk; kb++) {
+    issue(kb + GV_STAGES - 1);
+    cp_async_wait<GV_STAGES - 1>();  // this lane's block kb has landed
+    uint4 raw[2][2];
+    const uint32_t st = slot + (uint32_t)((kb % GV_STAGES) * GV_WARPS * 2048);
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(raw[c >> 1][c & 1].x), "=r"(raw[c >> 1][c & 1].y), "=r"(raw[c >> 1][c & 1].z),
+                     "=r"(raw[c >> 1][c & 1].w)
+                   : "r"(st + c * 512));
+    uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
+#pragma unroll
+    for (int u = 0; u < NT; u++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) {
+        const uint4 q = xin[u] ? __ldg(xr[u] + kb * (GV_BK / 8) + v) : make_uint4(0, 0, 0, 0);
+        xv[u][4 * v] = q.x; xv[u][4 * v + 1] = q.y; xv[u][4 * v + 2] = q.z; xv[u][4 * v + 3] = q.w;
+      }
+    uint32_t wv[2][16];  // weight rows g and g + 8 converted: the A operand pairs
+    gv_convert32<WF, F16>(raw[0], wv[0]);
+    gv_convert32<WF, F16>(raw[1], wv[1]);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int u = 0; u < NT; u++)
+        mma_16816<F16>(acc[u], wv[0][2 * j], wv[1][2 * j], wv[0][2 * j + 1], wv[1][2 * j + 1], xv[u][2 * j],
+                       xv[u][2 * j + 1]);
+  }
+  cp_async_wait<0>();
+
+  // partial sums part[x row][channel] (rows < 8 NT, all written): acc[u] = D^T rows (channels)
+  // g / g + 8, columns (x rows) 8u + 2t (+1)
+#pragma unroll
+  for (int u = 0; u < NT; u++) {
+    const int ch = 16 * warp + g, xrow = 8 * u + 2 * t;
+    part[xrow * GV_BN + ch] = acc[u][0];
+    part[(xrow + 1) * GV_BN + ch] = acc[u][1];
+    part[xrow * GV_BN + ch + 8] = acc[u][2];
+    part[(xrow + 1) * GV_BN + ch + 8] = acc[u][3];
+  }
+  cluster_sync();  // every CTA's partial sums are complete
+  // this CTA reduces and stores columns [rank * cw, (rank + 1) * cw) of the 64
+  const int cw = GV_BN / (int)ks;
+  const uint32_t part_addr = smem_u32(part);
+  for (int i = threadIdx.x; i < M * cw; i += 32 * GV_WARPS) {
+    const int m = i / cw, col = (int)rank * cw + (i - m * cw);
+    const int n = n0 + col;
+    float v = 0.f;
+    for (uint32_t q = 0; q < ks; q++) {
+      float pv;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv)
+                   : "r"(map_to_rank(part_addr + (uint32_t)((m * GV_BN + col) * 4), q)));
+      v += pv;
+    }
+    if (n < N) {
+      const float cs = p.sb_rowwise ? __ldg(p.sb + n) : __ldg(p.sb);
+      const float bb = p.bias ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
+      v = v * cs + bb;
+      char *d = reinterpret_cast<char *>(p.D);
+      const int64_t off = (int64_t)m * p.ldd + n;
+      if (p.out_dtype == FP8B200_F32) reinterpret_cast<float *>(d)[off] = v;
+      else if (p.out_dtype == FP8B200_BF16) reinterpret_cast<__nv_bfloat16 *>(d)[off] = __float2bfloat16_rn(v);
+      else reinterpret_cast<__half *>(d)[off] = __float2half_rn(v);
+    }
+  }
+  cluster_sync();  // no CTA leaves while a peer may still read its partial sums
+}
+
 unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
 int g_debug_skip_first_load = 0;
 int g_path = 0;  // 0 = by shape, 1 = single-CTA, 2 = CTA-pair 256x256, 3 = small-M, 4 = CTA-pair 256x512
@@ -2108,6 +2298,62 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     cudaError_t e = cudaFuncSetAttribute(linear_fp8w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LW_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
+  }
+  if (M <= 16 && K % GV_BK == 0 && g_path != 3) {
+    // very few rows: weights converted in registers for warp-level MMAs, K
+    // split over a cluster of ks CTAs (enough CTAs to cover the GPU a few
+    // times over, each K slice a multiple of the 128-value block and small
+    // enough for its staged x rows)
+    const int64_t nb = (N + GV_BN - 1) / GV_BN;
+    int ks = 1;
+    const int64_t ring = GV_STAGES * GV_WARPS * 2048;
+    while (ks < 8 && K % (GV_BK * 2 * ks) == 0 && nb * ks < 4LL * current_sm_count()) ks *= 2;
+    const int64_t kslice = K / ks;
+    const int64_t smem = ring + 16 * GV_BN * 4;
+    if (smem <= 200 * 1024 && nb <= 65535) {
+      Params p;
+      memset(&p, 0, sizeof(p));
+      p.M = (int)M; p.N = (int)N; p.K = (int)K;
+      p.sb = w_scale; p.sb_rowwise = w_scale_layout == FP8B200_SCALE_ROWWISE;
+      p.bias = bias; p.bias_dtype = bias_dtype;
+      p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
+      p.sk_cs = ks;
+      const bool f16 = x_dtype == FP8B200_F16;
+      using GvKernel = void (*)(const uint16_t *, int64_t, const uint8_t *, int64_t, int, int, int, const Params);
+      static const GvKernel kernels[8] = {
+          linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 1>, linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 2>,
+          linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 1>,  linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 2>,
+          linear_fp8w_gemv_kernel<FP8B200_E5M2, false, 1>, linear_fp8w_gemv_kernel<FP8B200_E5M2, false, 2>,
+          linear_fp8w_gemv_kernel<FP8B200_E5M2, true, 1>,  linear_fp8w_gemv_kernel<FP8B200_E5M2, true, 2>};
+      const int ki = (w_dtype == FP8B200_E4M3 ? 0 : 4) + (f16 ? 2 : 0) + (M > 8 ? 1 : 0);
+      const GvKernel kern = kernels[ki];
+      {  // dynamic shared-memory limit per kernel, only ever raised
+        static std::mutex mu;
+        static int limit[8][64] = {};
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 64 && limit[ki][dev] < smem) {
+          cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
+          limit[ki][dev] = (int)smem;
+        }
+      }
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)ks;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3((unsigned)ks, (unsigned)nb, 1);
+      cfg.blockDim = dim3(32 * GV_WARPS, 1, 1);
+      cfg.dynamicSmemBytes = (size_t)smem;
+      cfg.stream = (cudaStream_t)stream;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaLaunchKernelEx(&cfg, kern, (const uint16_t *)x, (int64_t)ldx, (const uint8_t *)w, (int64_t)ldw, (int)M,
+                         (int)N, (int)kslice, p);
+      count_launch();
+      return check_launch("linear_fp8w");
+    }
   }
   if (M <= SK_MAX_MT) {
     // few rows: the small-M kernel with weights dequantised on load (128

@@ -170,3 +170,74 @@ def test_gemm_16bit(nat, dt, odt, M, N, K):
     r = (av @ bv.T) * sv[None, :] + bb[None, :]
     S = (np.abs(av) @ np.abs(bv).T) * sv[None, :] + np.abs(bb)[None, :] * 2.0 ** -4
     check(out, r, S, f"gemm_16bit {dt} {odt} {M}x{N}x{K}")
+
+
+# ---------------------------------------------------------------- M <= 16, K % 128 == 0: register-converted path
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 14336, 4096), (3, 4096, 14336), (5, 300, 256),
+                                   (16, 64, 128), (8, 1000, 1408), (2, 65, 2048)])
+def test_few_rows_shapes(nat, M, N, K):
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = rand_w((N, K), E4, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    r, S = reference(x, w, s)
+    check(out, r, S, f"few rows {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("wdt", [E4, E5])
+@pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("bias_dt", [None, torch.float16])
+def test_few_rows_dtypes_scales_bias(nat, xdt, wdt, odt, bias_dt):
+    M, N, K = 7, 200, 384
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(M, K, generator=g) * 2).to(xdt)
+    w = rand_w((N, K), wdt, g)
+    s = torch.tensor(0.0071) if bias_dt is None else torch.rand(N, generator=g) * 0.01 + 1e-3
+    bias = None if bias_dt is None else (torch.randn(N, generator=g) * 5).to(bias_dt)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda(), None if bias is None else bias.cuda(), out_dtype=odt)
+    r, S = reference(x, w, s, bias)
+    check(out, r, S, f"few rows {xdt} {wdt} {odt} bias={bias_dt}")
+
+
+@pytest.mark.parametrize("wdt", [E4, E5])
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
+def test_few_rows_every_finite_weight_code(nat, wdt, xdt):
+    """Every finite code in every k position, picked out exactly by one-hot x
+    rows, 16 rows at a time: the in-register conversion is exact."""
+    codes = torch.arange(256, dtype=torch.uint8)
+    finite = codes[torch.isfinite(codes.view(wdt).float())]
+    K = 128
+    w = finite.repeat(256 * K // finite.numel() + 1)[: 256 * K].reshape(256, K).view(wdt)
+    eye = torch.eye(K, dtype=xdt)
+    for k0 in range(0, K, 16):
+        out = nat.fp8_linear(eye[k0:k0 + 16].cuda(), w.cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32)
+        assert torch.equal(out.cpu(), w.float().T[k0:k0 + 16]), k0
+
+
+def test_few_rows_nan_weight_propagates(nat):
+    x = torch.ones(4, 128, dtype=torch.bfloat16)
+    w = torch.zeros(256, 128, dtype=torch.uint8)
+    w[3, 5] = 0x7F                                          # e4m3 NaN
+    out = nat.fp8_linear(x.cuda(), w.view(E4).cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32).cpu()
+    assert torch.isnan(out[:, 3]).all() and not torch.isnan(out[:, [0, 1, 2, 4]]).any()
+
+
+def test_few_rows_matches_tensor_core_path(nat):
+    """The register-converted path and the tcgen05 small-M path (forced) agree
+    within the tolerance on the same inputs."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(9, 2048, generator=g).to(torch.bfloat16)
+    w = rand_w((1536, 2048), E4, g)
+    s = torch.rand(1536, generator=g) * 0.01 + 1e-3
+    r, S = reference(x, w, s)
+    a = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    L.lib().fp8b200_gemm_set_path(3)
+    try:
+        b = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    finally:
+        L.lib().fp8b200_gemm_set_path(0)
+    check(a, r, S, "register-converted")
+    check(b, r, S, "tcgen05 small-M")
