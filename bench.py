@@ -859,9 +859,41 @@ class LlamaFp8:
         self.h_in = self.x_host.pin_memory()
         self.h_out = torch.empty_like(self.x_host).pin_memory()
         self.gemm_flops = self.model.gemm_flops(t)
+        from fp4_fp8_for_torch_mps import _lib as L
+        self.L = L
+        self.eager = bool(getattr(args, "eager", False))
 
     def step(self):
         self.y = self.model.forward(self.x, self.batch, self.seq)
+
+    graph = None
+    graph_launches = 0
+
+    def capture(self, steps):
+        """The forward pass (32 layers, ~500 kernels) captured once as a CUDA
+        graph; each timed step replays it, so no host dispatch gap sits
+        between kernels. Every kernel of the eager step runs in the replay."""
+        self.steps = steps
+        if getattr(self, "eager", False):
+            return
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = self.L.launch_count()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(self.graph, stream=side):
+                self.y = self.model.forward(self.x, self.batch, self.seq)
+        self.per_forward = self.L.launch_count() - n0
+        self.graph_launches = self.per_forward * steps
+        torch.cuda.synchronize()
+        self.config["launch"] = "forward pass captured once as a CUDA graph, replayed per step"
+
+    def replay(self):
+        for _ in range(self.steps):
+            if self.graph is None:
+                self.step()
+            else:
+                self.graph.replay()
 
     def e2e_step(self):
         x = self.h_in.to("cuda", non_blocking=True)
@@ -1013,6 +1045,8 @@ def main():
                     help="fp8_roundtrip: elements per step (default 4096x4096; 1073741824 for the 1 Gi sweep)")
     ap.add_argument("--src", default="f32", choices=["f32", "bf16", "f16"], help="fp8_roundtrip: source dtype")
     ap.add_argument("--fmt", default="e4m3", choices=["e4m3", "e5m2"], help="fp8_roundtrip: fp8 format")
+    ap.add_argument("--eager", action="store_true",
+                    help="llama_fp8: launch every kernel from Python instead of replaying a captured graph")
     ap.add_argument("--gather", action="store_true",
                     help="scaled_mm at N > 1: also time the replicated-output all-gather of the M-sharded result")
     ap.add_argument("--m", type=int, default=0,

@@ -36,3 +36,27 @@ def test_one_layer_matches_float32(device):
     ref = ref + (F.silu(g) * u) @ deq(layer.w_d, layer.s_d).t()
     rel = ((y - ref).norm() / (ref - xf).norm()).item()   # error relative to the layer's update
     assert torch.isfinite(y).all() and rel < 0.10, rel
+
+
+def test_graph_replay_matches_eager(device):
+    """Two layers captured as one CUDA graph (the benchmark's timed step)
+    give the eager forward's bits: the library's launches (tensor maps,
+    programmatic dependent launch, clusters) are capture-safe."""
+    from fp4_fp8_for_torch_mps import workloads as W
+    stack = W.Fp8LlamaStack("cuda", layers=2, seed=0)
+    x = W.llama_input(1, 512).cuda()
+    eager = stack.forward(x, 1, 512).clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            y = stack.forward(x, 1, 512)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), eager.view(torch.int16))
+    x.copy_(W.llama_input(1, 512, seed=3).cuda())         # new input through the same graph
+    g.replay()
+    torch.cuda.synchronize()
+    again = stack.forward(x, 1, 512)
+    assert torch.equal(y.view(torch.int16), again.view(torch.int16))
