@@ -1815,15 +1815,17 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 // feeds them straight to the warp-level tensor-core instruction
 // mma.sync.m16n8k16 computing D^T = W x^T: 16 weight rows as the A operand,
 // 8 x rows as B (NT = 1 or 2 tiles, zero rows past M), float32 accumulators.
-//   CTA: 4 warps, 64 output channels (16 weight rows per warp);
+//   CTA: 4 consumer warps, 64 output channels (16 weight rows per warp), and
+//   a producer warp whose lane 0 streams the CTA's 64 x 128-byte weight
+//   tiles with TMA into a GV_STAGES-deep ring (128-byte swizzle, full /
+//   empty mbarriers, bounded waits);
 //   cluster: ks CTAs splitting K, partial sums reduced through distributed
 //   shared memory (each CTA reduces and stores 64 / ks columns), so no
 //   global scratch and a fixed summation order.
-//   k-loop: 128-value blocks; lane (g, t) copies 32 weight bytes of rows g
-//   and 8 + g per block into a GV_STAGES-deep shared-memory ring with
-//   cp.async (its own slots only, so no barrier), and reads 32 x values of
-//   x row g (and g + 8) with read-only loads (the x rows are shared by every
-//   warp and CTA of a column and stay in L1 / L2). Within a block the lane's
+//   k-loop: 128-value blocks; lane (g, t) reads 32 weight bytes of rows g
+//   and 8 + g of the tile and 32 x values of x row g (and g + 8) with
+//   read-only loads (the x rows are shared by every warp and CTA of a
+//   column and stay in L1 / L2). Within a block the lane's
 //   32 physical k positions 32t .. 32t+31 are the logical positions {2t,
 //   2t+1, 2t+8, 2t+9} of eight consecutive m16n8k16 steps (four positions
 //   per step), the same permutation for A and B, which leaves the sum
@@ -1832,7 +1834,8 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 constexpr int GV_WARPS = 4;
 constexpr int GV_BN = 16 * GV_WARPS;  // 64 output channels per CTA
 constexpr int GV_BK = 128;
-constexpr int GV_STAGES = 4;  // weight blocks in flight per lane (cp.async ring)
+constexpr int GV_STAGES = 6;  // weight tiles in flight per CTA (TMA ring)
+constexpr int GV_TILE = GV_BN * GV_BK;  // 64 weight rows x 128 codes, 8 KiB
 
 template <int WF, bool F16>
 __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o)[16]) {
@@ -1872,20 +1875,19 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 template <int WF, bool F16, int NT>  // NT: 8-row tiles of x (1 for M <= 8, 2 for M <= 16)
-__global__ void __launch_bounds__(32 * GV_WARPS)
-linear_fp8w_gemv_kernel(const uint16_t *__restrict__ x, int64_t ldx, const uint8_t *__restrict__ w, int64_t ldw,
+__global__ void __launch_bounds__(32 * (GV_WARPS + 1))
+linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t *__restrict__ x, int64_t ldx,
                         int M, int N, int kslice, const Params p) {
-  extern __shared__ __align__(16) uint8_t gv_smem[];
-  const uint32_t ring = smem_u32(gv_smem);  // GV_STAGES x GV_WARPS x 2 KiB of raw weights
-  float *part = reinterpret_cast<float *>(gv_smem + GV_STAGES * GV_WARPS * 2048);  // [16][GV_BN]
+  extern __shared__ uint8_t gv_raw[];
+  const uint32_t raw_addr = smem_u32(gv_raw);
+  const uint32_t ring = (raw_addr + 1023u) & ~1023u;  // GV_STAGES x 8 KiB tiles (128-byte swizzle)
+  uint8_t *base = gv_raw + (ring - raw_addr);
+  float *part = reinterpret_cast<float *>(base + GV_STAGES * GV_TILE);  // [16][GV_BN]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(part + 16 * GV_BN);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int st) { return bar0 + 8u * st; };
+  auto empty_bar = [&](int st) { return bar0 + 8u * (GV_STAGES + st); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t rank = cluster_rank(), ks = p.sk_cs;
@@ -1893,87 +1895,102 @@ linear_fp8w_gemv_kernel(const uint16_t *__restrict__ x, int64_t ldx, const uint8
   const int64_t k0 = (int64_t)rank * kslice;
   const int nblk = kslice / GV_BK;
 
-  // this lane's weight rows: channel n0 + 16 warp + 8 h + g, h = 0, 1; its 32 bytes of each
-  // 128-value block land in the ring at chunk i = 2h + half: warp slot + i * 512 + lane * 16, so
-  // that the lane reads back exactly what it copied (no barrier) and a warp's 16-byte reads of
-  // one chunk are contiguous
-  const uint8_t *wrow[2];
-  uint32_t wbytes[2];
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    const int n = n0 + 16 * warp + 8 * h + g;
-    wbytes[h] = n < N ? 16u : 0u;
-    wrow[h] = w + (int64_t)(n < N ? n : 0) * ldw + k0 + 32 * t;
-  }
-  const uint32_t slot = ring + (uint32_t)(warp * 2048 + lane * 16);
-  auto issue = [&](int kb) {
-    if (kb < nblk) {
-      const uint32_t st = slot + (uint32_t)((kb % GV_STAGES) * GV_WARPS * 2048);
-#pragma unroll
-      for (int c = 0; c < 4; c++) cp_async16(st + c * 512, wrow[c >> 1] + (int64_t)kb * GV_BK + 16 * (c & 1), wbytes[c >> 1]);
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < GV_STAGES; st++) {
+      mbar_init(full_bar(st), 1);
+      mbar_init(empty_bar(st), GV_WARPS);
     }
-    cp_async_commit();  // one group per block, empty past the end, so the wait count stays uniform
-  };
-#pragma unroll
-  for (int s = 0; s < GV_STAGES - 1; s++) issue(s);
-
-  // D^T = W x^T per warp: the warp's 16 weight rows are the m16n8k16 A operand (rows g, g + 8),
-  // x rows the 8-column B operand (NT tiles: rows 0-7, 8-15). A lane needs x row g (+ 8).
-  float acc[NT][4] = {};
-  const uint4 *xr[NT];
-  bool xin[NT];
-#pragma unroll
-  for (int u = 0; u < NT; u++) {
-    xin[u] = 8 * u + g < M;
-    xr[u] = reinterpret_cast<const uint4 *>(x + (xin[u] ? (int64_t)(8 * u + g) * ldx : 0) + k0 + 32 * t);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmap_w);
   }
-#pragma unroll 1
-  for (int kb = 0; kb < nblk; kb++) {
-    issue(kb + GV_STAGES - 1);
-    cp_async_wait<GV_STAGES - 1>();  // this lane's block kb has landed
-    uint4 raw[2][2];
-    const uint32_t st = slot + (uint32_t)((kb % GV_STAGES) * GV_WARPS * 2048);
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(raw[c >> 1][c & 1].x), "=r"(raw[c >> 1][c & 1].y), "=r"(raw[c >> 1][c & 1].z),
-                     "=r"(raw[c >> 1][c & 1].w)
-                   : "r"(st + c * 512));
-    uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
-#pragma unroll
-    for (int u = 0; u < NT; u++)
-#pragma unroll
-      for (int v = 0; v < 4; v++) {
-        const uint4 q = xin[u] ? __ldg(xr[u] + kb * (GV_BK / 8) + v) : make_uint4(0, 0, 0, 0);
-        xv[u][4 * v] = q.x; xv[u][4 * v + 1] = q.y; xv[u][4 * v + 2] = q.z; xv[u][4 * v + 3] = q.w;
+  __syncthreads();
+
+  float acc[NT][4] = {};
+  if (warp == GV_WARPS) {
+    // ---------------- producer: one lane streams the CTA's 64 weight rows, 128 bytes of K per tile
+    if (lane == 0) {
+      for (int kb = 0; kb < nblk; kb++) {
+        const int st = kb % GV_STAGES;
+        const uint32_t ph = (uint32_t)((kb / GV_STAGES) & 1);
+        if (!mbar_wait(empty_bar(st), ph ^ 1u, p.timeout_ns, 20)) break;
+        mbar_expect_tx(full_bar(st), GV_TILE);
+        tma_load_2d(ring + (uint32_t)(st * GV_TILE), &tmap_w, full_bar(st), (int)(k0 + (int64_t)kb * GV_BK), n0);
       }
-    uint32_t wv[2][16];  // weight rows g and g + 8 converted: the A operand pairs
-    gv_convert32<WF, F16>(raw[0], wv[0]);
-    gv_convert32<WF, F16>(raw[1], wv[1]);
+    }
+  } else {
+    // ---------------- consumers: D^T = W x^T per warp; the warp's 16 weight rows (tile rows
+    // 16 warp + g, + 8) are the m16n8k16 A operand, x rows the 8-column B operand (NT tiles:
+    // rows 0-7, 8-15). Lane (g, t) reads 16-byte units 2t, 2t + 1 of its two rows; unit u of
+    // tile row r sits at u ^ (r & 7) (128-byte swizzle), so a warp's reads are conflict-free.
+    // The x rows are read from global memory (shared by every warp and CTA of a column, they
+    // stay in L1 / L2).
+    const uint4 *xr[NT];
+    bool xin[NT];
 #pragma unroll
-    for (int j = 0; j < 8; j++)
+    for (int u = 0; u < NT; u++) {
+      xin[u] = 8 * u + g < M;
+      xr[u] = reinterpret_cast<const uint4 *>(x + (xin[u] ? (int64_t)(8 * u + g) * ldx : 0) + k0 + 32 * t);
+    }
+    const uint32_t row_off[2] = {(uint32_t)((16 * warp + g) * 128), (uint32_t)((16 * warp + 8 + g) * 128)};
+    const uint32_t unit_off[2] = {(uint32_t)(((2 * t) ^ g) * 16), (uint32_t)(((2 * t + 1) ^ g) * 16)};
+#pragma unroll 1
+    for (int kb = 0; kb < nblk; kb++) {
+      const int st = kb % GV_STAGES;
+      const uint32_t ph = (uint32_t)((kb / GV_STAGES) & 1);
+      uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
 #pragma unroll
       for (int u = 0; u < NT; u++)
-        mma_16816<F16>(acc[u], wv[0][2 * j], wv[1][2 * j], wv[0][2 * j + 1], wv[1][2 * j + 1], xv[u][2 * j],
-                       xv[u][2 * j + 1]);
-  }
-  cp_async_wait<0>();
-
-  // partial sums part[x row][channel] (rows < 8 NT, all written): acc[u] = D^T rows (channels)
-  // g / g + 8, columns (x rows) 8u + 2t (+1)
 #pragma unroll
-  for (int u = 0; u < NT; u++) {
-    const int ch = 16 * warp + g, xrow = 8 * u + 2 * t;
-    part[xrow * GV_BN + ch] = acc[u][0];
-    part[(xrow + 1) * GV_BN + ch] = acc[u][1];
-    part[xrow * GV_BN + ch + 8] = acc[u][2];
-    part[(xrow + 1) * GV_BN + ch + 8] = acc[u][3];
+        for (int v = 0; v < 4; v++) {
+          const uint4 q = xin[u] ? __ldg(xr[u] + kb * (GV_BK / 8) + v) : make_uint4(0, 0, 0, 0);
+          xv[u][4 * v] = q.x; xv[u][4 * v + 1] = q.y; xv[u][4 * v + 2] = q.z; xv[u][4 * v + 3] = q.w;
+        }
+      const bool landed = mbar_wait(full_bar(st), ph, p.timeout_ns, 21);  // every lane waits (visibility)
+      if (!__all_sync(0xFFFFFFFFu, landed)) break;                         // and the warp leaves as one
+      uint4 raw[2][2];
+      const uint32_t tile = ring + (uint32_t)(st * GV_TILE);
+#pragma unroll
+      for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(raw[h][c].x), "=r"(raw[h][c].y), "=r"(raw[h][c].z), "=r"(raw[h][c].w)
+                       : "r"(tile + row_off[h] + unit_off[c]));
+      uint32_t wv[2][16];  // weight rows g and g + 8 converted: the A operand pairs
+      gv_convert32<WF, F16>(raw[0], wv[0]);
+      gv_convert32<WF, F16>(raw[1], wv[1]);
+      // the tile's bytes are now in registers (the conversions consumed them): only then may the
+      // producer's next TMA overwrite the stage; order these reads before that async-proxy write
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(st));  // this warp is done with the tile
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int u = 0; u < NT; u++)
+          mma_16816<F16>(acc[u], wv[0][2 * j], wv[1][2 * j], wv[0][2 * j + 1], wv[1][2 * j + 1], xv[u][2 * j],
+                         xv[u][2 * j + 1]);
+    }
   }
+
+  if (warp < GV_WARPS) {
+    // partial sums part[x row][channel] (rows < 8 NT, all written): acc[u] = D^T rows (channels)
+    // g / g + 8, columns (x rows) 8u + 2t (+1)
+#pragma unroll
+    for (int u = 0; u < NT; u++) {
+      const int ch = 16 * warp + g, xrow = 8 * u + 2 * t;
+      part[xrow * GV_BN + ch] = acc[u][0];
+      part[(xrow + 1) * GV_BN + ch] = acc[u][1];
+      part[xrow * GV_BN + ch + 8] = acc[u][2];
+      part[(xrow + 1) * GV_BN + ch + 8] = acc[u][3];
+    }
+  }
+  __syncwarp();
   cluster_sync();  // every CTA's partial sums are complete
   // this CTA reduces and stores columns [rank * cw, (rank + 1) * cw) of the 64
   const int cw = GV_BN / (int)ks;
   const uint32_t part_addr = smem_u32(part);
-  for (int i = threadIdx.x; i < M * cw; i += 32 * GV_WARPS) {
+  for (int i = threadIdx.x; i < M * cw; i += blockDim.x) {
     const int m = i / cw, col = (int)rank * cw + (i - m * cw);
     const int n = n0 + col;
     float v = 0.f;
@@ -2300,17 +2317,19 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     attr_done[dev] = true;
   }
   if (M <= 16 && K % GV_BK == 0 && g_path != 3) {
-    // very few rows: weights converted in registers for warp-level MMAs, K
-    // split over a cluster of ks CTAs (enough CTAs to cover the GPU a few
-    // times over, each K slice a multiple of the 128-value block and small
-    // enough for its staged x rows)
+    // very few rows: weights streamed by TMA and converted in registers for warp-level MMAs, K
+    // split over a cluster of ks CTAs (enough CTAs to cover the GPU a few times over, each K
+    // slice a multiple of the 128-value block)
     const int64_t nb = (N + GV_BN - 1) / GV_BN;
     int ks = 1;
-    const int64_t ring = GV_STAGES * GV_WARPS * 2048;
     while (ks < 8 && K % (GV_BK * 2 * ks) == 0 && nb * ks < 4LL * current_sm_count()) ks *= 2;
     const int64_t kslice = K / ks;
-    const int64_t smem = ring + 16 * GV_BN * 4;
-    if (smem <= 200 * 1024 && nb <= 65535) {
+    const int64_t smem = 1024 + GV_STAGES * GV_TILE + 16 * GV_BN * 4 + 2 * GV_STAGES * 8;
+    if (nb <= 65535) {
+      CUtensorMap mw;
+      if (int rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, GV_BK, GV_BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
       Params p;
       memset(&p, 0, sizeof(p));
       p.M = (int)M; p.N = (int)N; p.K = (int)K;
@@ -2318,8 +2337,9 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       p.bias = bias; p.bias_dtype = bias_dtype;
       p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
       p.sk_cs = ks;
+      p.timeout_ns = g_timeout_ns;
       const bool f16 = x_dtype == FP8B200_F16;
-      using GvKernel = void (*)(const uint16_t *, int64_t, const uint8_t *, int64_t, int, int, int, const Params);
+      using GvKernel = void (*)(const CUtensorMap, const uint16_t *, int64_t, int, int, int, const Params);
       static const GvKernel kernels[8] = {
           linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 1>, linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 2>,
           linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 1>,  linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 2>,
@@ -2344,13 +2364,12 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
       cfg.gridDim = dim3((unsigned)ks, (unsigned)nb, 1);
-      cfg.blockDim = dim3(32 * GV_WARPS, 1, 1);
+      cfg.blockDim = dim3(32 * (GV_WARPS + 1), 1, 1);
       cfg.dynamicSmemBytes = (size_t)smem;
       cfg.stream = (cudaStream_t)stream;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaLaunchKernelEx(&cfg, kern, (const uint16_t *)x, (int64_t)ldx, (const uint8_t *)w, (int64_t)ldw, (int)M,
-                         (int)N, (int)kslice, p);
+      cudaLaunchKernelEx(&cfg, kern, mw, (const uint16_t *)x, (int64_t)ldx, (int)M, (int)N, (int)kslice, p);
       count_launch();
       return check_launch("linear_fp8w");
     }
