@@ -253,10 +253,11 @@ int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64_t lda, int
 int fp8b200_gemm_status(uint32_t *status_out, int reset);
 
 /*
- * Test hook for the GEMM's bounded waits: skip_first_load != 0 makes the
- * producer never fill the first pipeline stage, so the consumer's wait runs
- * out after wait_timeout_ns (0 = the default of 2 s) and the kernel returns
- * with the status word set. Not for production use.
+ * Test hook for the bounded waits of the GEMM kernels and of the few-row
+ * fp8b200_linear_fp8w kernel: skip_first_load != 0 makes the producer never
+ * fill the first pipeline stage, so the consumers' waits run out after
+ * wait_timeout_ns (0 = the default of 2 s) and the kernel returns with the
+ * status word set. Not for production use.
  */
 int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
 

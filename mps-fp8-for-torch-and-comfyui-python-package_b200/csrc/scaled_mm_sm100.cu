@@ -1913,6 +1913,7 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
         const int st = kb % GV_STAGES;
         const uint32_t ph = (uint32_t)((kb / GV_STAGES) & 1);
         if (!mbar_wait(empty_bar(st), ph ^ 1u, p.timeout_ns, 20)) break;
+        if (p.debug_skip_first_load) break;  // test hook: no tile ever lands, the consumers' waits run out
         mbar_expect_tx(full_bar(st), GV_TILE);
         tma_load_2d(ring + (uint32_t)(st * GV_TILE), &tmap_w, full_bar(st), (int)(k0 + (int64_t)kb * GV_BK), n0);
       }
@@ -2338,6 +2339,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
       p.sk_cs = ks;
       p.timeout_ns = g_timeout_ns;
+      p.debug_skip_first_load = g_debug_skip_first_load;
       const bool f16 = x_dtype == FP8B200_F16;
       using GvKernel = void (*)(const CUtensorMap, const uint16_t *, int64_t, int, int, int, const Params);
       static const GvKernel kernels[8] = {

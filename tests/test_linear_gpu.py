@@ -258,3 +258,29 @@ def test_few_rows_repeated_calls_are_stable(nat):
     for i, o in enumerate(outs):
         assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16)), i
     check(outs[0], r, S, "repeated few-row calls")
+
+
+def test_few_rows_bounded_wait_times_out_and_context_survives(nat):
+    """The warp-level kernel's consumers wait for weight tiles that never
+    arrive (the test hook stops the producer before its first load): they give
+    up after 50 ms with the status word set, the call returns, and the next
+    call on the same context is correct."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    lib = L.lib()
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(4, 1024, generator=g).to(torch.bfloat16).cuda()
+    w = rand_w((512, 1024), E4, g).cuda()
+    s = torch.tensor(0.01).cuda()
+    L.gemm_status(reset=True)
+    try:
+        lib.fp8b200_debug_gemm(1, 50_000_000)
+        nat.fp8_linear(x, w, s)
+        status = L.gemm_status(reset=True)
+    finally:
+        lib.fp8b200_debug_gemm(0, 0)
+    assert status & 0x80000000, hex(status)
+    out = nat.fp8_linear(x, w, s)
+    torch.cuda.synchronize()
+    assert L.gemm_status() == 0
+    r, S = reference(x.cpu(), w.cpu(), s.cpu())
+    check(out, r, S, "after timeout")
