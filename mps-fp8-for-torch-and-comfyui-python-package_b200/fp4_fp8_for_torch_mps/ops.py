@@ -178,12 +178,14 @@ def _apply_memory_format(t: torch.Tensor, memory_format) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ aten overrides
-def _cuda_scaled_mm(self, mat2, scale_a, scale_b, bias=None, scale_result=None, out_dtype=None,
-                    use_fast_accum=False):
-    if not _device_ok(self.device):
-        raise RuntimeError(
-            f"_scaled_mm: the fp4_fp8_for_torch_mps override is registered but {self.device} is not "
-            "an sm_100 (B200) device; set FP8_B200_DISABLE_OVERRIDES=1 to use PyTorch's kernel")
+def check_scaled_mm_args(self, mat2, scale_a, scale_b, out_dtype=None):
+    """Argument checks of the `_scaled_mm` override: the rank, stride and
+    divisibility checks of PyTorch's meta function for the op
+    (torch/_meta_registrations.py, `meta_scaled_mm`) with its messages, plus the
+    scale-shape rules of its CUDA kernel. Returns (M, N, K, output dtype). Pure shape/dtype/stride logic: runs on any
+    device, so the boundary's error behaviour is testable without a GPU. Modes the
+    B200 kernels do not implement raise instead of falling back: float4_e2m1fn_x2
+    operands, block-scaled (MX / NVFP4) scales and e5m2 x e5m2."""
     if self.dim() != 2 or mat2.dim() != 2:
         raise RuntimeError(f"Inputs must be 2D but got self.dim()={self.dim()} and mat2.dim()={mat2.dim()}")
     if not (_is_fp8(self.dtype) and _is_fp8(mat2.dtype)):
@@ -219,6 +221,16 @@ def _cuda_scaled_mm(self, mat2, scale_a, scale_b, bias=None, scale_result=None, 
     odt = self.dtype if out_dtype is None else out_dtype
     if odt not in _FLOAT_DTYPES + _FP8_DTYPES:
         raise RuntimeError(f"_scaled_mm: unsupported out_dtype {odt}")
+    return M, N, K, odt
+
+
+def _cuda_scaled_mm(self, mat2, scale_a, scale_b, bias=None, scale_result=None, out_dtype=None,
+                    use_fast_accum=False):
+    if not _device_ok(self.device):
+        raise RuntimeError(
+            f"_scaled_mm: the fp4_fp8_for_torch_mps override is registered but {self.device} is not "
+            "an sm_100 (B200) device; set FP8_B200_DISABLE_OVERRIDES=1 to use PyTorch's kernel")
+    M, N, K, odt = check_scaled_mm_args(self, mat2, scale_a, scale_b, out_dtype)
     if M == 0 or N == 0:
         return torch.empty((M, N), dtype=odt, device=self.device)
     if K == 0:

@@ -167,3 +167,71 @@ print("ok")
 '''
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+def _fp8_pair(M, N, K, da=E4, db=E4):
+    a = torch.zeros(M, K, dtype=torch.uint8).view(da)
+    b = torch.zeros(N, K, dtype=torch.uint8).view(db)
+    return a, b
+
+
+def test_scaled_mm_argument_checks_accept():
+    """The `_scaled_mm` override's argument checks, run on CPU tensors: the
+    accepted modes (tensorwise and rowwise scales, mixed e4m3/e5m2, fp8 or
+    16/32-bit output, views with padded row strides)."""
+    from fp4_fp8_for_torch_mps.ops import check_scaled_mm_args
+    s = torch.tensor(1.0)
+    a, b = _fp8_pair(32, 48, 64)
+    assert check_scaled_mm_args(a, b.t(), s, s) == (32, 48, 64, E4)
+    assert check_scaled_mm_args(a, b.t(), s, s, BF) == (32, 48, 64, BF)
+    assert check_scaled_mm_args(a.view(E5), b.t(), s, s, F32)[3] == F32
+    assert check_scaled_mm_args(a, b.view(E5).t(), torch.ones(32, 1), torch.ones(1, 48), H)[3] == H
+    wide_a, wide_b = _fp8_pair(32, 48, 128)
+    assert check_scaled_mm_args(wide_a[:, 16:80], wide_b[:, 32:96].t(), s, s, BF)[:3] == (32, 48, 64)
+    e0, e1 = _fp8_pair(0, 16, 32)
+    assert check_scaled_mm_args(e0, e1.t(), s, s, BF)[:3] == (0, 16, 32)
+
+
+_REJECT_WHY = {
+    "fp4_operands": "operands must be float8", "int8_operands": "operands must be float8",
+    "bf16_operands": "operands must be float8", "e5m2_x_e5m2": "two Float8_e5m2",
+    "3d": "must be 2D", "k_mismatch": "cannot be multiplied", "mat2_row_major": "col_major",
+    "self_col_major": "row_major", "k_not_16": "self.size\\(1\\) to be divisible by 16",
+    "n_not_16": "mat2 to be divisible by 16", "f16_scales": "must be float32",
+    "blockwise_scales": "Invalid scaling configuration", "mx_scales": "must be float32",
+    "rowwise_transposed": "Invalid scaling configuration", "rowwise_noncontiguous": "contiguous",
+    "int_out": "unsupported out_dtype",
+}
+
+
+@pytest.mark.parametrize("case", sorted(_REJECT_WHY))
+def test_scaled_mm_argument_checks_reject(case):
+    """Every unsupported call raises RuntimeError, for its own reason, before any
+    device work: the stride/divisibility rules PyTorch's meta function enforces,
+    and the modes the B200 kernels do not implement (float4_e2m1fn_x2 operands,
+    block scales, e5m2 x e5m2), which raise instead of falling back to a library
+    kernel."""
+    from fp4_fp8_for_torch_mps.ops import check_scaled_mm_args
+    s = torch.tensor(1.0)
+    a, b = _fp8_pair(32, 48, 64)
+    args = {
+        "fp4_operands": (a.view(F4), b.view(F4).t(), s, s),
+        "int8_operands": (a.view(torch.int8), b.view(torch.int8).t(), s, s),
+        "bf16_operands": (torch.zeros(32, 64, dtype=BF), torch.zeros(48, 64, dtype=BF).t(), s, s),
+        "e5m2_x_e5m2": (a.view(E5), b.view(E5).t(), s, s),
+        "3d": (a.unsqueeze(0), b.t(), s, s),
+        "k_mismatch": (a, _fp8_pair(32, 48, 80)[1].t(), s, s),
+        "mat2_row_major": (a, torch.zeros(64, 48, dtype=torch.uint8).view(E4), s, s),
+        "self_col_major": (torch.zeros(64, 32, dtype=torch.uint8).view(E4).t(), b.t(), s, s),
+        "k_not_16": (a[:, :40], b[:, :40].t(), s, s),
+        "n_not_16": (a, _fp8_pair(32, 40, 64)[1].t(), s, s),
+        "f16_scales": (a, b.t(), s.half(), s.half()),
+        "blockwise_scales": (a, b.t(), torch.ones(32, 2), s),
+        "mx_scales": (a, b.t(), torch.ones(32, 2).to(torch.float8_e8m0fnu),
+                      torch.ones(48, 2).to(torch.float8_e8m0fnu)),
+        "rowwise_transposed": (a, b.t(), torch.ones(1, 32), torch.ones(48, 1)),
+        "rowwise_noncontiguous": (a, b.t(), torch.ones(32, 2)[:, :1], torch.ones(1, 48)),
+        "int_out": (a, b.t(), s, s, torch.int32),
+    }
+    with pytest.raises(RuntimeError, match=_REJECT_WHY[case]):
+        check_scaled_mm_args(*args[case])

@@ -169,6 +169,8 @@ def test_invalid_calls_raise(nat):
     with pytest.raises(RuntimeError):
         torch._scaled_mm(a.view(E5), b.view(E5).t(), s, s)  # e5m2 x e5m2
     with pytest.raises(RuntimeError):
+        torch._scaled_mm(a.view(torch.float4_e2m1fn_x2), b.view(torch.float4_e2m1fn_x2).t(), s, s)  # fp4
+    with pytest.raises(RuntimeError):
         torch._scaled_mm(a, b.t(), torch.ones(32, 2, device="cuda"), s)  # blockwise-like scales
     with pytest.raises(RuntimeError):
         torch._scaled_mm(a[:, :40], b[:, :40].t(), s, s)  # K not multiple of 16
