@@ -584,6 +584,12 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   uint8_t *out_ring = in_ring + kStages * C::kIn;
   uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * C::kOut);
   const int64_t nch = n / kEncElems;
+  // A per-tensor quantisation reads its input twice (amax pass, then this
+  // encode). Walking the chunks last-to-first here starts on the part the
+  // amax pass read most recently, which is still in L2; `at` maps the
+  // walk position to the chunk (a bijection of [0, nch)).
+  const bool rev = amax_bits != nullptr;
+  auto at = [&](int64_t c) { return rev ? nch - 1 - c : c; };
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -595,7 +601,7 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
       const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
-      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
+      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + at(c) * C::kIn, C::kIn, smem_addr(bar + i));
     }
   }
   __syncthreads();
@@ -623,12 +629,12 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0) {
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + c * C::kOut),
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + at(c) * C::kOut),
                    "r"(smem_addr(out)), "r"(C::kOut)
                    : "memory");
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       const int64_t c2 = blockIdx.x + (i + kStages) * gridDim.x;
-      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + c2 * C::kIn, C::kIn, smem_addr(bar + st));
+      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + at(c2) * C::kIn, C::kIn, smem_addr(bar + st));
     }
   }
   if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -762,6 +768,12 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
   uint8_t *out_ring = in_ring + kStages * C::kIn;
   uint64_t *bar = reinterpret_cast<uint64_t *>(out_ring + kStages * C::kOut);
   const int64_t nch = n / kEncElems;
+  // A per-tensor quantisation reads its input twice (amax pass, then this
+  // encode). Walking the chunks last-to-first here starts on the part the
+  // amax pass read most recently, which is still in L2; `at` maps the
+  // walk position to the chunk (a bijection of [0, nch)).
+  const bool rev = amax_bits != nullptr;
+  auto at = [&](int64_t c) { return rev ? nch - 1 - c : c; };
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -773,7 +785,7 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
       const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
-      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + c * C::kIn, C::kIn, smem_addr(bar + i));
+      if (c < nch) bulk_load(smem_addr(in_ring + i * C::kIn), src + at(c) * C::kIn, C::kIn, smem_addr(bar + i));
     }
   }
   __syncthreads();
@@ -826,12 +838,12 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0) {
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + c * C::kOut),
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + at(c) * C::kOut),
                    "r"(smem_addr(out)), "r"(C::kOut)
                    : "memory");
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       const int64_t c2 = blockIdx.x + (i + kStages) * gridDim.x;
-      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + c2 * C::kIn, C::kIn, smem_addr(bar + st));
+      if (c2 < nch) bulk_load(smem_addr(in_ring + st * C::kIn), src + at(c2) * C::kIn, C::kIn, smem_addr(bar + st));
     }
   }
   if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");

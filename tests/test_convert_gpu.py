@@ -200,6 +200,26 @@ def test_quantize_zero_input_and_repeat(nat):
     assert inv.item() == np.float32(1.0 / (448.0 / 2.0))
 
 
+@pytest.mark.parametrize("case", ["randn_e4m3", "randn_e5m2", "planted_e4m3"])
+def test_quantize_full_size(nat, case):
+    """Per-tensor quantize at the 4096x4096 f32 workload size: thousands of
+    chunks per launch, several per CTA, walked last-to-first by the encoder.
+    Every element against the oracle; the planted input (NaN, inf, every
+    code and midpoint) has a NaN amax, so its scale is 1."""
+    from fp4_fp8_for_torch_mps.workloads import fp8_roundtrip_input
+    fmt = 1 if case.endswith("e5m2") else 0
+    if case.startswith("planted"):
+        x = fp8_roundtrip_input(seed=3)
+    else:
+        x = torch.randn(4096, 4096, generator=torch.Generator().manual_seed(11)) * 64
+    q, sc = nat.quantize_fp8(x.cuda(), FP8[fmt])
+    xf = x.reshape(-1).numpy()
+    amax = float(np.max(np.abs(xf)))
+    scale = (57344.0 if fmt else 448.0) / amax if amax > 0 else 1.0
+    assert sc[0].item() == np.float32(scale) and sc[1].item() == np.float32(1.0 / scale)
+    assert np.array_equal(q.reshape(-1).cpu().numpy(), O.encode_fp8_scaled(xf, scale, fmt))
+
+
 # ---------------------------------------------------------------- fp4
 @pytest.mark.parametrize("odt", [0, 1, 2])
 @pytest.mark.parametrize("sc", list(SCALES))
@@ -275,6 +295,17 @@ def test_fp4_quantize_matches_reference_formula(nat, n, sdt):
     scale = 6.0 / amax
     assert np.array_equal(enc.cpu().numpy(), O.fp4_encode_ref(xf.numpy(), scale))
     assert inv.item() == np.float32(1.0 / scale) and enc.shape == (n // 2,)
+
+
+def test_fp4_quantize_full_size(nat):
+    """Per-tensor FP4 quantize of 8192x8192 bf16 (several chunks per CTA,
+    walked last-to-first by the encoder), every byte against the oracle."""
+    x = (torch.randn(8192, 8192, generator=torch.Generator().manual_seed(12)) * 3).to(torch.bfloat16)
+    enc, inv = torch.ops.fp8_mps.fp4_quantize(x.cuda())
+    xf = x.float().reshape(-1).numpy()
+    scale = 6.0 / float(np.max(np.abs(xf)))
+    assert inv.item() == np.float32(1.0 / scale)
+    assert np.array_equal(enc.cpu().numpy(), O.fp4_encode_ref(xf, scale))
 
 
 @pytest.mark.parametrize("sdt", [1, 2])
