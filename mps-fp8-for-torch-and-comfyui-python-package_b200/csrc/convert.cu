@@ -876,15 +876,20 @@ amax_kernel(const uint8_t *__restrict__ src, int64_t n, int64_t nunits, uint32_t
       }
     }
   };
-  int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (; u + 3 * nthreads < nunits; u += 4 * nthreads) {  // four 32-byte loads in flight per thread
+  // four 32-byte loads in flight per thread, the last round predicated (a
+  // unit past the end reads as zeros, which leave the max unchanged), so no
+  // thread ends on a chain of one-load rounds
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < nunits; u += 4 * nthreads) {
     U8x32 a[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) a[k] = ld_u256(src + (u + k * nthreads) * 32);
+    for (int k = 0; k < 4; k++) {
+      const int64_t v = u + k * nthreads;
+      if (v < nunits) a[k] = ld_u256(src + v * 32);
+      else a[k] = U8x32{};
+    }
 #pragma unroll
     for (int k = 0; k < 4; k++) fold(a[k]);
   }
-  for (; u < nunits; u += nthreads) fold(ld_u256(src + u * 32));
   for (int64_t i = nunits * PER + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nthreads)
     m = max(m, f2u(load_elem<SRC>(src, i)) & 0x7FFFFFFFu);
   m = __reduce_max_sync(0xFFFFFFFFu, m);
@@ -1378,7 +1383,12 @@ int launch_amax_and_scale(const void *src, int src_dtype, int64_t n, float fmax,
   if (n > 0) {
     const int eb = src_dtype == FP8B200_F32 ? 4 : 2;
     const int64_t nunits = aligned32(src) ? (n * eb) / 32 : 0;
-    const int g = grid_for(std::max<int64_t>(nunits ? nunits : n, 1), kThreads, 4);
+    // one wave: as many CTAs as fit on the SMs at once (the f32 variant holds
+    // twice the registers of the 16-bit ones, so fewer CTAs fit)
+    const void *k = src_dtype == FP8B200_F32    ? (const void *)amax_kernel<FP8B200_F32>
+                    : src_dtype == FP8B200_BF16 ? (const void *)amax_kernel<FP8B200_BF16>
+                                                : (const void *)amax_kernel<FP8B200_F16>;
+    const int g = grid_for(std::max<int64_t>(nunits ? nunits : n, 1), kThreads, resident_per_sm(k, 0));
     const uint8_t *s = (const uint8_t *)src;
     if (src_dtype == FP8B200_F32) amax_kernel<FP8B200_F32><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
     else if (src_dtype == FP8B200_BF16) amax_kernel<FP8B200_BF16><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);

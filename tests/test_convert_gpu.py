@@ -200,6 +200,22 @@ def test_quantize_zero_input_and_repeat(nat):
     assert inv.item() == np.float32(1.0 / (448.0 / 2.0))
 
 
+@pytest.mark.parametrize("sdt", [0, 1])
+@pytest.mark.parametrize("n", [4096 * 300 + 3, 1 << 22, (1 << 24) + 24])
+def test_quantize_amax_position(nat, sdt, n):
+    """The amax reduction finds a lone maximum wherever it sits: first
+    element, middle, the last vectorised unit, the scalar tail."""
+    base = (torch.rand(n, generator=torch.Generator().manual_seed(n)) - 0.5).to(OUT[sdt])
+    per_unit = 8 if sdt == 0 else 16
+    for pos in (0, n // 2, (n // per_unit - 1) * per_unit, n - 1):
+        for v in (1000.0, -1000.0):
+            x = base.clone()
+            x[pos] = v
+            q, sc = nat.quantize_fp8(x.cuda(), torch.float8_e4m3fn)
+            assert sc[0].item() == np.float32(448.0 / 1000.0), (pos, v)
+            assert q.view(-1)[pos].item() == (0x7E if v > 0 else 0xFE), (pos, v)
+
+
 @pytest.mark.parametrize("case", ["randn_e4m3", "randn_e5m2", "planted_e4m3"])
 def test_quantize_full_size(nat, case):
     """Per-tensor quantize at the 4096x4096 f32 workload size: thousands of
