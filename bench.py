@@ -481,10 +481,36 @@ class Quantize:
         self.h_out = torch.empty(out_n, dtype=torch.uint8).pin_memory()
         self.h_scales = torch.empty(self.scales.numel(), dtype=torch.float32).pin_memory()
 
+    graph = None
+    graph_launches = 0  # kernels in the captured graph
+
+    def capture(self, steps):
+        """One CUDA graph holding `steps` consecutive quantisations (cycling
+        through the buffer sets), replayed once for the timed region: a step
+        is up to three kernels of a few to 25 us (clear, amax, encode for
+        the per-tensor rows), which host launches one by one cannot keep
+        fed; the host-launched path is what `e2e` measures."""
+        side = torch.cuda.Stream()
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = self.L.launch_count()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(self.graph, stream=side):
+                for j in range(steps):
+                    self._launch((self.i + j) % self.sets, side.cuda_stream)
+        self.graph_launches = self.L.launch_count() - n0
+        torch.cuda.synchronize()
+        self.config["launch"] = f"one CUDA graph of {steps} steps"
+
+    def replay(self):
+        self.graph.replay()
+
     def step(self):
         k = self.i % self.sets
         self.i += 1
-        L, x, o, st = self.L, self.xs[k], self.outs[k], self.stream.cuda_stream
+        self._launch(k, self.stream.cuda_stream)
+
+    def _launch(self, k, st):
+        L, x, o = self.L, self.xs[k], self.outs[k]
         if self.kind == "fp8_quantize":
             rc = self.lib.fp8b200_quantize_fp8(x.data_ptr(), L.F32, o.data_ptr(), L.E4M3, self.n,
                                                self.scales.data_ptr(), self.scratch.data_ptr(), st)

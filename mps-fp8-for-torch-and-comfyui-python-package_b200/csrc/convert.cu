@@ -862,6 +862,7 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
 template <int SRC>
 __global__ void __launch_bounds__(kThreads)
 amax_kernel(const uint8_t *__restrict__ src, int64_t n, int64_t nunits, uint32_t *__restrict__ amax_out) {
+  pdl_launch_dependents();
   constexpr int EB = SRC == FP8B200_F32 ? 4 : 2;
   constexpr int PER = 32 / EB;
   uint32_t m = 0, sg;
@@ -899,8 +900,21 @@ amax_kernel(const uint8_t *__restrict__ src, int64_t n, int64_t nunits, uint32_t
   if (threadIdx.x < 32) {
     uint32_t r = threadIdx.x < blockDim.x / 32 ? warp_max[threadIdx.x] : 0u;
     r = __reduce_max_sync(0xFFFFFFFFu, r);
+    // the input was final before clear_amax_kernel started; amax_out is
+    // cleared by that kernel, so wait for it before the first global write
+    pdl_wait_prior();
     if (threadIdx.x == 0 && r) atomicMax(amax_out, r);
   }
+}
+
+// Clears the amax word of a per-tensor quantisation. Launched without the
+// programmatic attribute, so it starts after all earlier work in the stream
+// (the input is final from then on); the amax reduction after it is a
+// programmatic dependent launch that streams the input meanwhile and waits
+// for this kernel only before its atomicMax.
+__global__ void clear_amax_kernel(uint32_t *__restrict__ amax_out) {
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) *amax_out = 0u;
 }
 
 // scale = fmax/amax (1 if amax is 0 or NaN), computed in double as the
@@ -1378,8 +1392,9 @@ int check_scale_mode(int mode, const float *scale, int odt) {
 // element-wise encoders; the bulk encoders derive the scale themselves).
 int launch_amax_and_scale(const void *src, int src_dtype, int64_t n, float fmax, float *scale_out,
                           uint32_t *amax_scratch, cudaStream_t st, bool with_scale = true) {
-  if (cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t), st) != cudaSuccess)
-    return check_launch("quantize amax clear");
+  clear_amax_kernel<<<1, 32, 0, st>>>(amax_scratch);
+  count_launch();
+  if (int rc = check_launch("quantize amax clear")) return rc;
   if (n > 0) {
     const int eb = src_dtype == FP8B200_F32 ? 4 : 2;
     const int64_t nunits = aligned32(src) ? (n * eb) / 32 : 0;
@@ -1390,9 +1405,9 @@ int launch_amax_and_scale(const void *src, int src_dtype, int64_t n, float fmax,
                                                 : (const void *)amax_kernel<FP8B200_F16>;
     const int g = grid_for(std::max<int64_t>(nunits ? nunits : n, 1), kThreads, resident_per_sm(k, 0));
     const uint8_t *s = (const uint8_t *)src;
-    if (src_dtype == FP8B200_F32) amax_kernel<FP8B200_F32><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
-    else if (src_dtype == FP8B200_BF16) amax_kernel<FP8B200_BF16><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
-    else amax_kernel<FP8B200_F16><<<g, kThreads, 0, st>>>(s, n, nunits, amax_scratch);
+    if (src_dtype == FP8B200_F32) launch_pdl(amax_kernel<FP8B200_F32>, g, kThreads, 0, st, s, n, nunits, amax_scratch);
+    else if (src_dtype == FP8B200_BF16) launch_pdl(amax_kernel<FP8B200_BF16>, g, kThreads, 0, st, s, n, nunits, amax_scratch);
+    else launch_pdl(amax_kernel<FP8B200_F16>, g, kThreads, 0, st, s, n, nunits, amax_scratch);
     count_launch();
     if (int rc = check_launch("quantize amax")) return rc;
   }
