@@ -200,6 +200,25 @@ def test_quantize_zero_input_and_repeat(nat):
     assert inv.item() == np.float32(1.0 / (448.0 / 2.0))
 
 
+@pytest.mark.parametrize("sdt", [0, 1, 2])
+@pytest.mark.parametrize("offset", [1, 2, 8])
+def test_quantize_unaligned_views(nat, sdt, offset):
+    """Per-tensor fp8 and FP4 quantize of views that start off the 16-byte
+    boundary: the element-wise amax, scale and encode kernels instead of the
+    bulk ones, same results as the oracle."""
+    n = 300002
+    x = (torch.randn(n + offset, generator=torch.Generator().manual_seed(offset)) * 7).to(OUT[sdt])
+    dev = x.cuda()[offset:]
+    xf = x[offset:].float().numpy()
+    amax = float(np.max(np.abs(xf)))
+    q, sc = nat.quantize_fp8(dev, torch.float8_e4m3fn)
+    assert sc[0].item() == np.float32(448.0 / amax)
+    assert np.array_equal(q.cpu().numpy(), O.encode_fp8_scaled(xf, 448.0 / amax, 0))
+    enc, inv = torch.ops.fp8_mps.fp4_quantize(dev)
+    assert inv.item() == np.float32(1.0 / (6.0 / amax))
+    assert np.array_equal(enc.cpu().numpy(), O.fp4_encode_ref(xf, 6.0 / amax))
+
+
 @pytest.mark.parametrize("sdt", [0, 1])
 @pytest.mark.parametrize("n", [4096 * 300 + 3, 1 << 22, (1 << 24) + 24])
 def test_quantize_amax_position(nat, sdt, n):
