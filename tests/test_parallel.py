@@ -49,22 +49,21 @@ def _worker(rank, ws, port, rows, q):
 
 
 def _body(rank, ws, rows, q):
-    if True:
-        g = torch.Generator().manual_seed(0)
-        x = torch.randn(rows, 24, generator=g) * 50
-        enc = sharded_rows_apply(x, lambda t: t.to(torch.float8_e4m3fn), gather=True)
-        ok1 = torch.equal(enc.view(torch.uint8), x.to(torch.float8_e4m3fn).view(torch.uint8))
-        local = sharded_rows_apply(x, lambda t: t.to(torch.float8_e5m2))
-        s, e = shard_rows(rows, ws, rank)
-        ok2 = torch.equal(local.view(torch.uint8), x[s:e].to(torch.float8_e5m2).view(torch.uint8))
-        a = (torch.randn(rows, 32, generator=g) * 10).to(torch.float8_e4m3fn)
-        b = (torch.randn(16, 32, generator=g) * 10).to(torch.float8_e4m3fn)
-        sc = torch.tensor(0.5)
-        full = sharded_scaled_mm(a, b.t(), sc, sc, gather=True, out_dtype=torch.float32)
-        ok3 = torch.equal(full, torch._scaled_mm(a, b.t(), sc, sc, out_dtype=torch.float32))
-        back = gather_rows(local, rows)
-        ok4 = torch.equal(back.view(torch.uint8), x.to(torch.float8_e5m2).view(torch.uint8))
-        q.put((rank, ok1, ok2, ok3, ok4))
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(rows, 24, generator=g) * 50
+    enc = sharded_rows_apply(x, lambda t: t.to(torch.float8_e4m3fn), gather=True)
+    ok1 = torch.equal(enc.view(torch.uint8), x.to(torch.float8_e4m3fn).view(torch.uint8))
+    local = sharded_rows_apply(x, lambda t: t.to(torch.float8_e5m2))
+    s, e = shard_rows(rows, ws, rank)
+    ok2 = torch.equal(local.view(torch.uint8), x[s:e].to(torch.float8_e5m2).view(torch.uint8))
+    a = (torch.randn(rows, 32, generator=g) * 10).to(torch.float8_e4m3fn)
+    b = (torch.randn(16, 32, generator=g) * 10).to(torch.float8_e4m3fn)
+    sc = torch.tensor(0.5)
+    full = sharded_scaled_mm(a, b.t(), sc, sc, gather=True, out_dtype=torch.float32)
+    ok3 = torch.equal(full, torch._scaled_mm(a, b.t(), sc, sc, out_dtype=torch.float32))
+    back = gather_rows(local, rows)
+    ok4 = torch.equal(back.view(torch.uint8), x.to(torch.float8_e5m2).view(torch.uint8))
+    q.put((rank, ok1, ok2, ok3, ok4))
 
 
 @pytest.mark.parametrize("ws,rows", [(2, 37), (4, 64), (4, 3)])
@@ -80,3 +79,42 @@ def test_gloo_sharded_convert_and_gather(ws, rows):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert all(len(r) == 5 and all(r[1:]) for r in res), res
+
+
+def _failing_worker(rank, ws, port, q):
+    """Rank 1 fails on the host before the gather (an exception in its
+    conversion); the others must get an error from the collective, not wait
+    for ever."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=10))
+    x = torch.randn(8 * ws, 16)
+
+    def convert(t):
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        return t.to(torch.float8_e4m3fn)
+    try:
+        sharded_rows_apply(x, convert, gather=True)
+        q.put((rank, "completed"))
+    except Exception as e:  # noqa: BLE001 - the test wants whatever the collective raised
+        q.put((rank, "error", str(e)[:200]))
+    q.close()
+    q.join_thread()  # the message is in the pipe before the process ends
+    os._exit(0)  # no destroy_process_group: the group is broken
+
+
+@pytest.mark.parametrize("ws", [2, 3])
+def test_gloo_rank_failure_surfaces_as_error(ws):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, ws, port, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(ws))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1][:2] == (1, "error") and "injected" in res[1][2], res
+    for r in res:
+        assert r[1] == "error", res  # no rank completes a gather that lost a member
