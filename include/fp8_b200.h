@@ -40,6 +40,8 @@ extern "C" {
 #define FP8B200_F16 2
 #define FP8B200_E4M3 3 /* torch.float8_e4m3fn */
 #define FP8B200_E5M2 4 /* torch.float8_e5m2 */
+#define FP8B200_E2M1 5 /* torch.float4_e2m1fn_x2: two e2m1 values per byte, element
+                          2i in the low nibble (GEMM operands only) */
 
 /* scale modes for the decoders */
 #define FP8B200_SCALE_NONE 0     /* exact conversion, scale ignored */
@@ -183,20 +185,29 @@ int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, int64_t n,
 
 /*
  * D = (A * scale_a) @ (B * scale_b)^T [+ bias] [* scale_result] -> out_dtype.
- * A: M x K float8 codes, row-major with row stride lda (bytes).
- * B: N x K float8 codes, row-major with row stride ldb (bytes): the bytes of
+ * A: M x K codes, row-major with row stride lda (bytes).
+ * B: N x K codes, row-major with row stride ldb (bytes): the bytes of
  *    torch._scaled_mm's column-major mat2 (K x N).
+ * a_dtype / b_dtype: FP8B200_E4M3, FP8B200_E5M2 or FP8B200_E2M1, chosen per
+ *    operand (mixed float4 x float8 is allowed). A float4 operand is packed
+ *    (K/2 bytes per row, element 2i in the low nibble of byte i) and needs K
+ *    a multiple of 128, a row stride that is a multiple of 32 bytes and a
+ *    32-byte aligned base.
  * scale_a / scale_b: float32 device pointers, layout FP8B200_SCALE_TENSOR or
  *    FP8B200_SCALE_ROWWISE (M values for A, N values for B).
  * bias: N values of bias_dtype (F32/BF16/F16) or NULL; scale_result: one
  *    float32 or NULL. D: M x N of out_dtype (F32/BF16/F16/E4M3/E5M2), row
  *    stride ldd elements. K must be a positive multiple of 16; lda/ldb
  *    multiples of 16; A and B 16-byte aligned.
- * Accumulation is float32 on the tcgen05 tensor cores.
+ * Accumulation is float32 on the tcgen05 tensor cores (kind::f8f6f4, which
+ * takes e4m3, e5m2 and e2m1 operands at the same rate).
  * Replaces the reference's _scaled_mm override (ops.py:33-49) and the GEMM
  * kernels behind it: fp8_scaled_matmul_kernel (shaders/fp8_matmul.metal:
  * 145-180), fp8_scaled_vecmat_kernel (:183-226) and the decode+fp16-matmul
- * fast path (fp8_mps_native.py:129-159).
+ * fast path (fp8_mps_native.py:129-159). The float4 operands extend it to the
+ * reference's packed FP4 format (shaders/fp8_matmul.metal:77-102, produced by
+ * fp4_quantize, fp8_mps_native.py:200-221), which the reference can only
+ * decode, never multiply.
  */
 int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda,
                       const void *B, int b_dtype, int64_t ldb,
@@ -247,7 +258,9 @@ int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64_t lda, int
 /*
  * Device-side status of the scaled GEMM on the current device: 0 if no
  * bounded wait has timed out, else FP8B200_ETIMEOUT with *status_out holding
- * the site code. Synchronises the device. `reset` clears the word.
+ * the site code of the last launch that timed out (that launch's output is
+ * incomplete). A timeout affects only its own launch: later launches run to
+ * completion. Synchronises the device. `reset` clears the word.
  * (Failure reporting for the GEMM's bounded waits; the reference has none.)
  */
 int fp8b200_gemm_status(uint32_t *status_out, int reset);
@@ -257,7 +270,8 @@ int fp8b200_gemm_status(uint32_t *status_out, int reset);
  * fp8b200_linear_fp8w kernel: skip_first_load != 0 makes the producer never
  * fill the first pipeline stage, so the consumers' waits run out after
  * wait_timeout_ns (0 = the default of 2 s) and the kernel returns with the
- * status word set. Not for production use.
+ * status word set. Applies to launches from the calling host thread only.
+ * Not for production use.
  */
 int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
 
@@ -271,7 +285,7 @@ int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
  * (tiles of 256 rows of A when M > 256), 4 = always CTA-pair 256x512.
  * Path 3 also sends fp8b200_linear_fp8w calls with M <= 16 to its tcgen05
  * small-M kernel instead of the warp-level MMA kernel.
- * Process-wide; for tests and tuning.
+ * Applies to launches from the calling host thread only; for tests and tuning.
  */
 int fp8b200_gemm_set_path(int path);
 

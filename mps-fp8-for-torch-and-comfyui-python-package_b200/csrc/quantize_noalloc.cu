@@ -18,7 +18,6 @@
 
 #include <cuda_fp16.h>
 
-#include <mutex>
 
 namespace fp8b200 {
 namespace noalloc {
@@ -44,15 +43,64 @@ __device__ __forceinline__ uint32_t abs_bits(const void *src, int64_t i) {
   }
 }
 
+// |x| bits of the 16-byte unit q: f32 as float bits; 16-bit formats as their
+// own magnitude bits (bf16 << 16 is its float; f16 bits order like values,
+// NaN above inf), converted to float bits once per thread at the end.
+template <int SRC>
+__device__ __forceinline__ uint32_t unit_abs_max(const uint4 q) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    if constexpr (SRC == FP8B200_F32) {
+      m = max(m, w[j] & 0x7FFFFFFFu);
+    } else {
+      m = max(m, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));
+    }
+  }
+  return m;
+}
+
+template <int SRC>
+__device__ __forceinline__ uint32_t to_float_bits(uint32_t m16_or_f32) {
+  if constexpr (SRC == FP8B200_F32) return m16_or_f32;
+  else if constexpr (SRC == FP8B200_BF16) return m16_or_f32 << 16;
+  else return __float_as_uint(__half2float(__ushort_as_half((uint16_t)m16_or_f32))) & 0x7FFFFFFFu;
+}
+
 // One block per slice: partials[b] = max |x| over slice b, as float bits
 // (NaN sorts above inf, so a NaN anywhere wins, as in the allocating path).
-template <int SRC>
+// VEC: 16-byte loads, four in flight per thread (the slice starts on a
+// 16-byte boundary when src does: 65536 elements of 2 or 4 bytes), scalar
+// loads for the last partial unit; otherwise element by element.
+template <int SRC, bool VEC>
 __global__ void __launch_bounds__(kThreads)
 slice_amax_kernel(const void *__restrict__ src, int64_t n, uint32_t *__restrict__ partials) {
   const int64_t begin = (int64_t)blockIdx.x * kSliceElems;
   const int64_t end = min(n, begin + kSliceElems);
-  uint32_t m = 0;
-  for (int64_t i = begin + threadIdx.x; i < end; i += kThreads) m = max(m, abs_bits<SRC>(src, i));
+  uint32_t m = 0;  // magnitude bits in the source format
+  if constexpr (VEC) {
+    constexpr int per = SRC == FP8B200_F32 ? 4 : 8;  // elements per 16-byte unit
+    constexpr int esz = SRC == FP8B200_F32 ? 4 : 2;
+    const uint4 *v = reinterpret_cast<const uint4 *>(static_cast<const char *>(src) + begin * esz);
+    const int nvec = (int)((end - begin) / per);
+    int j = threadIdx.x;
+    for (; j + 3 * kThreads < nvec; j += 4 * kThreads) {
+      const uint4 q0 = __ldg(v + j), q1 = __ldg(v + j + kThreads), q2 = __ldg(v + j + 2 * kThreads),
+                  q3 = __ldg(v + j + 3 * kThreads);
+      m = max(max(m, unit_abs_max<SRC>(q0)), max(unit_abs_max<SRC>(q1), max(unit_abs_max<SRC>(q2),
+                                                                               unit_abs_max<SRC>(q3))));
+    }
+    for (; j < nvec; j += kThreads) m = max(m, unit_abs_max<SRC>(__ldg(v + j)));
+    for (int64_t i = begin + (int64_t)nvec * per + threadIdx.x; i < end; i += kThreads) {
+      const uint32_t b = SRC == FP8B200_F32 ? reinterpret_cast<const uint32_t *>(src)[i] & 0x7FFFFFFFu
+                                            : reinterpret_cast<const uint16_t *>(src)[i] & 0x7FFFu;
+      m = max(m, b);
+    }
+    m = to_float_bits<SRC>(m);
+  } else {
+    for (int64_t i = begin + threadIdx.x; i < end; i += kThreads) m = max(m, abs_bits<SRC>(src, i));
+  }
   m = __reduce_max_sync(0xFFFFFFFFu, m);
   __shared__ uint32_t warp_max[kThreads / 32];
   if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
@@ -88,23 +136,17 @@ scale_from_partials_kernel(const uint32_t *__restrict__ partials, int nslices, f
   }
 }
 
-// Device address of the scratch array, looked up once per device with that
-// device current.
-constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
-uint32_t *g_ptr[kMaxDevices] = {};
-cudaError_t g_lookup_err[kMaxDevices] = {};
-
-int scratch_ptr(int dev, uint32_t **out) {
-  std::call_once(g_once[dev], [dev] {
-    void *p = nullptr;
-    g_lookup_err[dev] = cudaGetSymbolAddress(&p, g_amax_partials);
-    g_ptr[dev] = static_cast<uint32_t *>(p);
-  });
-  if (g_lookup_err[dev] != cudaSuccess || g_ptr[dev] == nullptr)
-    return set_error(FP8B200_ELAUNCH, "quantize_noalloc: cudaGetSymbolAddress failed: %s",
-                     cudaGetErrorString(g_lookup_err[dev]));
-  *out = g_ptr[dev];
+// Device address of the scratch array on the current device. Looked up on
+// every call: after the first call on a device (which loads this library's
+// device code there, and so must come before any stream capture) the lookup
+// is a cheap host query, and it stays right if the context is ever
+// recreated (cudaDeviceReset) and the array lands at another address.
+int scratch_ptr(uint32_t **out) {
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_amax_partials);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(FP8B200_ELAUNCH, "quantize_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  *out = static_cast<uint32_t *>(p);
   return FP8B200_OK;
 }
 
@@ -130,15 +172,22 @@ extern "C" int fp8b200_quantize_fp8_noalloc(const void *src, int src_dtype, void
   if (n > 0 && (!src || !dst)) return set_error(FP8B200_EINVAL, "quantize_noalloc: null pointer");
   int dev;
   if (int rc = check_device(&dev)) return rc;
-  if (dev >= kMaxDevices) return set_error(FP8B200_EDEVICE, "quantize_noalloc: device index %d too large", dev);
   uint32_t *partials;
-  if (int rc = scratch_ptr(dev, &partials)) return rc;
+  if (int rc = scratch_ptr(&partials)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   const int nslices = (int)((n + kSliceElems - 1) / kSliceElems);
   if (nslices > 0) {
-    if (src_dtype == FP8B200_F32) slice_amax_kernel<FP8B200_F32><<<nslices, kThreads, 0, st>>>(src, n, partials);
-    else if (src_dtype == FP8B200_BF16) slice_amax_kernel<FP8B200_BF16><<<nslices, kThreads, 0, st>>>(src, n, partials);
-    else slice_amax_kernel<FP8B200_F16><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+    if (src_dtype == FP8B200_F32) {
+      if (vec) slice_amax_kernel<FP8B200_F32, true><<<nslices, kThreads, 0, st>>>(src, n, partials);
+      else slice_amax_kernel<FP8B200_F32, false><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    } else if (src_dtype == FP8B200_BF16) {
+      if (vec) slice_amax_kernel<FP8B200_BF16, true><<<nslices, kThreads, 0, st>>>(src, n, partials);
+      else slice_amax_kernel<FP8B200_BF16, false><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    } else {
+      if (vec) slice_amax_kernel<FP8B200_F16, true><<<nslices, kThreads, 0, st>>>(src, n, partials);
+      else slice_amax_kernel<FP8B200_F16, false><<<nslices, kThreads, 0, st>>>(src, n, partials);
+    }
     count_launch();
     if (int rc = check_launch("quantize_noalloc amax")) return rc;
   }

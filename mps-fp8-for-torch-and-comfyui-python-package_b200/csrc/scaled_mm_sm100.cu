@@ -31,6 +31,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -63,6 +64,8 @@ struct Params {
   int vec_store;
   uint32_t idesc;
   unsigned long long timeout_ns;
+  uint32_t epoch;                             // launch number: scopes the status word to this launch
+  uint32_t tx_bytes;                          // TMA bytes per stage credited to this CTA's full barrier
   int debug_skip_first_load;
   int sk_mt, sk_stages, sk_cs, sk_tmem_cols;  // small-M kernel: rows per tile, ring depth, split-K cluster, TMEM
   int tma_store;                              // epilogue stores through the output tensor map
@@ -71,8 +74,12 @@ struct Params {
   int act_f16;                                // fp8-weight linear: activations f16 (1) or bf16 (0)
 };
 
-// Status word: 0 = ok, otherwise (1 << 31) | site of the first wait that timed out.
-__device__ uint32_t g_status;
+// Status word: 0 = ok, otherwise (launch epoch << 32) | (1 << 31) | site of
+// the first wait that timed out in that launch. A launch gives up early only
+// on a failure recorded under its own epoch, so a timed-out launch leaves
+// every later launch unaffected; the word keeps the last failure until
+// fp8b200_gemm_status() resets it.
+__device__ unsigned long long g_status;
 
 // ------------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -105,15 +112,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait on phase `parity` of `bar`; false on timeout or if another
 // role already recorded a failure.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long timeout_ns, uint32_t site) {
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long timeout_ns, uint32_t epoch,
+                                       uint32_t site) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((n & 31u) == 0) {
-      if (*reinterpret_cast<volatile uint32_t *>(&g_status) != 0) return false;
+      unsigned long long s = *reinterpret_cast<volatile unsigned long long *>(&g_status);
+      if ((uint32_t)(s >> 32) == epoch) return false;  // another role of this launch gave up
       if (globaltimer() - t0 > timeout_ns) {
-        atomicCAS(&g_status, 0u, 0x80000000u | site);
+        // record the first failure of this launch, replacing an older launch's record
+        const unsigned long long mine = ((unsigned long long)epoch << 32) | 0x80000000ull | site;
+        while ((uint32_t)(s >> 32) != epoch) {
+          const unsigned long long prev = atomicCAS(&g_status, s, mine);
+          if (prev == s) break;
+          s = prev;
+        }
         return false;
       }
     }
@@ -512,9 +527,9 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         int tm, tn;
         tile_coords(p, tile, tm, tn);
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, p.epoch, 1)) { ok = false; break; }
           if (p.debug_skip_first_load) { ok = false; break; }  // test hook: never fill stage 0
-          mbar_expect_tx(full_bar(stage), STAGE_BYTES);
+          mbar_expect_tx(full_bar(stage), p.tx_bytes);
           tma_load_2d(sA + stage * A_BYTES, &tmap_a, full_bar(stage), kb * BK, tm * BM);
           tma_load_2d(sB + stage * B_BYTES, &tmap_b, full_bar(stage), kb * BK, tn * BN);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -530,11 +545,11 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, p.epoch, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, p.epoch, 3)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = sdesc_sw128_kmajor(sA + stage * A_BYTES);
           const uint64_t bdesc = sdesc_sw128_kmajor(sB + stage * B_BYTES);
@@ -569,7 +584,7 @@ scaled_mm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       epilogue_sync();
       // warp-uniform bounded wait
       int ok = 0;
-      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, p.epoch, 4) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -730,10 +745,10 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         const int arow = tm * (2 * BM) + (int)rank * BM;
         const int brow = tn * PAIR_BN + (int)rank * HALF_B;
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, p.epoch, 1)) { ok = false; break; }
           if (p.debug_skip_first_load) { ok = false; break; }
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
-          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * STAGE2_BYTES);
+          if (rank == 0) mbar_expect_tx(full_bar(stage), p.tx_bytes);
           tma_load_2d_pair(sA + stage * A2_BYTES, &tmap_a, leader_full, kb * BK, arow);
           tma_load_2d_pair(sB + stage * B2_BYTES, &tmap_b, leader_full, kb * BK, brow);
           if (++stage == nst) { stage = 0; phase ^= 1u; }
@@ -749,11 +764,11 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
-        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, p.epoch, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * PAIR_BN);
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, p.epoch, 3)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = sdesc_sw128_kmajor(sA + stage * A2_BYTES);
           const uint64_t bdesc = sdesc_sw128_kmajor(sB + stage * B2_BYTES);
@@ -785,7 +800,7 @@ scaled_mm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       stage_columns(p, tn * PAIR_BN, sb_t, s_scale, s_bias, etid);
       epilogue_sync();
       int ok = 0;
-      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, p.epoch, 4) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -906,10 +921,10 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         const int arow = tm * (2 * BM) + (int)rank * BM;
         const int brow0 = tn * WIDE_BN + (int)rank * HALF_B;
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, p.epoch, 1)) { ok = false; break; }
           if (p.debug_skip_first_load) { ok = false; break; }
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
-          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * W_STAGE_BYTES);
+          if (rank == 0) mbar_expect_tx(full_bar(stage), p.tx_bytes);
           const uint32_t st = stage_a(stage);
           const int kx = kb * p.kb_elems;  // tensor-map coordinate of the k-block
           tma_load_2d_pair(st, &tmap_a, leader_full, kx, arow);
@@ -932,13 +947,13 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       bool ok = true;
       for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
         const int head = min(W_STAGES, p.num_kb);  // k-blocks issued in two passes
-        if (!mbar_wait(tempty_bar(0), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        if (!mbar_wait(tempty_bar(0), acc_phase ^ 1u, p.timeout_ns, p.epoch, 2)) break;
         tc_fence_after();
         {
           int st = stage;
           uint32_t ph = phase;
           for (int kb = 0; kb < head; kb++) {
-            if (!mbar_wait(full_bar(st), ph, p.timeout_ns, 3)) { ok = false; break; }
+            if (!mbar_wait(full_bar(st), ph, p.timeout_ns, p.epoch, 3)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sa = stage_a(st);
             const uint64_t adesc = sdesc_sw128_kmajor(sa);
@@ -952,7 +967,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           }
         }
         if (!ok) break;
-        if (!mbar_wait(tempty_bar(1), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        if (!mbar_wait(tempty_bar(1), acc_phase ^ 1u, p.timeout_ns, p.epoch, 2)) break;
         tc_fence_after();
         for (int kb = 0; kb < head; kb++) {  // same stages, already full
           const uint32_t sa = stage_a(stage);
@@ -972,7 +987,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         // half-1 MMAs (stages still resident), then half 1 is complete
         const int tail = min(W_STAGES, p.num_kb - head);
         for (int kb = head; kb < p.num_kb - tail; kb++) {
-          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, p.epoch, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = stage_a(stage);
           const uint64_t adesc = sdesc_sw128_kmajor(sa);
@@ -992,7 +1007,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           int st = stage;
           uint32_t ph = phase;
           for (int t = 0; t < tail; t++) {
-            if (!mbar_wait(full_bar(st), ph, p.timeout_ns, 3)) { ok = false; break; }
+            if (!mbar_wait(full_bar(st), ph, p.timeout_ns, p.epoch, 3)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sa = stage_a(st);
             const uint64_t adesc = sdesc_sw128_kmajor(sa);
@@ -1051,7 +1066,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       int ok = 1;
 #pragma unroll 1
       for (int h = 0; h < 2 && ok; h++) {  // drain each half once it is complete; release it once read
-        if (lane == 0) ok = mbar_wait(tfull_bar(h), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+        if (lane == 0) ok = mbar_wait(tfull_bar(h), acc_phase, p.timeout_ns, p.epoch, 4) ? 1 : 0;
         ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         if (!ok) break;
         tc_fence_after();
@@ -1240,7 +1255,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       int stage = 0;
       uint32_t phase = 0;
       for (int kb = kb0; kb < kb1; kb++) {
-        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) break;
+        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, p.epoch, 1)) break;
         if (p.debug_skip_first_load) break;  // test hook: never fill stage 0
         const uint32_t st = base + (uint32_t)stage * stage_bytes;
         const int kx = kb * p.kb_elems;  // tensor-map coordinate of the k-block
@@ -1248,7 +1263,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
           mbar_expect_tx(full_bar(stage), a_bytes + SK_B_BYTES / 2);
           tma_load_2d(st + SK_B_BYTES + a_bytes, &tmap_b, full_bar(stage), kx, tn * SK_BN);  // raw weights
         } else {
-          mbar_expect_tx(full_bar(stage), stage_bytes);
+          mbar_expect_tx(full_bar(stage), p.tx_bytes);
           tma_load_2d(st, &tmap_b, full_bar(stage), kx, tn * SK_BN);
         }
         tma_load_2d(st + SK_B_BYTES, &tmap_a, full_bar(stage), kx, tm * MT);
@@ -1263,7 +1278,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       bool fine = true;
       for (int kb = kb0; kb < kb1; kb++) {
         // W8: the converters saw the stage land before converting it
-        if (!mbar_wait(W8 ? conv_bar(stage) : full_bar(stage), phase, p.timeout_ns, 3)) { fine = false; break; }
+        if (!mbar_wait(W8 ? conv_bar(stage) : full_bar(stage), phase, p.timeout_ns, p.epoch, 3)) { fine = false; break; }
         tc_fence_after();
         const uint32_t st = base + (uint32_t)stage * stage_bytes;
         const uint64_t wdesc = sdesc_sw128_kmajor(st);
@@ -1298,7 +1313,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
         const int stage = i % S;
         const uint32_t phase = (uint32_t)(i / S) & 1u;
         int got = 0;
-        if (lane == 0) got = mbar_wait(full_bar(stage), phase, p.timeout_ns, 5) ? 1 : 0;
+        if (lane == 0) got = mbar_wait(full_bar(stage), phase, p.timeout_ns, p.epoch, 5) ? 1 : 0;
         got = __shfl_sync(0xFFFFFFFFu, got, 0);
         if (!got) { cok = false; break; }
         const uint32_t st = base + (uint32_t)stage * stage_bytes;
@@ -1323,7 +1338,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
       const long long row = (long long)tm * MT + t;
       s_rs[t] = p.sa_rowwise ? (row < p.M ? __ldg(p.sa + row) : 0.0f) : sa_t;
     }
-    if (lane == 0) ok = mbar_wait(tfull, 0, p.timeout_ns, 4) ? 1 : 0;
+    if (lane == 0) ok = mbar_wait(tfull, 0, p.timeout_ns, p.epoch, 4) ? 1 : 0;
     ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
     tc_fence_after();
     if (ok) {
@@ -1607,7 +1622,7 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
         const int xrow = tm * (2 * BM) + (int)rank * BM;
         const int wrow = tn * PAIR_BN + (int)rank * HALF_B;
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, 1)) { ok = false; break; }
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, p.epoch, 1)) { ok = false; break; }
           if (p.debug_skip_first_load) { ok = false; break; }
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
           if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * LW_A_BYTES);
@@ -1627,12 +1642,12 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = pair; tile < p.num_tiles && ok; tile += npairs) {
-        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, 2)) break;
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, p.epoch, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * PAIR_BN);
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, 3)) { ok = false; break; }
-          if (!mbar_wait(conv_bar(cs), cphase, p.timeout_ns, 7)) { ok = false; break; }
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, p.epoch, 3)) { ok = false; break; }
+          if (!mbar_wait(conv_bar(cs), cphase, p.timeout_ns, p.epoch, 7)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = sdesc_sw128_kmajor(sx(stage));
           const uint64_t bdesc = sdesc_sw128_kmajor(sw(cs));
@@ -1668,7 +1683,7 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
         const uint32_t phase = (it / LW_LOADS) & 1u, cphase = (it / LW_CONVS) & 1u;
         int got = 0;
         if (lane == 0)
-          got = mbar_wait(rfull_bar(stage), phase, p.timeout_ns, 5) && mbar_wait(cempty_bar(cs), cphase ^ 1u, p.timeout_ns, 6)
+          got = mbar_wait(rfull_bar(stage), phase, p.timeout_ns, p.epoch, 5) && mbar_wait(cempty_bar(cs), cphase ^ 1u, p.timeout_ns, p.epoch, 6)
                     ? 1 : 0;
         got = __shfl_sync(0xFFFFFFFFu, got, 0);
         if (!got) { ok = false; break; }
@@ -1702,7 +1717,7 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
       stage_columns(p, tn * PAIR_BN, sb_t, s_scale, s_bias, etid);
       epilogue_sync();
       int ok = 0;
-      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, 4) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, p.epoch, 4) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -1742,14 +1757,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows);
+int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows, bool fp4);
 
 // Tensor maps describe only an address, extents, a stride and a box, so an
 // encoded map stays valid for any later call with the same five values. A
 // small per-thread cache skips the driver's encode on repeated calls (the
 // decode-time case: the same weights and activation buffers every step).
-int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows) {
-  struct Entry { const void *ptr; int64_t rows, k, ld; int box; int dev; CUtensorMap map; };
+int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows,
+                    bool fp4 = false) {
+  struct Entry { const void *ptr; int64_t rows, k, ld; int box; int dev; bool fp4; CUtensorMap map; };
   constexpr int kEntries = 32;
   thread_local Entry cache[kEntries];
   thread_local int used = 0, next = 0;
@@ -1757,12 +1773,13 @@ int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, in
   cudaGetDevice(&dev);
   for (int i = 0; i < used; i++) {
     const Entry &e = cache[i];
-    if (e.ptr == ptr && e.rows == rows && e.k == k && e.ld == ld && e.box == box_rows && e.dev == dev) {
+    if (e.ptr == ptr && e.rows == rows && e.k == k && e.ld == ld && e.box == box_rows && e.dev == dev &&
+        e.fp4 == fp4) {
       *m = e.map;
       return FP8B200_OK;
     }
   }
-  if (int rc = encode_kmajor_map(m, ptr, rows, k, ld, box_rows)) return rc;
+  if (int rc = encode_kmajor_map(m, ptr, rows, k, ld, box_rows, fp4)) return rc;
   int slot;
   if (used < kEntries) {
     slot = used++;
@@ -1770,18 +1787,29 @@ int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, in
     slot = next;
     next = (next + 1) % kEntries;
   }
-  cache[slot] = Entry{ptr, rows, k, ld, box_rows, dev, *m};
+  cache[slot] = Entry{ptr, rows, k, ld, box_rows, dev, fp4, *m};
   return FP8B200_OK;
 }
 
-int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+// K-major operand map: boxes of 128 k-values x box_rows rows, 128-byte
+// swizzle. fp8 codes land as they are (128 bytes per box row). Packed FP4
+// (e2m1, two values per byte, k-value 2i in the low nibble) is read as
+// 16U4_ALIGN16B: every 8 bytes (16 values) of a row land in a 16-byte unit of
+// shared memory followed by 8 bytes of padding, the layout tcgen05.mma
+// kind::f8f6f4 reads 4-bit operands in; the box row is again 128 bytes, so
+// the kernels' stage layout and descriptors are the fp8 ones. The TMA
+// transaction counts the 64 bytes of packed data per box row, not the
+// padding. Requirements (checked by the caller): k a multiple of 128, ld a
+// multiple of 32 bytes, a 32-byte aligned base.
+int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows, bool fp4) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld};
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                   const_cast<void *>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FP8B200_EINVAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -1912,7 +1940,7 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
       for (int kb = 0; kb < nblk; kb++) {
         const int st = kb % GV_STAGES;
         const uint32_t ph = (uint32_t)((kb / GV_STAGES) & 1);
-        if (!mbar_wait(empty_bar(st), ph ^ 1u, p.timeout_ns, 20)) break;
+        if (!mbar_wait(empty_bar(st), ph ^ 1u, p.timeout_ns, p.epoch, 20)) break;
         if (p.debug_skip_first_load) break;  // test hook: no tile ever lands, the consumers' waits run out
         mbar_expect_tx(full_bar(st), GV_TILE);
         tma_load_2d(ring + (uint32_t)(st * GV_TILE), &tmap_w, full_bar(st), (int)(k0 + (int64_t)kb * GV_BK), n0);
@@ -1946,7 +1974,7 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
           const uint4 q = xin[u] ? __ldg(xr[u] + kb * (GV_BK / 8) + v) : make_uint4(0, 0, 0, 0);
           xv[u][4 * v] = q.x; xv[u][4 * v + 1] = q.y; xv[u][4 * v + 2] = q.z; xv[u][4 * v + 3] = q.w;
         }
-      const bool landed = mbar_wait(full_bar(st), ph, p.timeout_ns, 21);  // every lane waits (visibility)
+      const bool landed = mbar_wait(full_bar(st), ph, p.timeout_ns, p.epoch, 21);  // every lane waits (visibility)
       if (!__all_sync(0xFFFFFFFFu, landed)) break;                         // and the warp leaves as one
       uint4 raw[2][2];
       const uint32_t tile = ring + (uint32_t)(st * GV_TILE);
@@ -2015,9 +2043,20 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
   cluster_sync();  // no CTA leaves while a peer may still read its partial sums
 }
 
-unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
-int g_debug_skip_first_load = 0;
-int g_path = 0;  // 0 = by shape, 1 = single-CTA, 2 = CTA-pair 256x256, 3 = small-M, 4 = CTA-pair 256x512
+// Test and tuning hooks, per host thread: a hook set by one thread (a test,
+// a tuning sweep) never changes the launches of another thread (one thread
+// per GPU is the supported threading model).
+thread_local unsigned long long g_timeout_ns = 2000000000ull;  // 2 s per wait
+thread_local int g_debug_skip_first_load = 0;
+thread_local int g_path = 0;  // 0 = by shape, 1 = single-CTA, 2 = CTA-pair 256x256, 3 = small-M, 4 = CTA-pair 256x512
+
+// Launch numbers for the status word (never 0, which means "no failure").
+uint32_t next_epoch() {
+  static std::atomic<uint32_t> counter{0};
+  uint32_t e;
+  do e = counter.fetch_add(1, std::memory_order_relaxed) + 1; while (e == 0);
+  return e;
+}
 
 // Resident 2-CTA clusters of the pair kernel (wide = false) or the wide
 // kernel (wide = true) on device `dev`.
@@ -2118,7 +2157,10 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
                                  const float *scale_b, int scale_b_layout, const void *bias, int bias_dtype,
                                  const float *scale_result, void *D, int out_dtype, int64_t ldd, void *stream) {
   auto fp8 = [](int d) { return d == FP8B200_E4M3 || d == FP8B200_E5M2; };
-  if (!fp8(a_dtype) || !fp8(b_dtype)) return set_error(FP8B200_EINVAL, "scaled_mm: operands must be e4m3fn/e5m2");
+  auto operand = [&](int d) { return fp8(d) || d == FP8B200_E2M1; };
+  if (!operand(a_dtype) || !operand(b_dtype))
+    return set_error(FP8B200_EINVAL, "scaled_mm: operands must be e4m3fn, e5m2 or e2m1 (packed float4)");
+  const bool a4 = a_dtype == FP8B200_E2M1, b4 = b_dtype == FP8B200_E2M1;
   if (out_dtype != FP8B200_F32 && out_dtype != FP8B200_BF16 && out_dtype != FP8B200_F16 && !fp8(out_dtype))
     return set_error(FP8B200_EINVAL, "scaled_mm: unsupported output dtype %d", out_dtype);
   if (M < 0 || N < 0 || K < 0) return set_error(FP8B200_EINVAL, "scaled_mm: negative size");
@@ -2127,11 +2169,18 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   if (K % 16) return set_error(FP8B200_EINVAL, "scaled_mm: K=%lld must be a multiple of 16", (long long)K);
   if (M > 0x7FFFFFFFLL || N > 0x7FFFFFFFLL || K > 0x7FFFFFFFLL)
     return set_error(FP8B200_EINVAL, "scaled_mm: dimension too large");
-  if (lda < K || ldb < K || (lda % 16) || (ldb % 16))
-    return set_error(FP8B200_EINVAL, "scaled_mm: row strides must be >= K and multiples of 16 bytes");
+  if ((a4 || b4) && K % 128)
+    return set_error(FP8B200_EINVAL, "scaled_mm: K=%lld must be a multiple of 128 with a float4 operand", (long long)K);
+  // row strides in bytes: K codes per row for float8, K/2 packed bytes for float4
+  const int64_t a_row = a4 ? K / 2 : K, b_row = b4 ? K / 2 : K;
+  if (lda < a_row || ldb < b_row || (lda % (a4 ? 32 : 16)) || (ldb % (b4 ? 32 : 16)))
+    return set_error(FP8B200_EINVAL,
+                     "scaled_mm: row strides must cover a row and be multiples of 16 bytes (32 for float4)");
   if (ldd < N) return set_error(FP8B200_EINVAL, "scaled_mm: output row stride < N");
   if (!A || !B || !D || !scale_a || !scale_b) return set_error(FP8B200_EINVAL, "scaled_mm: null pointer");
   if (!aligned16(A) || !aligned16(B)) return set_error(FP8B200_EINVAL, "scaled_mm: operands must be 16-byte aligned");
+  if ((a4 && (reinterpret_cast<uintptr_t>(A) & 31)) || (b4 && (reinterpret_cast<uintptr_t>(B) & 31)))
+    return set_error(FP8B200_EINVAL, "scaled_mm: float4 operands must be 32-byte aligned");
   if ((scale_a_layout != FP8B200_SCALE_TENSOR && scale_a_layout != FP8B200_SCALE_ROWWISE) ||
       (scale_b_layout != FP8B200_SCALE_TENSOR && scale_b_layout != FP8B200_SCALE_ROWWISE))
     return set_error(FP8B200_EINVAL, "scaled_mm: unknown scale layout");
@@ -2158,8 +2207,9 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   // small-M kernel: MT rows of A per tile (M rounded up to 16, at most 256)
   const int mt = skinny ? (int)std::min<int64_t>(SK_MAX_MT, (M + 15) / 16 * 16) : 0;
   CUtensorMap ma, mb;
-  if (int rc = make_kmajor_map(&ma, A, M, K, lda, skinny ? mt : BM)) return rc;
-  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, skinny ? SK_BN : (pair ? HALF_B : BN))) return rc;
+  const int a_box = skinny ? mt : BM, b_box = skinny ? SK_BN : (pair ? HALF_B : BN);
+  if (int rc = make_kmajor_map(&ma, A, M, K, lda, a_box, a4)) return rc;
+  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, b_box, b4)) return rc;
 
   Params p;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
@@ -2181,11 +2231,19 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
   const int esz = dtype_size(out_dtype);
   p.vec_store = aligned16(D) && ((ldd * esz) % 16 == 0);
-  const uint32_t afmt = a_dtype == FP8B200_E5M2 ? 1u : 0u, bfmt = b_dtype == FP8B200_E5M2 ? 1u : 0u;
+  // kind::f8f6f4 operand formats: 0 e4m3, 1 e5m2, 5 e2m1
+  auto mma_fmt = [](int d) { return d == FP8B200_E5M2 ? 1u : d == FP8B200_E2M1 ? 5u : 0u; };
+  const uint32_t afmt = mma_fmt(a_dtype), bfmt = mma_fmt(b_dtype);
+  // TMA bytes per stage: a box row carries 128 bytes of float8 or 64 bytes of packed float4; the CTA
+  // pairs credit both CTAs' loads to the leader's barrier
+  const uint32_t a_rb = a4 ? 64u : 128u, b_rb = b4 ? 64u : 128u;
+  p.tx_bytes = (uint32_t)a_box * a_rb + (uint32_t)b_box * b_rb * (wide ? 2u : 1u);
+  if (pair) p.tx_bytes *= 2u;
   // instruction descriptor: f32 accumulate, A/B formats, both K-major, N>>3, M>>4
   const uint32_t mma_m = pair ? 2 * BM : BM;
   p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((mma_m >> 4) << 24);
   p.timeout_ns = g_timeout_ns;
+  p.epoch = next_epoch();
   p.debug_skip_first_load = g_debug_skip_first_load;
   p.sk_mt = mt;
   p.kb_elems = BK;
@@ -2241,12 +2299,13 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
 }
 
 extern "C" int fp8b200_gemm_status(uint32_t *status_out, int reset) {
-  uint32_t v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+  unsigned long long w = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&w, g_status, sizeof(w));
   if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "gemm status read: %s", cudaGetErrorString(e));
+  const uint32_t v = (uint32_t)w;  // the site code; the launch epoch is internal
   if (status_out) *status_out = v;
   if (reset) {
-    const uint32_t z = 0;
+    const unsigned long long z = 0;
     e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "gemm status reset: %s", cudaGetErrorString(e));
   }
@@ -2339,6 +2398,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
       p.sk_cs = ks;
       p.timeout_ns = g_timeout_ns;
+  p.epoch = next_epoch();
       p.debug_skip_first_load = g_debug_skip_first_load;
       const bool f16 = x_dtype == FP8B200_F16;
       using GvKernel = void (*)(const CUtensorMap, const uint16_t *, int64_t, int, int, int, const Params);
@@ -2410,6 +2470,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     const uint32_t fmt = p.act_f16 ? 0u : 1u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(mt >> 3) << 17) | ((uint32_t)(SK_BN >> 4) << 24);
     p.timeout_ns = g_timeout_ns;
+  p.epoch = next_epoch();
     p.debug_skip_first_load = g_debug_skip_first_load;
     p.sk_mt = mt;
     const int stage_bytes = SK_B_BYTES + mt * BK + SK_B_BYTES / 2;
@@ -2465,6 +2526,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
   const uint32_t fmt = p.act_f16 ? 0u : 1u;  // kind::f16 operand type: 0 = f16, 1 = bf16
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(PAIR_BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
   p.timeout_ns = g_timeout_ns;
+  p.epoch = next_epoch();
   p.debug_skip_first_load = g_debug_skip_first_load;
   const int clusters = std::min(p.num_tiles, current_sm_count() / 2);
   linear_fp8w_kernel<<<2 * clusters, LW_THREADS, LW_SMEM_BYTES, (cudaStream_t)stream>>>(mx, mw, p);
@@ -2516,6 +2578,7 @@ extern "C" int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64
   memset(&p, 0, sizeof(p));
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.kb_elems = 64;
+  p.tx_bytes = 2 * W_STAGE_BYTES;
   p.num_kb = (int)((K + 63) / 64);
   p.tiles_m = (int)((M + 2 * BM - 1) / (2 * BM));
   p.tiles_n = (int)((N + WIDE_BN - 1) / WIDE_BN);
@@ -2529,6 +2592,7 @@ extern "C" int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64
   const uint32_t fmt = dtype == FP8B200_BF16 ? 1u : 0u;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(PAIR_BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
   p.timeout_ns = g_timeout_ns;
+  p.epoch = next_epoch();
   p.debug_skip_first_load = g_debug_skip_first_load;
   const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
   scaled_mm_wide_kernel<1><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);

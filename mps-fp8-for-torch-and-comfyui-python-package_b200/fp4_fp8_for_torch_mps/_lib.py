@@ -17,7 +17,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libfp8_b200.so")
 
 # dtype codes of include/fp8_b200.h
-F32, BF16, F16, E4M3, E5M2 = 0, 1, 2, 3, 4
+F32, BF16, F16, E4M3, E5M2, E2M1 = 0, 1, 2, 3, 4, 5
 SCALE_NONE, SCALE_F32, SCALE_F16_REF = 0, 1, 2
 SCALE_TENSOR, SCALE_ROWWISE = 0, 1
 ETIMEOUT = -4
@@ -28,6 +28,7 @@ _CODE = {
     torch.float16: F16,
     torch.float8_e4m3fn: E4M3,
     torch.float8_e5m2: E5M2,
+    torch.float4_e2m1fn_x2: E2M1,
 }
 
 _lock = threading.Lock()

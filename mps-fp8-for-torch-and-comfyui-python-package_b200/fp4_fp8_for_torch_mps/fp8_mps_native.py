@@ -12,7 +12,8 @@ current CUDA device, as the reference moves them to "mps".
 Additions beyond the reference (used by the aten overrides in ops.py):
 `encode_fp8` / `decode_fp8` for both fp8 formats and any float dtype,
 `quantize_fp8`, `fp4_decode` (shape-preserving, any float dtype, f32
-scale), and `scaled_mm` with torch._scaled_mm's full argument set.
+scale), `scaled_mm` with torch._scaled_mm's full argument set, and
+`fp4_scaled_mm` (packed FP4 operands multiplied on the tensor cores).
 """
 from __future__ import annotations
 
@@ -410,13 +411,17 @@ def scaled_mm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: torch.Tensor, scale_
     """D = (A * scale_a) @ (B * scale_b)^T [+ bias] [* scale_result].
 
     a: (M, K) fp8 codes, rows contiguous; b_nk: (N, K) fp8 codes, rows
-    contiguous (the bytes of torch._scaled_mm's column-major mat2).
+    contiguous (the bytes of torch._scaled_mm's column-major mat2). An
+    operand whose dtype argument is torch.float4_e2m1fn_x2 holds packed FP4
+    instead: (M, K/2) or (N, K/2) bytes, two values per byte.
     scale_a: 1 value or M values; scale_b: 1 value or N values (float32).
     """
     if a.dim() != 2 or b_nk.dim() != 2:
         raise RuntimeError("scaled_mm: inputs must be 2-D")
     M, K = a.shape
     N, Kb = b_nk.shape
+    K *= 2 if a_dtype == torch.float4_e2m1fn_x2 else 1
+    Kb *= 2 if b_dtype == torch.float4_e2m1fn_x2 else 1
     if Kb != K:
         raise RuntimeError(f"scaled_mm: K mismatch ({K} vs {Kb})")
     dev = a.device
@@ -463,6 +468,38 @@ def fp8_scaled_mm(A, B, scale_a, scale_b):
     A = _on_cuda(A)
     B = B.to(A.device)
     return scaled_mm(A, B, scale_a, scale_b, out_dtype=torch.float32)
+
+
+def _gemm_operand(t: torch.Tensor, what: str):
+    """(uint8 view, dtype) of a float4 / float8 GEMM operand: uint8 and
+    float4_e2m1fn_x2 tensors are packed FP4 bytes, float8 tensors their codes."""
+    if t.dim() != 2:
+        raise RuntimeError(f"fp4_scaled_mm: {what} must be 2-D")
+    if t.dtype in (torch.uint8, torch.float4_e2m1fn_x2):
+        return t.view(torch.uint8), torch.float4_e2m1fn_x2
+    if t.dtype in _FP8:
+        return t.view(torch.uint8), t.dtype
+    raise RuntimeError(f"fp4_scaled_mm: {what} must be packed float4 (uint8 / float4_e2m1fn_x2) or float8, "
+                       f"got {t.dtype}")
+
+
+def fp4_scaled_mm(A, B, scale_a, scale_b, out_dtype: torch.dtype = torch.float32):
+    """GEMM on packed FP4 operands: (A * scale_a) @ (B * scale_b)^T.
+
+    A: (M, K/2) packed FP4 bytes (the format fp4_encode / fp4_quantize write,
+    element 2i in the low nibble); B: (N, K/2) packed FP4 bytes or (N, K)
+    float8 codes. Scales: one value or one per row of A / column of the
+    output. Float32 accumulation on the tensor cores (tcgen05 kind::f8f6f4),
+    so the FP4 codes are multiplied as they are, never decoded to 16-bit.
+    An addition to the reference, whose FP4 path (fp8_mps_native.py:162-221)
+    ends at decoding."""
+    a, adt = _gemm_operand(_on_cuda(A), "A")
+    b, bdt = _gemm_operand(B, "B")
+    b = b.to(a.device)
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise RuntimeError("fp4_scaled_mm: operand rows must be contiguous")
+    return scaled_mm(a, b, torch.as_tensor(scale_a), torch.as_tensor(scale_b), out_dtype=out_dtype,
+                     a_dtype=adt, b_dtype=bdt)
 
 
 def fp8_scaled_mm_auto(A, B, scale_a, scale_b):

@@ -480,6 +480,21 @@ def _(x, weight, weight_scale, bias=None):
     return x.new_empty(tuple(x.shape[:-1]) + (weight.shape[0],))
 
 
+@torch.library.custom_op("fp8_mps::fp4_scaled_mm", mutates_args=())
+def fp4_scaled_mm(A: torch.Tensor, B: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                  out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """(A * scale_a) @ (B * scale_b)^T on packed FP4 operands (A: (M, K/2)
+    bytes; B: (N, K/2) bytes or (N, K) float8), float32 output by default
+    like fp8_mps::scaled_mm (an addition to the reference's seven ops)."""
+    from fp4_fp8_for_torch_mps.fp8_mps_native import fp4_scaled_mm as _mm
+    return _mm(A, B, scale_a, scale_b, out_dtype=out_dtype or torch.float32)
+
+
+@fp4_scaled_mm.register_fake
+def _(A, B, scale_a, scale_b, out_dtype=None):
+    return A.new_empty((A.shape[0], B.shape[0]), dtype=out_dtype or torch.float32)
+
+
 @torch.library.custom_op("fp8_mps::fp4_dequantize", mutates_args=())
 def fp4_dequantize(input: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     from fp4_fp8_for_torch_mps.fp8_mps_native import fp4_dequantize as _dequantize

@@ -12,6 +12,7 @@ workloads the package is measured on.
                   scale = amax/448 (M=N=K in {4096, 8192, 16384})
   scaled_mm_rowwise  rowwise e4m3: activations N(0,1) per-row, weights
                   N(0,0.02) per-column, LLM shapes
+  fp4_scaled_mm   packed FP4 operands, uniform bytes, per-tensor scales
 """
 from __future__ import annotations
 
@@ -99,6 +100,16 @@ def rowwise_operands(m: int, n: int, k: int, seed: int = 0):
     sw = (w.abs().amax(dim=1, keepdim=True) / 448.0).float()
     wq = (w / sw).to(torch.float8_e4m3fn)
     return aq, wq, sa, sw.reshape(1, n)
+
+
+def fp4_gemm_operands(m: int, n: int, k: int, seed: int = 0):
+    """Packed FP4 GEMM operands: A (M, K/2) and B (N, K/2) bytes uniform over
+    all 256 patterns (every e2m1 code in both nibbles, like the FP4 decode
+    input), per-tensor f32 scales 0.01 and 0.02."""
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randint(0, 256, (m, k // 2), dtype=torch.uint8, generator=g)
+    b = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g)
+    return a, b, torch.tensor(0.01), torch.tensor(0.02)
 
 
 # ---------------------------------------------------------------------------

@@ -26,6 +26,7 @@ _lib = None
 
 F32, BF16, F16 = 0, 1, 2
 E4M3, E5M2 = 0, 1
+FP4 = 2  # GEMM operand format: packed float4_e2m1fn_x2 (two values per byte, low nibble first)
 
 _NP_OF = {F32: np.uint32, BF16: np.uint16, F16: np.uint16}
 
@@ -203,20 +204,37 @@ def fp8_table_f64(fmt: int) -> np.ndarray:
     return bits.view(np.float32).astype(np.float64)
 
 
+def fp4_unpack_f64(packed: np.ndarray) -> np.ndarray:
+    """Values of packed FP4 rows (R, K/2) bytes as float64 (R, K): byte i
+    gives elements 2i (low nibble) and 2i+1 (high nibble), the nibble order of
+    shaders/fp8_matmul.metal:251-261; the 16 values are the format's table
+    (shaders/fp8_matmul.metal:77-80, tests/test_fp4.py:14-20)."""
+    t = fp4_values().astype(np.float64)
+    p = np.asarray(packed, np.uint8)
+    out = np.empty(p.shape[:-1] + (2 * p.shape[-1],), np.float64)
+    out[..., 0::2] = t[p & 0xF]
+    out[..., 1::2] = t[p >> 4]
+    return out
+
+
+def _operand_f64(codes: np.ndarray, fmt: int) -> np.ndarray:
+    return fp4_unpack_f64(codes) if fmt == FP4 else fp8_table_f64(fmt)[codes]
+
+
 def scaled_mm_ref(a_codes: np.ndarray, b_codes_nk: np.ndarray, scale_a, scale_b,
                   fmt_a: int = E4M3, fmt_b: int = E4M3, bias=None,
                   rows=None) -> tuple[np.ndarray, np.ndarray]:
     """Reference for C = (A*sa) @ (B*sb)^T (+ bias) in float64.
 
-    a_codes (M,K) and b_codes_nk (N,K) are fp8 bytes; scale_a is a scalar or
+    a_codes (M,K) and b_codes_nk (N,K) are fp8 bytes (fmt E4M3 / E5M2), or
+    packed FP4 bytes (M,K/2) / (N,K/2) with fmt FP4; scale_a is a scalar or
     M values, scale_b a scalar or N values. ``rows`` optionally restricts the
     result to a subset of output rows. Returns (C, S) where
     S = |A*sa| @ |B*sb|^T bounds the accumulation error.
     """
-    ta, tb = fp8_table_f64(fmt_a), fp8_table_f64(fmt_b)
     a = a_codes if rows is None else a_codes[rows]
-    A = ta[a]
-    B = tb[b_codes_nk]
+    A = _operand_f64(a, fmt_a)
+    B = _operand_f64(b_codes_nk, fmt_b)
     sa = np.asarray(scale_a, np.float64).reshape(-1)
     if sa.size > 1:
         sa = sa.reshape(-1, 1)

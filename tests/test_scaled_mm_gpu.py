@@ -204,7 +204,7 @@ def test_per_tensor_workload(nat, size):
     from fp4_fp8_for_torch_mps.workloads import scaled_mm_operands
     aq, bq, sa, sb = scaled_mm_operands(size, size, size)
     out = torch._scaled_mm(aq.cuda(), bq.cuda().t(), sa.cuda(), sb.cuda(), out_dtype=torch.bfloat16)
-    rows = np.sort(np.random.default_rng(size).choice(size, 128, replace=False))
+    rows = np.sort(np.random.default_rng(size).choice(size, 256, replace=False))
     ref, S = O.scaled_mm_ref(codes(aq), codes(bq), sa.item(), sb.item(), rows=rows)
     check_close(out[torch.from_numpy(rows).cuda()], ref, S, f"{size}^3 per-tensor")
 
@@ -215,7 +215,7 @@ def test_rowwise_workload(nat, shape):
     M, N, K = shape
     aq, wq, sa, sw = rowwise_operands(M, N, K)
     out = torch._scaled_mm(aq.cuda(), wq.cuda().t(), sa.cuda(), sw.cuda(), out_dtype=torch.bfloat16)
-    rows = np.sort(np.random.default_rng(N).choice(M, 96, replace=False))
+    rows = np.sort(np.random.default_rng(N).choice(M, 256, replace=False))
     ref, S = O.scaled_mm_ref(codes(aq), codes(wq), sa.numpy().reshape(-1), sw.numpy().reshape(-1), rows=rows)
     check_close(out[torch.from_numpy(rows).cuda()], ref, S, f"rowwise {shape}")
 
@@ -281,6 +281,66 @@ def test_bounded_wait_times_out_and_context_survives(nat, path):
     assert L.gemm_status() == 0
     ref, S = O.scaled_mm_ref(codes(a), codes(b), 0.01, 0.01)
     check_close(out, ref, S, "after timeout")
+
+
+def test_timeout_does_not_leak_into_later_launches(nat, path):
+    """A launch that timed out leaves its record in the status word, but the
+    next launches, run without a reset, are complete and correct: the word is
+    scoped to the launch that wrote it. The record stays readable until a
+    reset."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    lib = L.lib()
+    g = torch.Generator().manual_seed(2)
+    a = rand_fp8((300, 512), E4, g).cuda()
+    b = rand_fp8((272, 512), E4, g).cuda()
+    s = torch.tensor(0.02)
+    L.gemm_status(reset=True)
+    try:
+        lib.fp8b200_debug_gemm(1, 50_000_000)
+        nat.scaled_mm(a, b, s, s, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+    finally:
+        lib.fp8b200_debug_gemm(0, 0)
+    ref, S = O.scaled_mm_ref(codes(a), codes(b), 0.02, 0.02)
+    for _ in range(3):
+        out = nat.scaled_mm(a, b, s, s, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        check_close(out, ref, S, "launch after an unread timeout")
+    status = L.gemm_status(reset=True)
+    assert status & 0x80000000, hex(status)
+    assert L.gemm_status() == 0
+
+
+def test_debug_hooks_are_per_thread(nat):
+    """A test hook set on one host thread (a forced kernel path, a skipped
+    load) does not reach launches from another thread."""
+    import threading
+    from fp4_fp8_for_torch_mps import _lib as L
+    lib = L.lib()
+    g = torch.Generator().manual_seed(4)
+    a = rand_fp8((256, 256), E4, g).cuda()
+    b = rand_fp8((256, 256), E4, g).cuda()
+    s = torch.tensor(0.01)
+    ref, S = O.scaled_mm_ref(codes(a), codes(b), 0.01, 0.01)
+    L.gemm_status(reset=True)
+    lib.fp8b200_debug_gemm(1, 50_000_000)
+    lib.fp8b200_gemm_set_path(3)
+    result = {}
+
+    def other():
+        torch.cuda.set_device(0)
+        out = nat.scaled_mm(a, b, s, s, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        result["out"] = out
+    try:
+        t = threading.Thread(target=other)
+        t.start()
+        t.join()
+    finally:
+        lib.fp8b200_debug_gemm(0, 0)
+        lib.fp8b200_gemm_set_path(0)
+    assert L.gemm_status() == 0
+    check_close(result["out"], ref, S, "other thread")
 
 
 def test_single_cta_kernel_at_8192(nat):

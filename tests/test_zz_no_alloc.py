@@ -88,3 +88,57 @@ def test_rejects_inputs_beyond_its_scratch(L):
                                           torch.cuda.current_stream().cuda_stream)
     assert rc == -1
     assert b"exceed the limit" in lib.fp8b200_last_error()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_unaligned_view(L, dtype):
+    """A view one element into its storage (not 16-byte aligned) takes the
+    element-by-element amax and encode paths; results still match."""
+    g = torch.Generator().manual_seed(3)
+    base = (torch.randn(5 * 65536 + 77, generator=g) * 50).to(dtype).cuda()
+    x = base[1:]
+    assert x.data_ptr() % 16 != 0
+    rc, rs = _allocating(L, x, 3)
+    gc, gs = _noalloc(L, x, 3)
+    torch.cuda.synchronize()
+    assert torch.equal(gs.cpu(), rs.cpu()) and torch.equal(gc.cpu(), rc.cpu())
+
+
+def test_graph_capture_and_replay(L):
+    """After a first (warm) call on the device, the entry point can be captured
+    in a CUDA graph; each replay equals an eager call on the current input."""
+    g = torch.Generator().manual_seed(9)
+    x = (torch.randn(200_000, generator=g) * 10).cuda()
+    _noalloc(L, x, 3)  # first call on the device before any capture
+    torch.cuda.synchronize()
+    out = torch.empty(x.numel(), dtype=torch.uint8, device="cuda")
+    scales = torch.empty(2, dtype=torch.float32, device="cuda")
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            L.check(L.lib().fp8b200_quantize_fp8_noalloc(x.data_ptr(), 0, out.data_ptr(), 3, x.numel(),
+                                                         scales.data_ptr(), side.cuda_stream), "capture")
+    for scale in (1.0, 0.01):
+        x.mul_(scale)
+        graph.replay()
+        torch.cuda.synchronize()
+        rc, rs = _allocating(L, x, 3)
+        torch.cuda.synchronize()
+        assert torch.equal(scales.cpu(), rs.cpu()) and torch.equal(out.cpu(), rc.cpu())
+
+
+def test_at_the_size_limit(L):
+    """Exactly FP8B200_NOALLOC_MAX_ELEMENTS bf16 elements (512 MiB, all 4096
+    scratch slices), the largest amax in the last slice."""
+    limit = 4096 * 65536
+    x = torch.empty(limit, dtype=torch.bfloat16, device="cuda")
+    x.normal_(generator=torch.Generator(device="cuda").manual_seed(1))
+    x[-5] = 1000.0
+    rc, rs = _allocating(L, x, 3)
+    gc, gs = _noalloc(L, x, 3)
+    torch.cuda.synchronize()
+    assert torch.equal(gs.cpu(), rs.cpu())
+    assert torch.equal(gc, rc)
+    del x, rc, gc
+    torch.cuda.empty_cache()
