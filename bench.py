@@ -354,6 +354,7 @@ class Fp4Decode:
         return {"metric": "fp4_decode_GBps", "unit": "GB/s", "dtype": "u8->bf16", "splits": True, "bound": "hbm",
                 "config": {"workload": "fp4_decode", "shape": [rows, cols], "out": f"bf16[{rows},{2 * cols}]",
                            "scale": FP4_DECODE_SCALE, "l2": l2_note(sets, step),
+                           "launch": "K steps (one decode kernel each) replayed as one CUDA graph",
                            "parallelism": ctx.parallelism()}}
 
     def __init__(self, ctx, args):
@@ -385,14 +386,39 @@ class Fp4Decode:
         self.d_in = [torch.empty(crow, cols, dtype=torch.uint8, device="cuda") for _ in self.streams]
         self.d_out = [torch.empty(crow, 2 * cols, dtype=torch.bfloat16, device="cuda") for _ in self.streams]
 
+    graph = None
+    graph_launches = 0  # kernels in the captured graph
+
+    def _launch(self, k, st):
+        x, out = self.xs[k], self.outs[k]
+        rc = self.lib.fp8b200_decode_fp4(x.data_ptr(), x.numel(), out.data_ptr(), self.L.BF16,
+                                         self.scale.data_ptr(), self.L.SCALE_F32, st)
+        if rc:
+            self.L.check(rc, "fp4 decode")
+
+    def capture(self, steps):
+        """The K timed steps (one decode launch each, cycling through the
+        buffer sets) as one CUDA graph, replayed once per timed region, so
+        that consecutive launches overlap through programmatic dependent
+        launch with no host launch gap (a row block on 8 GPUs is a ~13 us
+        launch)."""
+        side = torch.cuda.Stream()
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = self.L.launch_count()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(self.graph, stream=side):
+                for j in range(steps):
+                    self._launch((self.i + j) % self.sets, side.cuda_stream)
+        self.graph_launches = self.L.launch_count() - n0
+        torch.cuda.synchronize()
+
+    def replay(self):
+        self.graph.replay()
+
     def step(self):
         k = self.i % self.sets
         self.i += 1
-        x, out = self.xs[k], self.outs[k]
-        rc = self.lib.fp8b200_decode_fp4(x.data_ptr(), x.numel(), out.data_ptr(), self.L.BF16,
-                                         self.scale.data_ptr(), self.L.SCALE_F32, self.stream.cuda_stream)
-        if rc:
-            self.L.check(rc, "fp4 decode")
+        self._launch(k, self.stream.cuda_stream)
 
     def e2e_step(self):
         def body(i, lo, hi, j):
@@ -812,10 +838,16 @@ def gemm_check(w, rows):
     got = w.h_out[torch.from_numpy(rows)].float().double().numpy()
     u = O.bf16_ulp(ref)
     err = np.abs(got - ref)
-    ok = bool(np.all(err <= u + (0.0 if w.fp4 else 2.0 ** -20) * S))
+    acc = (0.0 if w.fp4 else 2.0 ** -20) * S
+    ok = bool(np.all(err <= u + acc))
+    # outputs whose float32 accumulation bound is below half an output ulp (no cancellation)
+    well = acc <= 0.5 * u
     return ok, {"rows_checked": int(len(rows)), "cols_checked": int(ref.shape[1]),
                 "max_err_bf16_ulp": round(float((err / u).max()), 4),
-                "frac_over_1_ulp": float((err > u).mean())}
+                "max_err_bf16_ulp_well_conditioned": round(float((err / u)[well].max()), 4) if well.any() else None,
+                "frac_well_conditioned": round(float(well.mean()), 6),
+                "frac_over_1_ulp": float((err > u).mean()),
+                "reference": "float64 dequantised product"}
 
 
 class ScaledMM:
@@ -1391,11 +1423,20 @@ def gpu_line(args, ctx):
         achieved, gemm_ms, n_gemm = w.gemm_roofline()
         extra = {"gemm_ms_per_step": round(gemm_ms, 3), "gemm_launches_per_step": n_gemm,
                  "gemm_share": round(gemm_ms / ms_step, 4)}
-    # GEMMs timed inside a long step (seconds under the power cap) against the
-    # sustained GEMM peak, GEMMs timed on their own against the burst peak
-    bf16_key = "bf16_tflops_sustained" if getattr(w, "sustained", False) and "bf16_tflops_sustained" in pk \
-        else "bf16_tflops"
+    # Tensor-core lines: the timed repeats run the GEMM back to back for at
+    # least MIN_REGION_MS, long enough for the 1000 W power cap to lower the
+    # clocks, so they are held against the sustained GEMM peak (measured the
+    # same way, back to back); the fastest repeat (burst clocks) is reported
+    # beside it against the burst peak.
     bound = desc["bound"]
+    long_run = bound in ("tensor", "tensor_bf16") and sum(regions) >= 100.0
+    bf16_key = "bf16_tflops_sustained" if (getattr(w, "sustained", False) or long_run) \
+        and "bf16_tflops_sustained" in pk else "bf16_tflops"
+    if long_run and not extra:
+        burst = total_work / ctx.ws / (min(regions) / args.steps * 1e-3) / scale
+        burst_peak = (2.0 if bound == "tensor" else 1.0) * pk["bf16_tflops"]
+        extra = {"burst": {"achieved": round(burst, 2), "peak": burst_peak, "frac": round(burst / burst_peak, 4),
+                           "from": "fastest timed repeat, against the burst peak"}}
     if bound == "hbm":
         peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
     elif bound == "tensor_bf16":

@@ -1843,27 +1843,37 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 // feeds them straight to the warp-level tensor-core instruction
 // mma.sync.m16n8k16 computing D^T = W x^T: 16 weight rows as the A operand,
 // 8 x rows as B (NT = 1 or 2 tiles, zero rows past M), float32 accumulators.
-//   CTA: 4 consumer warps, 64 output channels (16 weight rows per warp), and
-//   a producer warp whose lane 0 streams the CTA's 64 x 128-byte weight
-//   tiles with TMA into a GV_STAGES-deep ring (128-byte swizzle, full /
-//   empty mbarriers, bounded waits);
+//   CTA: 64 output channels; a producer warp whose lane 0 streams, per
+//   128-value k-block, the 64 x 128-byte weight tile and the block's x tile
+//   (8 NT rows x 128 values, two 128-byte-wide boxes; rows past M are the
+//   TMA's zero fill) into a GV_STAGES-deep ring (128-byte swizzle, full /
+//   empty mbarriers, bounded waits); 8 consumer warps, two per 16-row group
+//   of channels, taking alternate k-blocks, so one warp's conversion and
+//   MMAs overlap its partner's shared-memory loads; nothing in the k-loop
+//   reads global memory;
 //   cluster: ks CTAs splitting K, partial sums reduced through distributed
 //   shared memory (each CTA reduces and stores 64 / ks columns), so no
 //   global scratch and a fixed summation order.
-//   k-loop: 128-value blocks; lane (g, t) reads 32 weight bytes of rows g
-//   and 8 + g of the tile and 32 x values of x row g (and g + 8) with
-//   read-only loads (the x rows are shared by every warp and CTA of a
-//   column and stay in L1 / L2). Within a block the lane's
+//   k-loop: lane (g, t) reads 32 weight bytes of rows g and 8 + g of its
+//   group and 32 x values of x row g (and g + 8). Within a block the lane's
 //   32 physical k positions 32t .. 32t+31 are the logical positions {2t,
 //   2t+1, 2t+8, 2t+9} of eight consecutive m16n8k16 steps (four positions
 //   per step), the same permutation for A and B, which leaves the sum
 //   unchanged, and makes both operands' register pairs come straight from
 //   the conversions and the 16-byte loads.
-constexpr int GV_WARPS = 4;
+constexpr int GV_WARPS = 4;                        // 16-channel row groups per CTA
+constexpr int GV_CONSUMERS = 2 * GV_WARPS;         // two warps per row group, alternate k-blocks
+constexpr int GV_THREADS = 32 * (GV_CONSUMERS + 1);
 constexpr int GV_BN = 16 * GV_WARPS;  // 64 output channels per CTA
 constexpr int GV_BK = 128;
-constexpr int GV_STAGES = 6;  // weight tiles in flight per CTA (TMA ring)
+constexpr int GV_STAGES = 8;  // k-blocks in flight per CTA (TMA ring)
 constexpr int GV_TILE = GV_BN * GV_BK;  // 64 weight rows x 128 codes, 8 KiB
+// x tile of a k-block: two 128-byte-wide boxes (values 0-63, 64-127) of 8 NT rows
+__host__ __device__ constexpr int gv_x_half(int nt) { return 8 * nt * 128; }
+__host__ __device__ constexpr int gv_stage(int nt) { return GV_TILE + 2 * gv_x_half(nt); }
+__host__ __device__ constexpr int gv_smem(int nt) {
+  return 1024 + GV_STAGES * gv_stage(nt) + 2 * 16 * GV_BN * 4 /*partials*/ + 2 * GV_STAGES * 8 /*barriers*/;
+}
 
 template <int WF, bool F16>
 __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o)[16]) {
@@ -1904,15 +1914,16 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
 }
 
 template <int WF, bool F16, int NT>  // NT: 8-row tiles of x (1 for M <= 8, 2 for M <= 16)
-__global__ void __launch_bounds__(32 * (GV_WARPS + 1))
-linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t *__restrict__ x, int64_t ldx,
+__global__ void __launch_bounds__(GV_THREADS, 2)
+linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         int M, int N, int kslice, const Params p) {
   extern __shared__ uint8_t gv_raw[];
+  constexpr int XH = gv_x_half(NT), ST = gv_stage(NT);
   const uint32_t raw_addr = smem_u32(gv_raw);
-  const uint32_t ring = (raw_addr + 1023u) & ~1023u;  // GV_STAGES x 8 KiB tiles (128-byte swizzle)
+  const uint32_t ring = (raw_addr + 1023u) & ~1023u;  // GV_STAGES x [w tile | x half 0 | x half 1], 1 KiB aligned
   uint8_t *base = gv_raw + (ring - raw_addr);
-  float *part = reinterpret_cast<float *>(base + GV_STAGES * GV_TILE);  // [16][GV_BN]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(part + 16 * GV_BN);
+  float *part = reinterpret_cast<float *>(base + GV_STAGES * ST);  // [2][16][GV_BN]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(part + 2 * 16 * GV_BN);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int st) { return bar0 + 8u * st; };
   auto empty_bar = [&](int st) { return bar0 + 8u * (GV_STAGES + st); };
@@ -1920,64 +1931,55 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
   const int g = lane >> 2, t = lane & 3;
   const uint32_t rank = cluster_rank(), ks = p.sk_cs;
   const int n0 = blockIdx.y * GV_BN;
-  const int64_t k0 = (int64_t)rank * kslice;
+  const int k0 = (int)rank * kslice;
   const int nblk = kslice / GV_BK;
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < GV_STAGES; st++) {
       mbar_init(full_bar(st), 1);
-      mbar_init(empty_bar(st), GV_WARPS);
+      mbar_init(empty_bar(st), GV_WARPS);  // the four warps (one per row group) that read the stage
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
   }
   __syncthreads();
 
   float acc[NT][4] = {};
-  if (warp == GV_WARPS) {
-    // ---------------- producer: one lane streams the CTA's 64 weight rows, 128 bytes of K per tile
+  const int rg = warp & 3, par = warp >> 2;  // consumers: row group, k-block parity
+  if (warp == GV_CONSUMERS) {
+    // ---------------- producer: one lane streams the CTA's weight rows and the x rows, one k-block per stage
     if (lane == 0) {
       for (int kb = 0; kb < nblk; kb++) {
         const int st = kb % GV_STAGES;
         const uint32_t ph = (uint32_t)((kb / GV_STAGES) & 1);
         if (!mbar_wait(empty_bar(st), ph ^ 1u, p.timeout_ns, p.epoch, 20)) break;
         if (p.debug_skip_first_load) break;  // test hook: no tile ever lands, the consumers' waits run out
-        mbar_expect_tx(full_bar(st), GV_TILE);
-        tma_load_2d(ring + (uint32_t)(st * GV_TILE), &tmap_w, full_bar(st), (int)(k0 + (int64_t)kb * GV_BK), n0);
+        const uint32_t sa = ring + (uint32_t)(st * ST);
+        const int kx = k0 + kb * GV_BK;
+        mbar_expect_tx(full_bar(st), (uint32_t)ST);
+        tma_load_2d(sa, &tmap_w, full_bar(st), kx, n0);
+        tma_load_2d(sa + GV_TILE, &tmap_x, full_bar(st), kx, 0);
+        tma_load_2d(sa + GV_TILE + XH, &tmap_x, full_bar(st), kx + 64, 0);
       }
     }
   } else {
-    // ---------------- consumers: D^T = W x^T per warp; the warp's 16 weight rows (tile rows
-    // 16 warp + g, + 8) are the m16n8k16 A operand, x rows the 8-column B operand (NT tiles:
-    // rows 0-7, 8-15). Lane (g, t) reads 16-byte units 2t, 2t + 1 of its two rows; unit u of
-    // tile row r sits at u ^ (r & 7) (128-byte swizzle), so a warp's reads are conflict-free.
-    // The x rows are read from global memory (shared by every warp and CTA of a column, they
-    // stay in L1 / L2).
-    const uint4 *xr[NT];
-    bool xin[NT];
-#pragma unroll
-    for (int u = 0; u < NT; u++) {
-      xin[u] = 8 * u + g < M;
-      xr[u] = reinterpret_cast<const uint4 *>(x + (xin[u] ? (int64_t)(8 * u + g) * ldx : 0) + k0 + 32 * t);
-    }
-    const uint32_t row_off[2] = {(uint32_t)((16 * warp + g) * 128), (uint32_t)((16 * warp + 8 + g) * 128)};
+    // ---------------- consumers: D^T = W x^T; warp (rg, par) takes k-blocks par, par + 2, ... Its 16
+    // weight rows (tile rows 16 rg + g, + 8) are the m16n8k16 A operand, x rows the 8-column B
+    // operand (NT tiles: rows 0-7, 8-15). Lane (g, t) reads 16-byte units 2t, 2t + 1 of its two
+    // weight rows (unit u of tile row r at u ^ (r & 7): conflict-free), and of x row 8u + g the
+    // units 4 (t & 1) .. + 3 of box t >> 1 (same swizzle).
+    const uint32_t row_off[2] = {(uint32_t)((16 * rg + g) * 128), (uint32_t)((16 * rg + 8 + g) * 128)};
     const uint32_t unit_off[2] = {(uint32_t)(((2 * t) ^ g) * 16), (uint32_t)(((2 * t + 1) ^ g) * 16)};
+    const uint32_t x_off = (uint32_t)(GV_TILE + (t >> 1) * XH + g * 128);
 #pragma unroll 1
-    for (int kb = 0; kb < nblk; kb++) {
+    for (int kb = par; kb < nblk; kb += 2) {
       const int st = kb % GV_STAGES;
       const uint32_t ph = (uint32_t)((kb / GV_STAGES) & 1);
-      uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
-#pragma unroll
-      for (int u = 0; u < NT; u++)
-#pragma unroll
-        for (int v = 0; v < 4; v++) {
-          const uint4 q = xin[u] ? __ldg(xr[u] + kb * (GV_BK / 8) + v) : make_uint4(0, 0, 0, 0);
-          xv[u][4 * v] = q.x; xv[u][4 * v + 1] = q.y; xv[u][4 * v + 2] = q.z; xv[u][4 * v + 3] = q.w;
-        }
       const bool landed = mbar_wait(full_bar(st), ph, p.timeout_ns, p.epoch, 21);  // every lane waits (visibility)
-      if (!__all_sync(0xFFFFFFFFu, landed)) break;                         // and the warp leaves as one
+      if (!__all_sync(0xFFFFFFFFu, landed)) break;                                // and the warp leaves as one
+      const uint32_t tile = ring + (uint32_t)(st * ST);
       uint4 raw[2][2];
-      const uint32_t tile = ring + (uint32_t)(st * GV_TILE);
 #pragma unroll
       for (int h = 0; h < 2; h++)
 #pragma unroll
@@ -1988,11 +1990,20 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
       uint32_t wv[2][16];  // weight rows g and g + 8 converted: the A operand pairs
       gv_convert32<WF, F16>(raw[0], wv[0]);
       gv_convert32<WF, F16>(raw[1], wv[1]);
-      // the tile's bytes are now in registers (the conversions consumed them): only then may the
-      // producer's next TMA overwrite the stage; order these reads before that async-proxy write
+      uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
+#pragma unroll
+      for (int u = 0; u < NT; u++)
+#pragma unroll
+        for (int v = 0; v < 4; v++)
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(xv[u][4 * v]), "=r"(xv[u][4 * v + 1]), "=r"(xv[u][4 * v + 2]), "=r"(xv[u][4 * v + 3])
+                       : "r"(tile + x_off + (uint32_t)(u * 1024) + (uint32_t)(((4 * (t & 1) + v) ^ g) * 16)));
+      // the stage's bytes are now in registers (the conversions consumed the weights, the MMAs below
+      // read only registers): only then may the producer's next TMA overwrite it; order these reads
+      // before that async-proxy write
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(st));  // this warp is done with the tile
+      if (lane == 0) mbar_arrive(empty_bar(st));  // this warp is done with the stage
 #pragma unroll
       for (int j = 0; j < 8; j++)
 #pragma unroll
@@ -2002,18 +2013,22 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16
     }
   }
 
-  if (warp < GV_WARPS) {
-    // partial sums part[x row][channel] (rows < 8 NT, all written): acc[u] = D^T rows (channels)
-    // g / g + 8, columns (x rows) 8u + 2t (+1)
+  if (warp < GV_CONSUMERS) {
+    // partial sums part[par][x row][channel] (rows < 8 NT, all written): acc[u] = D^T rows
+    // (channels) g / g + 8, columns (x rows) 8u + 2t (+1)
+    float *pp = part + par * 16 * GV_BN;
 #pragma unroll
     for (int u = 0; u < NT; u++) {
-      const int ch = 16 * warp + g, xrow = 8 * u + 2 * t;
-      part[xrow * GV_BN + ch] = acc[u][0];
-      part[(xrow + 1) * GV_BN + ch] = acc[u][1];
-      part[xrow * GV_BN + ch + 8] = acc[u][2];
-      part[(xrow + 1) * GV_BN + ch + 8] = acc[u][3];
+      const int ch = 16 * rg + g, xrow = 8 * u + 2 * t;
+      pp[xrow * GV_BN + ch] = acc[u][0];
+      pp[(xrow + 1) * GV_BN + ch] = acc[u][1];
+      pp[xrow * GV_BN + ch + 8] = acc[u][2];
+      pp[(xrow + 1) * GV_BN + ch + 8] = acc[u][3];
     }
   }
+  __syncthreads();
+  // the two parities' sums, in a fixed order, into part[0]
+  for (int i = threadIdx.x; i < 8 * NT * GV_BN; i += blockDim.x) part[i] += part[16 * GV_BN + i];
   __syncwarp();
   cluster_sync();  // every CTA's partial sums are complete
   // this CTA reduces and stores columns [rank * cw, (rank + 1) * cw) of the 64
@@ -2376,18 +2391,24 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
   }
-  if (M <= 16 && K % GV_BK == 0 && g_path != 3) {
-    // very few rows: weights streamed by TMA and converted in registers for warp-level MMAs, K
-    // split over a cluster of ks CTAs (enough CTAs to cover the GPU a few times over, each K
-    // slice a multiple of the 128-value block)
+  if (M <= 16 && K % GV_BK == 0 && K <= 0x7FFFFFFFLL - GV_BK && g_path != 3) {
+    // very few rows: weights and x streamed by TMA, weights converted in registers for warp-level
+    // MMAs, K split over a cluster of ks CTAs: the smallest split whose CTAs cover every SM once
+    // (two CTAs fit on an SM, so the grid stays within about two waves), each K slice a multiple
+    // of the 128-value block
     const int64_t nb = (N + GV_BN - 1) / GV_BN;
     int ks = 1;
-    while (ks < 8 && K % (GV_BK * 2 * ks) == 0 && nb * ks < 4LL * current_sm_count()) ks *= 2;
+    while (ks < 8 && K % (GV_BK * 2 * ks) == 0 && nb * ks < (int64_t)current_sm_count()) ks *= 2;
     const int64_t kslice = K / ks;
-    const int64_t smem = 1024 + GV_STAGES * GV_TILE + 16 * GV_BN * 4 + 2 * GV_STAGES * 8;
+    const int nt = M > 8 ? 2 : 1;
+    const int64_t smem = gv_smem(nt);
     if (nb <= 65535) {
-      CUtensorMap mw;
+      CUtensorMap mw, mx;
       if (int rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, GV_BK, GV_BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+      // x: M rows of K 16-bit values; boxes of 64 values x 8 NT rows (rows past M read as zeros)
+      if (int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, M, ldx * 2, 64, (uint32_t)(8 * nt),
                                CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
       Params p;
@@ -2398,10 +2419,10 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
       p.sk_cs = ks;
       p.timeout_ns = g_timeout_ns;
-  p.epoch = next_epoch();
+      p.epoch = next_epoch();
       p.debug_skip_first_load = g_debug_skip_first_load;
       const bool f16 = x_dtype == FP8B200_F16;
-      using GvKernel = void (*)(const CUtensorMap, const uint16_t *, int64_t, int, int, int, const Params);
+      using GvKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, const Params);
       static const GvKernel kernels[8] = {
           linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 1>, linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 2>,
           linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 1>,  linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 2>,
@@ -2426,12 +2447,12 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
       cfg.gridDim = dim3((unsigned)ks, (unsigned)nb, 1);
-      cfg.blockDim = dim3(32 * (GV_WARPS + 1), 1, 1);
+      cfg.blockDim = dim3(GV_THREADS, 1, 1);
       cfg.dynamicSmemBytes = (size_t)smem;
       cfg.stream = (cudaStream_t)stream;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaLaunchKernelEx(&cfg, kern, mw, (const uint16_t *)x, (int64_t)ldx, (int)M, (int)N, (int)kslice, p);
+      cudaLaunchKernelEx(&cfg, kern, mw, mx, (int)M, (int)N, (int)kslice, p);
       count_launch();
       return check_launch("linear_fp8w");
     }
@@ -2470,7 +2491,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     const uint32_t fmt = p.act_f16 ? 0u : 1u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(mt >> 3) << 17) | ((uint32_t)(SK_BN >> 4) << 24);
     p.timeout_ns = g_timeout_ns;
-  p.epoch = next_epoch();
+    p.epoch = next_epoch();
     p.debug_skip_first_load = g_debug_skip_first_load;
     p.sk_mt = mt;
     const int stage_bytes = SK_B_BYTES + mt * BK + SK_B_BYTES / 2;

@@ -52,6 +52,7 @@ def _declare(L):
         "fp8b200_decode_fp8": [vp, i32, vp, i32, i64, vp, i32, vp],
         "fp8b200_decode_fp4": [vp, i64, vp, i32, vp, i32, vp],
         "fp8b200_quantize_fp8": [vp, i32, vp, i32, i64, vp, vp, vp],
+        "fp8b200_quantize_fp8_noalloc": [vp, i32, vp, i32, i64, vp, vp],
         "fp8b200_encode_fp4": [vp, i32, vp, i64, vp, vp],
         "fp8b200_quantize_rows_fp8": [vp, i32, i64, i64, i64, vp, i64, i32, vp, vp],
         "fp8b200_silu_mul_quantize_rows_fp8": [vp, i64, i64, i64, vp, i64, i32, vp, vp],

@@ -8,6 +8,13 @@ optional replicated-output mode gathers the row blocks to every rank with one
 all-gather (NCCL over NVLink/NVSwitch on GPUs, gloo on CPU), for callers that
 need the full result everywhere.
 
+Failure detection between steps: a rank that leaves the job between two
+steps announces it in the process group's key-value store (`announce_leave`,
+before the barrier that closes its last step), and every other rank checks
+the store before it launches its next step (`check_peers`), so the survivors
+stop on the host with `PeerLeft` instead of entering a collective that can
+never complete.
+
 The reference is single-device and has no counterpart of this module.
 """
 from __future__ import annotations
@@ -93,3 +100,28 @@ def sharded_scaled_mm(a: torch.Tensor, mat2: torch.Tensor, scale_a: torch.Tensor
     sa = scale_a[s:e] if scale_a.numel() > 1 else scale_a
     local = torch._scaled_mm(a[s:e], mat2, sa, scale_b, **kwargs)
     return gather_rows(local, M, group) if gather else local
+
+
+class PeerLeft(RuntimeError):
+    """A rank of the job announced that it left between steps."""
+
+
+def _leave_key(rank: int) -> str:
+    return f"fp8b200/left/{rank}"
+
+
+def announce_leave(store, rank: int) -> None:
+    """Record in the job's store that `rank` leaves. Call it in the rank's
+    last step before the collective that closes the step (a barrier), so that
+    every other rank finds the record when it next calls check_peers; then
+    leave with no kernel or collective in flight."""
+    store.set(_leave_key(rank), "1")
+
+
+def check_peers(store, world_size: int, rank: int) -> None:
+    """Raise PeerLeft if any other rank announced that it left. A non-blocking
+    store lookup per rank; call it before launching a step's kernels and
+    collectives."""
+    gone = [r for r in range(world_size) if r != rank and store.check([_leave_key(r)])]
+    if gone:
+        raise PeerLeft(f"rank(s) {gone} left the job; rank {rank} stops before its next step")

@@ -27,6 +27,23 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
+def test_binding_declares_every_entry_point_with_arguments():
+    """Every C entry point that takes arguments has ctypes argtypes in the
+    package's binding: an undeclared one would pass 64-bit pointers and
+    streams as truncated C ints."""
+    from fp4_fp8_for_torch_mps import _lib
+    L = _lib.lib()
+    txt = open(HDR).read()
+    decls = re.findall(r"^(?:int|const char \*|uint64_t)\s*(fp8b200_[a-z0-9_]+)\s*\(([^)]*)\);", txt, re.M)
+    assert len(decls) >= 11
+    for name, args in decls:
+        if args.strip() in ("", "void"):
+            continue
+        fn = getattr(L, name)
+        assert fn.argtypes is not None, name
+        assert len(fn.argtypes) == len(args.split(",")), name
+
+
 def test_library_argument_validation():
     from fp4_fp8_for_torch_mps import _lib as L
     lib = L.lib()

@@ -10,7 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from fp4_fp8_for_torch_mps.parallel import gather_rows, shard_rows, sharded_rows_apply, sharded_scaled_mm
+from fp4_fp8_for_torch_mps.parallel import (PeerLeft, announce_leave, check_peers, gather_rows, shard_rows,
+                                            sharded_rows_apply, sharded_scaled_mm)
 
 
 @pytest.mark.parametrize("total,ws", [(0, 2), (1, 4), (7, 2), (16, 4), (1000, 8), (16384, 8)])
@@ -118,3 +119,62 @@ def test_gloo_rank_failure_surfaces_as_error(ws):
     assert res[1][:2] == (1, "error") and "injected" in res[1][2], res
     for r in res:
         assert r[1] == "error", res  # no rank completes a gather that lost a member
+
+
+def _leaving_worker(rank, ws, port, q):
+    """Two steps of a sharded conversion + gather on every rank; then rank 1
+    leaves between steps (announcing it in the store). The other ranks must
+    detect that on the host before their third step and stop with PeerLeft,
+    without entering a collective."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    store = dist.TCPStore("127.0.0.1", port + 1, ws, rank == 0, timeout=datetime.timedelta(seconds=30))
+    dist.init_process_group("gloo", rank=rank, world_size=ws, store=dist.PrefixStore("pg", store),
+                            timeout=datetime.timedelta(seconds=10))
+    x = torch.randn(8 * ws, 16)
+    steps = 0
+    try:
+        for step in range(4):
+            check_peers(store, ws, rank)
+            sharded_rows_apply(x, lambda t: t.to(torch.float8_e4m3fn), gather=True)
+            steps += 1
+            leaving = rank == 1 and step == 1
+            if leaving:
+                announce_leave(store, rank)  # before the barrier that closes its last step
+            dist.barrier()  # the step is complete on every rank before the next check
+            if leaving:
+                q.put((rank, "left", steps))
+                break
+        else:
+            q.put((rank, "completed", steps))
+    except PeerLeft as e:
+        q.put((rank, "peer_left", steps, str(e)))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("ws", [2, 3])
+def test_gloo_rank_leaving_between_steps_is_detected(ws):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, ws, port, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(ws))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == (1, "left", 2), res
+    for r in res:
+        if r[0] != 1:
+            assert r[1] == "peer_left" and r[2] == 2 and "[1]" in r[3], res
+
+
+def test_check_peers_single_store():
+    store = dist.HashStore()
+    check_peers(store, 3, 0)
+    announce_leave(store, 2)
+    with pytest.raises(PeerLeft):
+        check_peers(store, 3, 0)
+    check_peers(store, 3, 2)  # a rank does not report itself
