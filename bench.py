@@ -806,6 +806,33 @@ class Quantize:
             f"{x.shape[0]}x{x.shape[1]} {kind} per pass (oracle, C, 1 thread)", dt
 
 
+class GraphSteps:
+    """Launch-bound workloads (decode-sized GEMMs and linears, a few to 40 us
+    per call): the K timed steps are captured once as a CUDA graph (each step
+    one C-ABI call, rotating through the weight sets) and replayed per timed
+    region; `e2e` keeps the host-launched public API."""
+    graph = None
+    graph_launches = 0
+
+    def capture(self, steps):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = self.L.launch_count()
+        saved = self.stream
+        with torch.cuda.stream(side):
+            self.stream = side
+            with torch.cuda.graph(self.graph, stream=side):
+                for _ in range(steps):
+                    self.step()
+        self.stream = saved
+        self.graph_launches = self.L.launch_count() - n0
+        torch.cuda.synchronize()
+
+    def replay(self):
+        self.graph.replay()
+
+
 def _quantize_factory(kind):
     class _K(Quantize):
         name = kind
@@ -987,7 +1014,7 @@ def _gemm_factory(rowwise, fp4):
     return _G
 
 
-class ScaledMMSmallM:
+class ScaledMMSmallM(GraphSteps):
     """Decode-sized rowwise GEMM: M (--m, default 16) activation rows against
     Llama-shaped e4m3 weights (N, K from --shape). The weights dominate the
     bytes, so the bound is HBM: work = N*K + M*K bytes read + 2*M*N written.
@@ -1006,6 +1033,7 @@ class ScaledMMSmallM:
                 "splits": False, "bound": "hbm",
                 "config": {"workload": "scaled_mm_small_m", "M": M, "N": N, "K": K, "scales": "rowwise",
                            "out": "bf16", "l2": f"{nsets} rotating weight sets, {nsets * N * K / 2**20:.0f} MiB > L2",
+                           "launch": "K steps replayed as one CUDA graph",
                            "parallelism": ctx.parallelism(False)}}
 
     def __init__(self, ctx, args):
@@ -1081,7 +1109,7 @@ class ScaledMMSmallM:
             f"{M}x{N}x{K} f32 dequantised matmul (CPU torch, {threads} threads; weights pre-dequantised)", dt
 
 
-class LinearFp8W:
+class LinearFp8W(GraphSteps):
     """FP8-weight linear with dequant-on-load: y = x @ (w * s)^T, x bf16
     (M, K) N(0,1), w e4m3 quantised per output channel from N(0, 0.02),
     Llama shapes (N, K from --shape, M from --m, default 16384). Compute in
@@ -1111,6 +1139,7 @@ class LinearFp8W:
                            "activations": "bf16", "out": "bf16",
                            "l2": ("x+w+y {:.0f} MiB > L2".format(foot / 2**20) if nsets == 1 else
                                   f"{nsets} rotating weight sets, {nsets * N * K / 2**20:.0f} MiB > L2"),
+                           "launch": "K steps replayed as one CUDA graph" if small else "host-launched",
                            "parallelism": ctx.parallelism(False)}}
 
     def __init__(self, ctx, args):
@@ -1139,6 +1168,19 @@ class LinearFp8W:
         self.h_x = self.x_host.pin_memory()
         self.h_out = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
         self.d_x = torch.empty_like(self.x)
+
+    def capture(self, steps):
+        if self.M <= 256:
+            GraphSteps.capture(self, steps)
+        else:
+            self.steps = steps
+
+    def replay(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            for _ in range(self.steps):
+                self.step()
 
     def step(self):
         L = self.L

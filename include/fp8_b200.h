@@ -149,10 +149,10 @@ int fp8b200_rope_bf16(const void *qkv, int64_t tokens, int64_t ld, int n_q_heads
  * Allocation-free fp8b200_quantize_fp8 (no counterpart in the reference; the
  * reference has no device memory management of its own). Same inputs,
  * outputs and results, but no amax_scratch argument: the scratch is a fixed
- * 16 KiB array inside this library's device memory (one amax partial per
- * 65536 elements), so a caller that cannot allocate device memory, such as a
- * host runtime that only passes in the tensors to read and write, needs
- * nothing beyond src, dst and scale_out.
+ * 16 KiB array inside this library's device memory (4096 amax partials,
+ * one per slice of 4096 to 65536 elements), so a caller that cannot
+ * allocate device memory, such as a host runtime that only passes in the
+ * tensors to read and write, needs nothing beyond src, dst and scale_out.
  * Limits: n <= FP8B200_NOALLOC_MAX_ELEMENTS, else FP8B200_EINVAL. The first
  * call on each device looks up the array's device address (make that first
  * call before any stream capture). Every call shares the array: calls that

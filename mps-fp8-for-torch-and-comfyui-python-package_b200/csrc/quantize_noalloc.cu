@@ -8,8 +8,11 @@
 // that path. For them, fp8b200_quantize_fp8_noalloc keeps its scratch in a
 // fixed array in this library's own device memory instead.
 //
-// Scratch layout: one max-|x| partial per slice of kSliceElems input
-// elements, kSlices slots (16 KiB). Every slot a call reads was written
+// Scratch layout: one max-|x| partial per slice of input elements, kSlices
+// slots (16 KiB). A call's slice length is the smallest multiple of
+// kSliceUnit that needs at most kSlices slices (4096 elements up to 2^24
+// elements, growing to kMaxSliceElems at the limit), so small inputs still
+// spread over many blocks. Every slot a call reads was written
 // earlier in the same call, so nothing has to be cleared between calls; the
 // array keeps the last call's partials. Two calls that run at the same time
 // on the GPU (different streams, or different host threads) share the array
@@ -18,13 +21,16 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 
 namespace fp8b200 {
 namespace noalloc {
 
-constexpr int64_t kSliceElems = 65536;
+constexpr int64_t kSliceUnit = 4096;       // slice lengths are multiples of this (16-byte aligned slices)
+constexpr int64_t kMaxSliceElems = 65536;
 constexpr int kSlices = 4096;
-constexpr int64_t kMaxElems = kSliceElems * kSlices;  // 2^28 elements
+constexpr int64_t kMaxElems = kMaxSliceElems * kSlices;  // 2^28 elements
 constexpr int kThreads = 256;
 
 // The scratch. In host code this name is only a stand-in for the symbol: the
@@ -71,13 +77,13 @@ __device__ __forceinline__ uint32_t to_float_bits(uint32_t m16_or_f32) {
 // One block per slice: partials[b] = max |x| over slice b, as float bits
 // (NaN sorts above inf, so a NaN anywhere wins, as in the allocating path).
 // VEC: 16-byte loads, four in flight per thread (the slice starts on a
-// 16-byte boundary when src does: 65536 elements of 2 or 4 bytes), scalar
+// 16-byte boundary when src does: a multiple of 4096 elements), scalar
 // loads for the last partial unit; otherwise element by element.
 template <int SRC, bool VEC>
 __global__ void __launch_bounds__(kThreads)
-slice_amax_kernel(const void *__restrict__ src, int64_t n, uint32_t *__restrict__ partials) {
-  const int64_t begin = (int64_t)blockIdx.x * kSliceElems;
-  const int64_t end = min(n, begin + kSliceElems);
+slice_amax_kernel(const void *__restrict__ src, int64_t n, int64_t slice, uint32_t *__restrict__ partials) {
+  const int64_t begin = (int64_t)blockIdx.x * slice;
+  const int64_t end = min(n, begin + slice);
   uint32_t m = 0;  // magnitude bits in the source format
   if constexpr (VEC) {
     constexpr int per = SRC == FP8B200_F32 ? 4 : 8;  // elements per 16-byte unit
@@ -163,7 +169,7 @@ extern "C" int fp8b200_quantize_fp8_noalloc(const void *src, int src_dtype, void
     return set_error(FP8B200_EINVAL,
                      "quantize_noalloc: %lld elements exceed the limit of %lld (its fixed scratch holds %d "
                      "partials of %lld elements); use fp8b200_quantize_fp8 with caller-provided scratch",
-                     (long long)n, (long long)kMaxElems, kSlices, (long long)kSliceElems);
+                     (long long)n, (long long)kMaxElems, kSlices, (long long)kMaxSliceElems);
   if (src_dtype != FP8B200_F32 && src_dtype != FP8B200_BF16 && src_dtype != FP8B200_F16)
     return set_error(FP8B200_EINVAL, "quantize_noalloc: source dtype %d is not f32/bf16/f16", src_dtype);
   if (fp8_dtype != FP8B200_E4M3 && fp8_dtype != FP8B200_E5M2)
@@ -175,18 +181,20 @@ extern "C" int fp8b200_quantize_fp8_noalloc(const void *src, int src_dtype, void
   uint32_t *partials;
   if (int rc = scratch_ptr(&partials)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const int nslices = (int)((n + kSliceElems - 1) / kSliceElems);
+  const int64_t per = (n + kSlices - 1) / kSlices;
+  const int64_t slice = std::max<int64_t>(kSliceUnit, (per + kSliceUnit - 1) / kSliceUnit * kSliceUnit);
+  const int nslices = (int)((n + slice - 1) / slice);
   if (nslices > 0) {
     const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
     if (src_dtype == FP8B200_F32) {
-      if (vec) slice_amax_kernel<FP8B200_F32, true><<<nslices, kThreads, 0, st>>>(src, n, partials);
-      else slice_amax_kernel<FP8B200_F32, false><<<nslices, kThreads, 0, st>>>(src, n, partials);
+      if (vec) slice_amax_kernel<FP8B200_F32, true><<<nslices, kThreads, 0, st>>>(src, n, slice, partials);
+      else slice_amax_kernel<FP8B200_F32, false><<<nslices, kThreads, 0, st>>>(src, n, slice, partials);
     } else if (src_dtype == FP8B200_BF16) {
-      if (vec) slice_amax_kernel<FP8B200_BF16, true><<<nslices, kThreads, 0, st>>>(src, n, partials);
-      else slice_amax_kernel<FP8B200_BF16, false><<<nslices, kThreads, 0, st>>>(src, n, partials);
+      if (vec) slice_amax_kernel<FP8B200_BF16, true><<<nslices, kThreads, 0, st>>>(src, n, slice, partials);
+      else slice_amax_kernel<FP8B200_BF16, false><<<nslices, kThreads, 0, st>>>(src, n, slice, partials);
     } else {
-      if (vec) slice_amax_kernel<FP8B200_F16, true><<<nslices, kThreads, 0, st>>>(src, n, partials);
-      else slice_amax_kernel<FP8B200_F16, false><<<nslices, kThreads, 0, st>>>(src, n, partials);
+      if (vec) slice_amax_kernel<FP8B200_F16, true><<<nslices, kThreads, 0, st>>>(src, n, slice, partials);
+      else slice_amax_kernel<FP8B200_F16, false><<<nslices, kThreads, 0, st>>>(src, n, slice, partials);
     }
     count_launch();
     if (int rc = check_launch("quantize_noalloc amax")) return rc;

@@ -1853,7 +1853,8 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 //   reads global memory;
 //   cluster: ks CTAs splitting K, partial sums reduced through distributed
 //   shared memory (each CTA reduces and stores 64 / ks columns), so no
-//   global scratch and a fixed summation order.
+//   global scratch and a fixed summation order; launched with programmatic
+//   stream serialization (launch and prologue overlap the previous kernel).
 //   k-loop: lane (g, t) reads 32 weight bytes of rows g and 8 + g of its
 //   group and 32 x values of x row g (and g + 8). Within a block the lane's
 //   32 physical k positions 32t .. 32t+31 are the logical positions {2t,
@@ -1875,6 +1876,23 @@ __host__ __device__ constexpr int gv_smem(int nt) {
   return 1024 + GV_STAGES * gv_stage(nt) + 2 * 16 * GV_BN * 4 /*partials*/ + 2 * GV_STAGES * 8 /*barriers*/;
 }
 
+// Four finite e4m3 codes c0..c3 (bytes of w) -> bf16 pairs (c0, c1), (c2, c3),
+// exact: each 16-bit half is first assembled as sign | 0000 e3e2e1e0 | m2m1m0 0000
+// (the code's exponent and mantissa where a bf16 has them, exponent bias 0
+// instead of 127), then one packed multiply by 2^120 rebiases it; subnormal
+// codes come out right from the same multiply. The high byte of a half is
+// (c & 0x80) | ((c >> 4) & 7), the low byte (c & 15) << 4: built for all four
+// codes at once and interleaved with two byte permutes.
+__device__ __forceinline__ void e4m3x4_to_bf16x2x2(uint32_t w, uint32_t &o01, uint32_t &o23) {
+  const uint32_t lo = (w << 4) & 0xF0F0F0F0u;
+  const uint32_t hi = (w & 0x80808080u) | ((w >> 4) & 0x07070707u);
+  uint32_t p01, p23;
+  asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(p01) : "r"(lo), "r"(hi));
+  asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(p23) : "r"(lo), "r"(hi));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o01) : "r"(p01), "r"(0x7B807B80u));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o23) : "r"(p23), "r"(0x7B807B80u));
+}
+
 template <int WF, bool F16>
 __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o)[16]) {
   const uint32_t q[2][4] = {{raw[0].x, raw[0].y, raw[0].z, raw[0].w}, {raw[1].x, raw[1].y, raw[1].z, raw[1].w}};
@@ -1883,8 +1901,12 @@ __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o
     for (int h = 0; h < 2; h++)
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        o[8 * h + 2 * i] = fp8x2_fast<WF, F16>(q[h][i], 0x4140u, 0x1404u);
-        o[8 * h + 2 * i + 1] = fp8x2_fast<WF, F16>(q[h][i], 0x4342u, 0x3424u);
+        if constexpr (WF == FP8B200_E4M3 && !F16) {
+          e4m3x4_to_bf16x2x2(q[h][i], o[8 * h + 2 * i], o[8 * h + 2 * i + 1]);
+        } else {
+          o[8 * h + 2 * i] = fp8x2_fast<WF, F16>(q[h][i], 0x4140u, 0x1404u);
+          o[8 * h + 2 * i + 1] = fp8x2_fast<WF, F16>(q[h][i], 0x4342u, 0x3424u);
+        }
       }
   } else {  // NaN / inf codes: conversion instructions
 #pragma unroll
@@ -1944,6 +1966,10 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
     tma_prefetch_desc(&tmap_x);
   }
   __syncthreads();
+  // programmatic dependent launch: the next kernel may launch now; nothing in
+  // global memory is read or written before the previous kernel has completed
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   float acc[NT][4] = {};
   const int rg = warp & 3, par = warp >> 2;  // consumers: row group, k-block parity
@@ -2441,17 +2467,19 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
         }
       }
       cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
+      cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = (unsigned)ks;
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.gridDim = dim3((unsigned)ks, (unsigned)nb, 1);
       cfg.blockDim = dim3(GV_THREADS, 1, 1);
       cfg.dynamicSmemBytes = (size_t)smem;
       cfg.stream = (cudaStream_t)stream;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
+      cfg.numAttrs = 2;
       cudaLaunchKernelEx(&cfg, kern, mw, mx, (int)M, (int)N, (int)kslice, p);
       count_launch();
       return check_launch("linear_fp8w");
