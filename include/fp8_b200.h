@@ -282,7 +282,9 @@ int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
  * output tile, or per 256x256 tile where the wider tiles would leave too many
  * SMs idle in the last wave; else the single-CTA kernel with 128x256 tiles),
  * 1 = always single-CTA, 2 = always CTA-pair 256x256, 3 = always small-M
- * (tiles of 256 rows of A when M > 256), 4 = always CTA-pair 256x512.
+ * (tiles of 256 rows of A when M > 256), 4 = always CTA-pair 256x512 (or
+ * 256x480 where the shape picks it; 256x256 when the output rows are not
+ * 16-byte aligned, since the 256x512 kernel stores through a tensor map).
  * Path 3 also sends fp8b200_linear_fp8w calls with M <= 16 to its tcgen05
  * small-M kernel instead of the warp-level MMA kernel.
  * Applies to launches from the calling host thread only; for tests and tuning.

@@ -72,6 +72,8 @@ struct Params {
   int w_fp8;                                  // fp8-weight linear: weight format (FP8B200_E4M3 / E5M2)
   int kb_elems;                               // elements per 128-byte k-block (128 fp8, 64 16-bit)
   int act_f16;                                // fp8-weight linear: activations f16 (1) or bf16 (0)
+  int w_bn1;                                  // 256x512 kernel: width of the second 256-row MMA (256 or 224)
+  uint32_t idesc1;                            // its instruction descriptor (N = w_bn1)
 };
 
 // Status word: 0 = ok, otherwise (launch epoch << 32) | (1 << 31) | site of
@@ -441,7 +443,7 @@ __device__ __forceinline__ void store_chunk_tma(const Params &p, const CUtensorM
 // TMEM loads run one chunk ahead of the conversion (two register sets), so
 // their latency hides behind the previous chunk's arithmetic.
 __device__ __forceinline__ void drain_accumulator_tma(const Params &p, const CUtensorMap *tmap_d, uint32_t t_acc,
-                                                      int row0, int n0, int quarter, int lane, float rs_t,
+                                                      int row0, int n0, int width, int quarter, int lane, float rs_t,
                                                       const float *col_scale, const float *col_bias, float sr,
                                                       uint32_t buf, int cfirst, int cstep) {
   const int row = row0 + quarter * 32 + lane;
@@ -449,7 +451,7 @@ __device__ __forceinline__ void drain_accumulator_tma(const Params &p, const CUt
   const uint32_t t_row = t_acc + ((uint32_t)(quarter * 32) << 16);
   const int esz = p.out_dtype == FP8B200_F32 ? 4 : (p.out_dtype == FP8B200_BF16 || p.out_dtype == FP8B200_F16) ? 2 : 1;
   const int y0 = row0 + quarter * 32;
-  const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);  // chunks with at least one column in range
+  const int nchunks = min(width / 32, (p.N - n0 + 31) / 32);  // chunks with at least one column in range
   if (cfirst >= nchunks) return;
   uint32_t ra[32], rb[32];
   tmem_ld_32x32b_x32(t_row + (uint32_t)(cfirst * 32), ra);
@@ -860,7 +862,8 @@ constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + W_EPI_WARPS * W_STG_BYTE
 template <int KIND>  // 0: kind::f8f6f4 (fp8 operands, K = 32 per MMA), 1: kind::f16 (16-bit operands, K = 16)
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W_THREADS, 1)
 scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                      const __grid_constant__ CUtensorMap tmap_d, const Params p) {
+                      const __grid_constant__ CUtensorMap tmap_b1, const __grid_constant__ CUtensorMap tmap_d,
+                      const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -896,6 +899,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_b1);
     if (p.tma_store) tma_prefetch_desc(&tmap_d);
   }
   if (warp == 1) {
@@ -919,7 +923,10 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         int tm, tn;
         tile_coords(p, tile, tm, tn);
         const int arow = tm * (2 * BM) + (int)rank * BM;
-        const int brow0 = tn * WIDE_BN + (int)rank * HALF_B;
+        const int tw = PAIR_BN + p.w_bn1;  // tile width: 512, or 480 (second MMA N = 224)
+        const int brow0 = tn * tw + (int)rank * HALF_B;
+        // second block: each CTA holds w_bn1 / 2 rows of it (tmap_b1's box height)
+        const int brow1 = tn * tw + PAIR_BN + (int)rank * (p.w_bn1 / 2);
         for (int kb = 0; kb < p.num_kb; kb++) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, p.epoch, 1)) { ok = false; break; }
           if (p.debug_skip_first_load) { ok = false; break; }
@@ -929,7 +936,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           const int kx = kb * p.kb_elems;  // tensor-map coordinate of the k-block
           tma_load_2d_pair(st, &tmap_a, leader_full, kx, arow);
           tma_load_2d_pair(st + A2_BYTES, &tmap_b, leader_full, kx, brow0);
-          tma_load_2d_pair(st + A2_BYTES + B2_BYTES, &tmap_b, leader_full, kx, brow0 + PAIR_BN);
+          tma_load_2d_pair(st + A2_BYTES + B2_BYTES, &tmap_b1, leader_full, kx, brow1);
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -976,7 +983,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc,
+            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1,
                              (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(empty_bar(stage));
@@ -997,7 +1004,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
             umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
-            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc, 1u);
+            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1, 1u);
           }
           umma_commit_pair(empty_bar(stage));
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
@@ -1029,7 +1036,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc, 1u);
+            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1, 1u);
           }
           umma_commit_pair(empty_bar(stage));
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
@@ -1055,8 +1062,9 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
       int tm, tn;
       tile_coords(p, tile, tm, tn);
       wide_epilogue_sync();  // the previous tile's column tables are no longer read
-      for (int j = etid; j < WIDE_BN; j += 32 * W_EPI_WARPS) {
-        const int col = tn * WIDE_BN + j;
+      const int tw = PAIR_BN + p.w_bn1;
+      for (int j = etid; j < tw; j += 32 * W_EPI_WARPS) {
+        const int col = tn * tw + j;
         const bool in = col < p.N;
         s_scale[j] = in ? (p.sb_rowwise ? __ldg(p.sb + col) : sb_t) : 0.0f;
         s_bias[j] = (in && p.bias != nullptr) ? load_bias(p.bias, p.bias_dtype, col) : 0.0f;
@@ -1070,8 +1078,9 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         if (!ok) break;
         tc_fence_after();
-        drain_accumulator_tma(p, &tmap_d, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * WIDE_BN + h * PAIR_BN,
-                              quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN, sr, buf, sub, 2);
+        drain_accumulator_tma(p, &tmap_d, tmem_base + (uint32_t)(h * PAIR_BN), row0, tn * tw + h * PAIR_BN,
+                              h ? p.w_bn1 : PAIR_BN, quarter, lane, sa_t, s_scale + h * PAIR_BN, s_bias + h * PAIR_BN,
+                              sr, buf, sub, 2);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(h), 0));
@@ -2119,16 +2128,29 @@ int pair_clusters(int dev, bool wide) {
   return c;
 }
 
-// The wide kernel does twice the work per tile; prefer it unless its tile
-// count fills the resident clusters in so few waves that the coarser
+// Tile width of the wide kernel: 512 columns, or 480 (second MMA N = 224)
+// where that fills the resident CTA pairs in fewer column-waves: cost =
+// waves x width, and 480 must win by 5 % (it moves 7 % more operand bytes
+// per flop). 4096^3 and the 1024-8192-row shards of 8192^3: 2 x 480 against
+// 2 x 512 (or 1 x 480 against 1 x 512).
+int wide_width(int dev, int64_t M, int64_t N) {
+  const int64_t slots = pair_clusters(dev, true);
+  const int64_t tm = (M + 2 * BM - 1) / (2 * BM);
+  auto cost = [&](int64_t w) { return (double)((tm * ((N + w - 1) / w) + slots - 1) / slots) * (double)w; };
+  return (N > 480 && cost(480) <= 0.95 * cost(WIDE_BN)) ? 480 : WIDE_BN;
+}
+
+// The wide kernel does about twice the work per tile; prefer it unless its
+// tile count fills the resident clusters in so few waves that the coarser
 // granularity costs more than 10 % against 256 x 256 tiles.
 bool prefer_wide(int dev, int64_t M, int64_t N) {
   if (N < WIDE_BN) return false;
   const int64_t slots = pair_clusters(dev, true);
   const int64_t tm = (M + 2 * BM - 1) / (2 * BM);
+  const int64_t w = wide_width(dev, M, N);
   const int64_t waves_pair = (tm * ((N + PAIR_BN - 1) / PAIR_BN) + slots - 1) / slots;
-  const int64_t waves_wide = (tm * ((N + WIDE_BN - 1) / WIDE_BN) + slots - 1) / slots;
-  return 2.0 * (double)waves_wide <= 1.1 * (double)waves_pair;
+  const int64_t waves_wide = (tm * ((N + w - 1) / w) + slots - 1) / slots;
+  return (double)(waves_wide * w) <= 1.1 * (double)(waves_pair * PAIR_BN);
 }
 
 // Resident clusters of `cs` CTAs of the small-M kernel with `smem` bytes of
@@ -2244,7 +2266,9 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
 
   const bool skinny = g_path == 3 || (g_path == 0 && M <= SK_MAX_MT);
   const bool pair = !skinny && (g_path == 2 || g_path == 4 || (g_path == 0 && M >= 2 * BM && N >= PAIR_BN));
-  const bool wide = pair && (g_path == 4 || (g_path == 0 && prefer_wide(dev, M, N)));
+  // the 256x512 kernel stores through an output tensor map: 16-byte aligned output rows only
+  const bool out_aligned = aligned16(D) && ((ldd * dtype_size(out_dtype)) % 16 == 0);
+  const bool wide = pair && out_aligned && (g_path == 4 || (g_path == 0 && prefer_wide(dev, M, N)));
   // small-M kernel: MT rows of A per tile (M rounded up to 16, at most 256)
   const int mt = skinny ? (int)std::min<int64_t>(SK_MAX_MT, (M + 15) / 16 * 16) : 0;
   CUtensorMap ma, mb;
@@ -2260,8 +2284,10 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     p.tiles_n = (int)((N + SK_BN - 1) / SK_BN);
   } else {
     p.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
-    p.tiles_n = (int)((N + (wide ? WIDE_BN : BN) - 1) / (wide ? WIDE_BN : BN));
+    const int tw = wide ? wide_width(dev, M, N) : BN;
+    p.tiles_n = (int)((N + tw - 1) / tw);
   }
+  p.w_bn1 = wide ? wide_width(dev, M, N) - PAIR_BN : 0;
   if ((long long)p.tiles_m * p.tiles_n > 0x7FFFFFFFLL / 8) return set_error(FP8B200_EINVAL, "scaled_mm: too many tiles");
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.sa = scale_a; p.sb = scale_b;
@@ -2271,18 +2297,19 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.scale_result = scale_result;
   p.D = D; p.ldd = ldd; p.out_dtype = out_dtype;
   const int esz = dtype_size(out_dtype);
-  p.vec_store = aligned16(D) && ((ldd * esz) % 16 == 0);
+  p.vec_store = out_aligned;
   // kind::f8f6f4 operand formats: 0 e4m3, 1 e5m2, 5 e2m1
   auto mma_fmt = [](int d) { return d == FP8B200_E5M2 ? 1u : d == FP8B200_E2M1 ? 5u : 0u; };
   const uint32_t afmt = mma_fmt(a_dtype), bfmt = mma_fmt(b_dtype);
   // TMA bytes per stage: a box row carries 128 bytes of float8 or 64 bytes of packed float4; the CTA
   // pairs credit both CTAs' loads to the leader's barrier
   const uint32_t a_rb = a4 ? 64u : 128u, b_rb = b4 ? 64u : 128u;
-  p.tx_bytes = (uint32_t)a_box * a_rb + (uint32_t)b_box * b_rb * (wide ? 2u : 1u);
+  p.tx_bytes = (uint32_t)a_box * a_rb + (uint32_t)b_box * b_rb + (wide ? (uint32_t)(p.w_bn1 / 2) * b_rb : 0u);
   if (pair) p.tx_bytes *= 2u;
   // instruction descriptor: f32 accumulate, A/B formats, both K-major, N>>3, M>>4
   const uint32_t mma_m = pair ? 2 * BM : BM;
   p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((mma_m >> 4) << 24);
+  p.idesc1 = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(p.w_bn1 >> 3) << 17) | ((mma_m >> 4) << 24);
   p.timeout_ns = g_timeout_ns;
   p.epoch = next_epoch();
   p.debug_skip_first_load = g_debug_skip_first_load;
@@ -2292,9 +2319,12 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   p.tma_store = 0;
   CUtensorMap md;
   memset(&md, 0, sizeof(md));
-  if (wide && p.vec_store) {
+  CUtensorMap mb1 = mb;  // the wide kernel's second B block: w_bn1 / 2 rows per CTA
+  if (wide) {
     if (int rc = make_out_map(&md, D, M, N, ldd, esz)) return rc;
     p.tma_store = 1;
+    if (p.w_bn1 != PAIR_BN)
+      if (int rc = make_kmajor_map(&mb1, B, N, K, ldb, p.w_bn1 / 2, b4)) return rc;
   }
   int sk_smem = 0;
   if (skinny) {
@@ -2327,7 +2357,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel<false>, ma, mb, p);
   } else if (wide) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
-    scaled_mm_wide_kernel<0><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
+    scaled_mm_wide_kernel<0><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, mb1, md, p);
   } else if (pair) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, false));
     scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);
@@ -2485,7 +2515,12 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       return check_launch("linear_fp8w");
     }
   }
-  if (M <= SK_MAX_MT) {
+  // 16 < M <= 256: the small-M kernel (K split over a cluster) unless the CTA-pair kernel's
+  // 256-wide column tiles alone occupy at least half of the resident CTA pairs (large N),
+  // where its four converter groups move the weights faster (N = 14336: 52 against 92 us)
+  const bool pair_mid = M > 16 && (N + PAIR_BN - 1) / PAIR_BN >= (int64_t)(pair_clusters(dev, false) / 2) &&
+                        g_path != 3;
+  if (M <= SK_MAX_MT && !pair_mid) {
     // few rows: the small-M kernel with weights dequantised on load (128
     // weight rows per tile on the MMA's M, K split over a cluster)
     static bool sk_attr[64] = {};
@@ -2640,11 +2675,13 @@ extern "C" int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64
   p.tma_store = 1;
   const uint32_t fmt = dtype == FP8B200_BF16 ? 1u : 0u;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(PAIR_BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+  p.w_bn1 = PAIR_BN;
+  p.idesc1 = p.idesc;
   p.timeout_ns = g_timeout_ns;
   p.epoch = next_epoch();
   p.debug_skip_first_load = g_debug_skip_first_load;
   const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
-  scaled_mm_wide_kernel<1><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, md, p);
+  scaled_mm_wide_kernel<1><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, mb, md, p);
   count_launch();
   return check_launch("gemm_16bit");
 }

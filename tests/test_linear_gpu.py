@@ -138,6 +138,22 @@ def test_rejects_bad_input(nat):
         nat.fp8_linear(x.bfloat16(), w, torch.ones(3))
 
 
+# ---------------------------------------------------------------- 16 < M <= 256 with many output channels
+@pytest.mark.parametrize("M,N,K", [(17, 14336, 256), (100, 9600, 384), (256, 10240, 128), (200, 14336, 1040)])
+@pytest.mark.parametrize("wdt", [E4, E5])
+def test_mid_rows_wide_output(nat, M, N, K, wdt):
+    """16 < M <= 256 and N wide enough that the CTA-pair dequant-on-load kernel's column
+    tiles fill half the GPU: that kernel serves these calls; per-channel scales, bias."""
+    g = torch.Generator().manual_seed(M * 3 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = rand_w((N, K), wdt, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda(), bias.cuda())
+    r, S = reference(x, w, s, bias.float())
+    check(out, r, S, f"{M}x{N}x{K} {wdt}")
+
+
 # ---------------------------------------------------------------- many rows: decode once + 16-bit GEMM
 @pytest.mark.parametrize("M,N,K", [(1024, 512, 256), (2048, 1024, 512), (1500, 776, 333), (1100, 100, 64)])
 @pytest.mark.parametrize("wdt", [E4, E5])

@@ -160,6 +160,39 @@ def test_strided_operands_and_output(nat, path):
     check_close(out, ref, S, "strided")
 
 
+@pytest.mark.parametrize("force", [0, 4], ids=["by_shape", "wide_requested"])
+@pytest.mark.parametrize("case", ["fp8_out_n1000", "bf16_ldd_odd"])
+def test_unaligned_output_rows(nat, force, case):
+    """Output rows that are not 16-byte aligned (fp8 output with N % 16 != 0, a bf16
+    output with an odd row stride) go to a kernel with plain stores even where the
+    256x512 kernel (which stores through a tensor map) would be chosen by shape or
+    requested."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    M, N, K = 512, 1000, 256
+    g = torch.Generator().manual_seed(21)
+    a = rand_fp8((M, K), E4, g).cuda()
+    b = rand_fp8((N, K), E4, g).cuda()
+    sa, sb = torch.tensor(0.01), torch.tensor(0.02)
+    L.check(L.lib().fp8b200_gemm_set_path(force), "gemm path")
+    try:
+        if case == "fp8_out_n1000":
+            out = nat.scaled_mm(a, b, sa, sb, out_dtype=torch.float32)
+            o8 = nat.scaled_mm(a, b, sa, sb, out_dtype=torch.float8_e4m3fn, scale_result=torch.tensor([1 / 16.0]))
+            torch.cuda.synchronize()
+            ref8 = (out.cpu() / 16.0).to(torch.float8_e4m3fn)
+            diff = (o8.cpu().float() - ref8.float()).abs()
+            # one e4m3 step at most (the f32 output and the fp8 epilogue round independently)
+            assert bool((diff <= ref8.float().abs() * 0.125 + 2.0 ** -9).all())
+        else:
+            buf = torch.empty(M, N + 1, dtype=torch.bfloat16, device="cuda")
+            out = nat.scaled_mm(a, b, sa, sb, out_dtype=torch.bfloat16, out=buf[:, :N])
+            torch.cuda.synchronize()
+        ref, S = O.scaled_mm_ref(codes(a), codes(b), 0.01, 0.02)
+        check_close(out, ref, S, f"unaligned output ({case}, path {force})")
+    finally:
+        L.check(L.lib().fp8b200_gemm_set_path(0), "gemm path")
+
+
 def test_invalid_calls_raise(nat):
     a = torch.zeros(32, 64, dtype=torch.uint8, device="cuda").view(E4)
     b = torch.zeros(48, 64, dtype=torch.uint8, device="cuda").view(E4)
