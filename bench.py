@@ -898,7 +898,9 @@ class ScaledMM:
         foot = (e - s) * kb + N * kb + 2 * (e - s) * N
         metric = {"scaled_mm": "scaled_mm_TFLOPS", "scaled_mm_rowwise": "scaled_mm_rowwise_TFLOPS",
                   "fp4_scaled_mm": "fp4_scaled_mm_TFLOPS"}[name]
-        return {"metric": metric, "unit": "TFLOP/s", "splits": True, "bound": "tensor",
+        # packed FP4 x FP4 with K a multiple of 256 runs as tcgen05 kind::mxf4: four times the bf16 rate
+        bound = "tensor_fp4" if (fp4 and K % 256 == 0) else "tensor"
+        return {"metric": metric, "unit": "TFLOP/s", "splits": True, "bound": bound,
                 "dtype": "e2m1xe2m1->bf16 (f32 acc)" if fp4 else "e4m3xe4m3->bf16 (f32 acc)",
                 "config": {"workload": name, "M": M, "N": N, "K": K,
                            "scales": "rowwise" if rowwise else "tensorwise", "out": "bf16",
@@ -1471,18 +1473,21 @@ def gpu_line(args, ctx):
     # same way, back to back); the fastest repeat (burst clocks) is reported
     # beside it against the burst peak.
     bound = desc["bound"]
-    long_run = bound in ("tensor", "tensor_bf16") and sum(regions) >= 100.0
+    long_run = bound in ("tensor", "tensor_bf16", "tensor_fp4") and sum(regions) >= 100.0
     bf16_key = "bf16_tflops_sustained" if (getattr(w, "sustained", False) or long_run) \
         and "bf16_tflops_sustained" in pk else "bf16_tflops"
     if long_run and not extra:
         burst = total_work / ctx.ws / (min(regions) / args.steps * 1e-3) / scale
-        burst_peak = (2.0 if bound == "tensor" else 1.0) * pk["bf16_tflops"]
+        burst_peak = {"tensor": 2.0, "tensor_fp4": 4.0}.get(bound, 1.0) * pk["bf16_tflops"]
         extra = {"burst": {"achieved": round(burst, 2), "peak": burst_peak, "frac": round(burst / burst_peak, 4),
                            "from": "fastest timed repeat, against the burst peak"}}
     if bound == "hbm":
         peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
     elif bound == "tensor_bf16":
         peak, punit, psrc = pk[bf16_key], "TFLOP/s", f"{pk_kind} {bf16_key}"
+    elif bound == "tensor_fp4":
+        peak, punit = 4.0 * pk[bf16_key], "TFLOP/s"
+        psrc = f"4 x {pk_kind} {bf16_key} (dense fp4 kind::mxf4 issue rate is four times bf16 on tcgen05)"
     else:
         peak, punit = 2.0 * pk[bf16_key], "TFLOP/s"
         psrc = f"2 x {pk_kind} {bf16_key} (dense fp8/fp6/fp4 kind::f8f6f4 issue rate is twice bf16 on tcgen05)"
@@ -1500,7 +1505,7 @@ def gpu_line(args, ctx):
             "dtype": desc["dtype"],
             "e2e": {"value": round(e2e_value, 3), "unit": desc["unit"], "h2d_bytes_per_step": int(w.h2d),
                     "d2h_bytes_per_step": int(w.d2h)},
-            "roofline": {"bound": "tensor" if bound == "tensor_bf16" else bound, "achieved": round(achieved, 2),
+            "roofline": {"bound": "tensor" if bound.startswith("tensor") else bound, "achieved": round(achieved, 2),
                          "peak": peak, "unit": punit, "frac": round(achieved / peak, 4), "peak_source": psrc,
                          "per": "GPU" if ctx.ws > 1 else "launch-averaged step",
                          "traffic": profile_traffic(getattr(w, "profile", None)), **extra},

@@ -833,13 +833,30 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, u
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// One CTA-pair MMA of the kind the kernel is built for; the descriptors step
-// through the 128-byte swizzled rows 32 bytes per MMA in both cases.
+// Packed FP4 x FP4 with every block scale 1.0: kind::mxf4 multiplies two e2m1
+// values per operand byte, K = 64 per instruction, at twice the f8f6f4 rate;
+// its block32 scale factors (UE8M0) are read from tensor memory at sf (all
+// 0x7F = 2^0 here), so the product equals the unscaled one.
+__device__ __forceinline__ void umma_mxf4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate, uint32_t sf) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%5], p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sf)
+      : "memory");
+}
+
+// KIND 0: kind::f8f6f4 (8-bit codes, or e2m1 padded to a byte, K = 32 per MMA);
+// KIND 1: kind::f16 (16-bit operands, K = 16); KIND 2: kind::mxf4 (packed
+// e2m1, K = 64, unit block scales at sf). Each steps through the 128-byte
+// swizzled rows 32 bytes per MMA.
 template <int KIND>
-__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+__device__ __forceinline__ void umma_pair(uint32_t sf, uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accumulate) {
   if constexpr (KIND == 0) umma_f8f6f4_pair(tmem_d, adesc, bdesc, idesc, accumulate);
-  else umma_f16_pair(tmem_d, adesc, bdesc, idesc, accumulate);
+  else if constexpr (KIND == 1) umma_f16_pair(tmem_d, adesc, bdesc, idesc, accumulate);
+  else umma_mxf4_pair(tmem_d, adesc, bdesc, idesc, accumulate, sf);
 }
 
 // ------------------------------------------------------------------ CTA-pair wide kernel
@@ -859,7 +876,25 @@ constexpr int W_THREADS = 64 + 32 * W_EPI_WARPS;     // producer warp, MMA warp,
 constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + W_EPI_WARPS * W_STG_BYTES /*epilogue staging*/ +
                              1024 /*align*/ + 2 * WIDE_BN * 4 /*column tables*/ + 256;
 
-template <int KIND>  // 0: kind::f8f6f4 (fp8 operands, K = 32 per MMA), 1: kind::f16 (16-bit operands, K = 16)
+// TMEM columns of the unit block scales for kind::mxf4 (the 256 x 480 tile's
+// accumulators use columns 0-479)
+constexpr int W_SF_COL = 480;
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// KIND 0: kind::f8f6f4 (fp8 codes or byte-padded e2m1, K = 32 per MMA); 1: kind::f16 (16-bit
+// operands, K = 16); 2: kind::mxf4 (packed e2m1, K = 64, unit block scales; 256 x 480 tiles)
+template <int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W_THREADS, 1)
 scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_b1, const __grid_constant__ CUtensorMap tmap_d,
@@ -912,6 +947,21 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+  const uint32_t sf_tmem = tmem_base + (uint32_t)W_SF_COL;
+  if constexpr (KIND == 2) {
+    // unit block scales: 0x7F (2^0 in UE8M0) in columns W_SF_COL.. of every lane of both
+    // CTAs' tensor memory, written by four warps, one per 32-lane quarter (warp % 4)
+    if (warp >= 2 && warp < 6) {
+      uint32_t ones[32];
+#pragma unroll
+      for (int j = 0; j < 32; j++) ones[j] = 0x7F7F7F7Fu;
+      tmem_st_32x32b_x32(sf_tmem + ((uint32_t)((warp & 3) * 32) << 16), ones);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+  }
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs)
@@ -968,7 +1018,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; k++) {
               const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-              umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_pair<KIND>(sf_tmem, tmem_base, adesc + koff, b0desc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
             }
             if (++st == W_STAGES) { st = 0; ph ^= 1u; }
           }
@@ -983,7 +1033,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1,
+            umma_pair<KIND>(sf_tmem, tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1,
                              (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(empty_bar(stage));
@@ -1003,8 +1053,8 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
-            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1, 1u);
+            umma_pair<KIND>(sf_tmem, tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
+            umma_pair<KIND>(sf_tmem, tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1, 1u);
           }
           umma_commit_pair(empty_bar(stage));
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
@@ -1022,7 +1072,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; k++) {
               const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-              umma_pair<KIND>(tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
+              umma_pair<KIND>(sf_tmem, tmem_base, adesc + koff, b0desc + koff, p.idesc, 1u);
             }
             if (++st == W_STAGES) { st = 0; ph ^= 1u; }
           }
@@ -1036,7 +1086,7 @@ scaled_mm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; k++) {
             const uint64_t koff = (uint64_t)((k * UMMA_K) >> 4);
-            umma_pair<KIND>(tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1, 1u);
+            umma_pair<KIND>(sf_tmem, tmem_base + (uint32_t)PAIR_BN, adesc + koff, b1desc + koff, p.idesc1, 1u);
           }
           umma_commit_pair(empty_bar(stage));
           if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
@@ -1766,15 +1816,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows, bool fp4);
+int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows, int fp4);
 
 // Tensor maps describe only an address, extents, a stride and a box, so an
 // encoded map stays valid for any later call with the same five values. A
 // small per-thread cache skips the driver's encode on repeated calls (the
 // decode-time case: the same weights and activation buffers every step).
 int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows,
-                    bool fp4 = false) {
-  struct Entry { const void *ptr; int64_t rows, k, ld; int box; int dev; bool fp4; CUtensorMap map; };
+                    int fp4 = 0) {
+  struct Entry { const void *ptr; int64_t rows, k, ld; int box; int dev; int fp4; CUtensorMap map; };
   constexpr int kEntries = 32;
   thread_local Entry cache[kEntries];
   thread_local int used = 0, next = 0;
@@ -1800,24 +1850,28 @@ int make_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, in
   return FP8B200_OK;
 }
 
-// K-major operand map: boxes of 128 k-values x box_rows rows, 128-byte
-// swizzle. fp8 codes land as they are (128 bytes per box row). Packed FP4
-// (e2m1, two values per byte, k-value 2i in the low nibble) is read as
-// 16U4_ALIGN16B: every 8 bytes (16 values) of a row land in a 16-byte unit of
-// shared memory followed by 8 bytes of padding, the layout tcgen05.mma
-// kind::f8f6f4 reads 4-bit operands in; the box row is again 128 bytes, so
-// the kernels' stage layout and descriptors are the fp8 ones. The TMA
-// transaction counts the 64 bytes of packed data per box row, not the
+// K-major operand map: boxes of one 128-byte swizzled row x box_rows rows.
+// fp4 = 0: fp8 codes, 128 values per box row, landing as they are.
+// fp4 = 1: packed FP4 (e2m1, two values per byte, k-value 2i in the low
+// nibble) read as 16U4_ALIGN16B: every 8 bytes (16 values) of a row land in a
+// 16-byte unit of shared memory followed by 8 bytes of padding, the layout
+// tcgen05.mma kind::f8f6f4 reads 4-bit operands in; 128 values per box row
+// again, so the kernels' stage layout and descriptors are the fp8 ones. The
+// TMA transaction counts the 64 bytes of packed data per box row, not the
 // padding. Requirements (checked by the caller): k a multiple of 128, ld a
 // multiple of 32 bytes, a 32-byte aligned base.
-int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows, bool fp4) {
+// fp4 = 2: packed FP4 kept packed (16U4_ALIGN8B), 256 values per 128-byte box
+// row: the operand layout of kind::mxf4.
+int encode_kmajor_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t k, int64_t ld, int box_rows, int fp4) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(FP8B200_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)(fp4 == 2 ? 2 * BK : BK), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+  const CUtensorMapDataType dt = fp4 == 2 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN8B
+                                 : fp4 == 1 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = enc(m, dt, 2,
                    const_cast<void *>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -2260,6 +2314,8 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
       e = cudaFuncSetAttribute(scaled_mm_skinny_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_MAX);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_wide_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(scaled_mm_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
   }
@@ -2269,25 +2325,31 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   // the 256x512 kernel stores through an output tensor map: 16-byte aligned output rows only
   const bool out_aligned = aligned16(D) && ((ldd * dtype_size(out_dtype)) % 16 == 0);
   const bool wide = pair && out_aligned && (g_path == 4 || (g_path == 0 && prefer_wide(dev, M, N)));
+  // FP4 x FP4 on the CTA-pair 256-row tiles runs as kind::mxf4 (packed operands, K = 64 per
+  // MMA at twice the f8f6f4 rate, unit block scales) on 256 x 480 tiles, which leave TMEM
+  // columns for the scales; 256-value k-blocks, so K a multiple of 256
+  const bool mx = a4 && b4 && wide && K % 256 == 0;
   // small-M kernel: MT rows of A per tile (M rounded up to 16, at most 256)
   const int mt = skinny ? (int)std::min<int64_t>(SK_MAX_MT, (M + 15) / 16 * 16) : 0;
   CUtensorMap ma, mb;
   const int a_box = skinny ? mt : BM, b_box = skinny ? SK_BN : (pair ? HALF_B : BN);
-  if (int rc = make_kmajor_map(&ma, A, M, K, lda, a_box, a4)) return rc;
-  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, b_box, b4)) return rc;
+  const int a_mode = mx ? 2 : (a4 ? 1 : 0), b_mode = mx ? 2 : (b4 ? 1 : 0);
+  if (int rc = make_kmajor_map(&ma, A, M, K, lda, a_box, a_mode)) return rc;
+  if (int rc = make_kmajor_map(&mb, B, N, K, ldb, b_box, b_mode)) return rc;
 
   Params p;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
-  p.num_kb = (int)((K + BK - 1) / BK);
+  const int kb_elems = mx ? 2 * BK : BK;  // k-values per 128-byte smem row
+  p.num_kb = (int)((K + kb_elems - 1) / kb_elems);
   if (skinny) {
     p.tiles_m = (int)((M + mt - 1) / mt);
     p.tiles_n = (int)((N + SK_BN - 1) / SK_BN);
   } else {
     p.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
-    const int tw = wide ? wide_width(dev, M, N) : BN;
+    const int tw = mx ? 480 : wide ? wide_width(dev, M, N) : BN;
     p.tiles_n = (int)((N + tw - 1) / tw);
   }
-  p.w_bn1 = wide ? wide_width(dev, M, N) - PAIR_BN : 0;
+  p.w_bn1 = mx ? 480 - PAIR_BN : wide ? wide_width(dev, M, N) - PAIR_BN : 0;
   if ((long long)p.tiles_m * p.tiles_n > 0x7FFFFFFFLL / 8) return set_error(FP8B200_EINVAL, "scaled_mm: too many tiles");
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.sa = scale_a; p.sb = scale_b;
@@ -2303,18 +2365,24 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
   const uint32_t afmt = mma_fmt(a_dtype), bfmt = mma_fmt(b_dtype);
   // TMA bytes per stage: a box row carries 128 bytes of float8 or 64 bytes of packed float4; the CTA
   // pairs credit both CTAs' loads to the leader's barrier
-  const uint32_t a_rb = a4 ? 64u : 128u, b_rb = b4 ? 64u : 128u;
+  const uint32_t a_rb = (a4 && !mx) ? 64u : 128u, b_rb = (b4 && !mx) ? 64u : 128u;
   p.tx_bytes = (uint32_t)a_box * a_rb + (uint32_t)b_box * b_rb + (wide ? (uint32_t)(p.w_bn1 / 2) * b_rb : 0u);
   if (pair) p.tx_bytes *= 2u;
   // instruction descriptor: f32 accumulate, A/B formats, both K-major, N>>3, M>>4
   const uint32_t mma_m = pair ? 2 * BM : BM;
   p.idesc = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((mma_m >> 4) << 24);
   p.idesc1 = (1u << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(p.w_bn1 >> 3) << 17) | ((mma_m >> 4) << 24);
+  if (mx) {
+    // block-scaled descriptor: A/B format 1 (e2m1, kind::mxf4), scale format 1 (UE8M0) at bit 23,
+    // scale-factor ids 0, dense K = 64; no accumulator-format field (always f32)
+    p.idesc = (1u << 7) | (1u << 10) | ((uint32_t)(PAIR_BN >> 3) << 17) | (1u << 23) | ((mma_m >> 4) << 24);
+    p.idesc1 = (1u << 7) | (1u << 10) | ((uint32_t)(p.w_bn1 >> 3) << 17) | (1u << 23) | ((mma_m >> 4) << 24);
+  }
   p.timeout_ns = g_timeout_ns;
   p.epoch = next_epoch();
   p.debug_skip_first_load = g_debug_skip_first_load;
   p.sk_mt = mt;
-  p.kb_elems = BK;
+  p.kb_elems = kb_elems;
   p.sk_stages = p.sk_cs = p.sk_tmem_cols = 0;
   p.tma_store = 0;
   CUtensorMap md;
@@ -2324,7 +2392,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     if (int rc = make_out_map(&md, D, M, N, ldd, esz)) return rc;
     p.tma_store = 1;
     if (p.w_bn1 != PAIR_BN)
-      if (int rc = make_kmajor_map(&mb1, B, N, K, ldb, p.w_bn1 / 2, b4)) return rc;
+      if (int rc = make_kmajor_map(&mb1, B, N, K, ldb, p.w_bn1 / 2, b_mode)) return rc;
   }
   int sk_smem = 0;
   if (skinny) {
@@ -2357,7 +2425,8 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     cudaLaunchKernelEx(&cfg, scaled_mm_skinny_kernel<false>, ma, mb, p);
   } else if (wide) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, true));
-    scaled_mm_wide_kernel<0><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, mb1, md, p);
+    if (mx) scaled_mm_wide_kernel<2><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, mb1, md, p);
+    else scaled_mm_wide_kernel<0><<<2 * clusters, W_THREADS, W_SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, mb1, md, p);
   } else if (pair) {
     const int clusters = std::min(p.num_tiles, pair_clusters(dev, false));
     scaled_mm_pair_kernel<<<2 * clusters, THREADS, SMEM2_BYTES, (cudaStream_t)stream>>>(ma, mb, p);

@@ -193,3 +193,30 @@ def test_invalid_fp4_calls(nat):
                                    s.data_ptr(), 0, s.data_ptr(), 0, None, 0, None, out.data_ptr(), L.F32, 64,
                                    torch.cuda.current_stream().cuda_stream)
     assert rc == -1 and b"32-byte" in L.lib().fp8b200_last_error()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 480, 256), (512, 1000, 1024), (300, 2048, 4096), (1024, 8192, 2048)])
+def test_block_scaled_path_matches_byte_padded_path(nat, M, N, K):
+    """FP4 x FP4 on the 256x480 CTA-pair kernel runs as tcgen05 kind::mxf4 (packed operands,
+    unit block scales); the 256x256 kernel (path 2) as kind::f8f6f4 on byte-padded operands.
+    Both accumulate exactly, so their outputs are identical, and equal the oracle within
+    one output ulp."""
+    from fp4_fp8_for_torch_mps import _lib as L
+    g = torch.Generator().manual_seed(M + N + K)
+    a, b = rand_fp4(M, K, g), rand_fp4(N, K, g)
+    sa = torch.rand(M, 1, generator=g) * 0.5 + 0.01
+    sb = torch.tensor(0.125)
+    outs = {}
+    try:
+        for path in (4, 2):
+            L.check(L.lib().fp8b200_gemm_set_path(path), "gemm path")
+            outs[path] = nat.scaled_mm(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(), out_dtype=torch.float32,
+                                       a_dtype=FP4, b_dtype=FP4)
+            torch.cuda.synchronize()
+    finally:
+        L.check(L.lib().fp8b200_gemm_set_path(0), "gemm path")
+    assert torch.equal(outs[4], outs[2])
+    rows = np.arange(0, M, max(1, M // 64))
+    ref, S = O.scaled_mm_ref(a.numpy(), b.numpy(), sa.numpy().reshape(-1), 0.125, fmt_a=O.FP4, fmt_b=O.FP4,
+                             rows=rows)
+    check(outs[4][torch.from_numpy(rows).cuda()], ref, S, 0.0, f"mxf4 {M}x{N}x{K}")
