@@ -200,7 +200,9 @@ int fp8b200_quantize_fp4(const void *src, int src_dtype, void *dst, int64_t n,
  *    stride ldd elements. K must be a positive multiple of 16; lda/ldb
  *    multiples of 16; A and B 16-byte aligned.
  * Accumulation is float32 on the tcgen05 tensor cores (kind::f8f6f4, which
- * takes e4m3, e5m2 and e2m1 operands at the same rate).
+ * takes e4m3, e5m2 and e2m1 operands at the same rate; e2m1 x e2m1 with K a
+ * multiple of 256 on large shapes runs as kind::mxf4 with unit block scales,
+ * at twice that rate and with the same result).
  * Replaces the reference's _scaled_mm override (ops.py:33-49) and the GEMM
  * kernels behind it: fp8_scaled_matmul_kernel (shaders/fp8_matmul.metal:
  * 145-180), fp8_scaled_vecmat_kernel (:183-226) and the decode+fp16-matmul
