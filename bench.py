@@ -661,6 +661,9 @@ class Quantize:
         self.x_host = x
         rows, cols = x.shape
         self.work, in_b, out_n = self._bytes(kind, rows, cols)
+        # a per-tensor scale needs the whole input's amax before the first code can be written, so the
+        # input is read twice (amax pass, encode pass): the line also reports that two-read bound
+        self.two_read_bytes = self.work + in_b if kind != "quantize_rows" else None
         n = x.numel()
         self.n = n
         self.sets = sets = rotating_sets(self.work)
@@ -1483,6 +1486,13 @@ def gpu_line(args, ctx):
                            "from": "fastest timed repeat, against the burst peak"}}
     if bound == "hbm":
         peak, punit, psrc = pk["hbm_gbs"], "GB/s", f"{pk_kind} hbm_gbs"
+        if getattr(w, "two_read_bytes", None):
+            moved = w.two_read_bytes / w.work * achieved
+            extra["two_read_bound"] = {
+                "bytes_per_step": int(w.two_read_bytes), "achieved": round(moved, 2),
+                "frac": round(moved / peak, 4),
+                "note": "bytes a per-tensor quantisation must move (input read twice: amax, then encode; "
+                        "output written once) over the step time, against the same HBM peak"}
     elif bound == "tensor_bf16":
         peak, punit, psrc = pk[bf16_key], "TFLOP/s", f"{pk_kind} {bf16_key}"
     elif bound == "tensor_fp4":

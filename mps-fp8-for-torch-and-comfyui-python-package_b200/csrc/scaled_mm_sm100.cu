@@ -1490,7 +1490,7 @@ scaled_mm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
 // bytes, 64-byte swizzle; TMA, completing on this CTA's barrier); four groups
 // of two converter warps (two weight rows per thread, k-blocks in turn)
 // convert the raw rows to the
-// activation type (exact, fp8x2_fast), write the 128-byte-swizzled K-major
+// activation type (exact, fp8x4_fast), write the 128-byte-swizzled K-major
 // half tile into a 4-slot ring, fence it to the async proxy and arrive on the
 // leader's `converted` barrier. (The weights come in through TMA, not loads
 // into registers: the release of that arrival would otherwise wait for every
@@ -1530,30 +1530,38 @@ __device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
   return *reinterpret_cast<const uint32_t *>(&b);
 }
 
-// Fast exact fp8 -> 16-bit conversion of two codes (bytes `sel` of w) without
-// conversion instructions: the code's exponent and mantissa bits are placed
-// where the target format's sit, the sign at bit 15, and the pair is scaled
-// by a power of two (the difference of the exponent biases) with one packed
-// multiply, which is exact for normal and subnormal codes alike. Codes with
-// an all-ones exponent (NaN for e4m3; inf / NaN for e5m2 into bf16) must not
-// come here (see fp8_unit_special); e5m2 -> f16 is a byte placement.
+// Fast exact fp8 -> 16-bit conversion of four codes (bytes of w) into the
+// pairs (code 0, code 1), (code 2, code 3), without conversion instructions:
+// each code's exponent and mantissa bits are placed where the target
+// format's sit, its sign at bit 15, and each pair is scaled by a power of two
+// (the difference of the exponent biases: e4m3 -> bf16 2^120, e4m3 -> f16
+// 2^8, e5m2 -> bf16 2^112) with one packed multiply, which is exact for
+// normal and subnormal codes alike. The placement takes one sign-replicating
+// byte permute per pair (low byte of each half: the code; high byte: copies
+// of its sign bit), one shift (the sign copies land on the sign bit) and one
+// mask. Codes with an all-ones exponent (NaN for e4m3; inf / NaN for e5m2
+// into bf16) must not come here (see fp8_unit_special); e5m2 -> f16 is a
+// byte placement.
 template <int WF, bool TO_F16>
-__device__ __forceinline__ uint32_t fp8x2_fast(uint32_t w, uint32_t sel_lowbytes, uint32_t sel_highbytes) {
-  uint32_t x, r;
-  if constexpr (WF == FP8B200_E5M2 && TO_F16) {
-    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(x) : "r"(w), "r"(sel_highbytes));  // code -> high byte of each half
-    return x;
+__device__ __forceinline__ void fp8x4_fast(uint32_t w, uint32_t &o01, uint32_t &o23) {
+  if constexpr (WF == FP8B200_E5M2 && TO_F16) {  // e5m2 is the high byte of an f16
+    asm("prmt.b32 %0, %1, 0, 0x1404;" : "=r"(o01) : "r"(w));
+    asm("prmt.b32 %0, %1, 0, 0x3424;" : "=r"(o23) : "r"(w));
   } else {
-    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(x) : "r"(w), "r"(sel_lowbytes));   // code -> low byte of each half
-    constexpr int SH = WF == FP8B200_E4M3 ? (TO_F16 ? 7 : 4) : 5;           // exponent-mantissa position
-    constexpr uint32_t EM = (WF == FP8B200_E4M3 ? 0x7Fu : 0x7Fu) << SH;
-    constexpr uint32_t MASK = EM | (EM << 16);
-    const uint32_t bits = ((x << SH) & MASK) | ((x << 8) & 0x80008000u);
-    // 2^(bias difference): e4m3 -> bf16 2^120, e4m3 -> f16 2^8, e5m2 -> bf16 2^112
+    uint32_t r01, r23;
+    asm("prmt.b32 %0, %1, 0, 0x9180;" : "=r"(r01) : "r"(w));  // halves {sign x8, code 0}, {sign x8, code 1}
+    asm("prmt.b32 %0, %1, 0, 0xB3A2;" : "=r"(r23) : "r"(w));  // codes 2, 3
+    constexpr int SH = WF == FP8B200_E4M3 ? (TO_F16 ? 7 : 4) : 5;
+    constexpr uint32_t MASK = WF == FP8B200_E4M3 ? (TO_F16 ? 0xBF80BF80u : 0x87F087F0u) : 0x8FE08FE0u;
     constexpr uint32_t SCALE = WF == FP8B200_E4M3 ? (TO_F16 ? 0x5C005C00u : 0x7B807B80u) : 0x77807780u;
-    if constexpr (TO_F16) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(SCALE));
-    else asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(bits), "r"(SCALE));
-    return r;
+    const uint32_t b01 = (r01 << SH) & MASK, b23 = (r23 << SH) & MASK;
+    if constexpr (TO_F16) {
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o01) : "r"(b01), "r"(SCALE));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o23) : "r"(b23), "r"(SCALE));
+    } else {
+      asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o01) : "r"(b01), "r"(SCALE));
+      asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o23) : "r"(b23), "r"(SCALE));
+    }
   }
 }
 
@@ -1589,10 +1597,7 @@ __device__ __forceinline__ void convert_weight_row(uint32_t raw, uint32_t dst, i
 #pragma unroll
     for (int c = 0; c < 4; c++)
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        o[c][2 * i] = fp8x2_fast<WF, TO_F16>(q[c][i], 0x4140u, 0x1404u);
-        o[c][2 * i + 1] = fp8x2_fast<WF, TO_F16>(q[c][i], 0x4342u, 0x3424u);
-      }
+      for (int i = 0; i < 4; i++) fp8x4_fast<WF, TO_F16>(q[c][i], o[c][2 * i], o[c][2 * i + 1]);
   } else {  // NaN / inf present: conversion instructions
 #pragma unroll
     for (int c = 0; c < 4; c++)
@@ -1939,23 +1944,6 @@ __host__ __device__ constexpr int gv_smem(int nt) {
   return 1024 + GV_STAGES * gv_stage(nt) + 2 * 16 * GV_BN * 4 /*partials*/ + 2 * GV_STAGES * 8 /*barriers*/;
 }
 
-// Four finite e4m3 codes c0..c3 (bytes of w) -> bf16 pairs (c0, c1), (c2, c3),
-// exact: each 16-bit half is first assembled as sign | 0000 e3e2e1e0 | m2m1m0 0000
-// (the code's exponent and mantissa where a bf16 has them, exponent bias 0
-// instead of 127), then one packed multiply by 2^120 rebiases it; subnormal
-// codes come out right from the same multiply. The high byte of a half is
-// (c & 0x80) | ((c >> 4) & 7), the low byte (c & 15) << 4: built for all four
-// codes at once and interleaved with two byte permutes.
-__device__ __forceinline__ void e4m3x4_to_bf16x2x2(uint32_t w, uint32_t &o01, uint32_t &o23) {
-  const uint32_t lo = (w << 4) & 0xF0F0F0F0u;
-  const uint32_t hi = (w & 0x80808080u) | ((w >> 4) & 0x07070707u);
-  uint32_t p01, p23;
-  asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(p01) : "r"(lo), "r"(hi));
-  asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(p23) : "r"(lo), "r"(hi));
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o01) : "r"(p01), "r"(0x7B807B80u));
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o23) : "r"(p23), "r"(0x7B807B80u));
-}
-
 template <int WF, bool F16>
 __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o)[16]) {
   const uint32_t q[2][4] = {{raw[0].x, raw[0].y, raw[0].z, raw[0].w}, {raw[1].x, raw[1].y, raw[1].z, raw[1].w}};
@@ -1963,14 +1951,7 @@ __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o
 #pragma unroll
     for (int h = 0; h < 2; h++)
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        if constexpr (WF == FP8B200_E4M3 && !F16) {
-          e4m3x4_to_bf16x2x2(q[h][i], o[8 * h + 2 * i], o[8 * h + 2 * i + 1]);
-        } else {
-          o[8 * h + 2 * i] = fp8x2_fast<WF, F16>(q[h][i], 0x4140u, 0x1404u);
-          o[8 * h + 2 * i + 1] = fp8x2_fast<WF, F16>(q[h][i], 0x4342u, 0x3424u);
-        }
-      }
+      for (int i = 0; i < 4; i++) fp8x4_fast<WF, F16>(q[h][i], o[8 * h + 2 * i], o[8 * h + 2 * i + 1]);
   } else {  // NaN / inf codes: conversion instructions
 #pragma unroll
     for (int h = 0; h < 2; h++)
