@@ -1911,16 +1911,19 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 // feeds them straight to the warp-level tensor-core instruction
 // mma.sync.m16n8k16 computing D^T = W x^T: 16 weight rows as the A operand,
 // 8 x rows as B (NT = 1 or 2 tiles, zero rows past M), float32 accumulators.
-//   CTA: 64 output channels; a producer warp whose lane 0 streams, per
-//   128-value k-block, the 64 x 128-byte weight tile and the block's x tile
+//   CTA: 16 NRG output channels (NRG = 4, or 7 where 64-channel CTAs would
+//   fill the SMs unevenly: 14336 channels are 224 CTAs of 64, two on 76 of
+//   the 148 SMs, or 128 CTAs of 112, one per SM; see gv_plan); a producer
+//   warp whose lane 0 streams, per 128-value
+//   k-block, the 16 NRG x 128-byte weight tile and the block's x tile
 //   (8 NT rows x 128 values, two 128-byte-wide boxes; rows past M are the
 //   TMA's zero fill) into a GV_STAGES-deep ring (128-byte swizzle, full /
-//   empty mbarriers, bounded waits); 8 consumer warps, two per 16-row group
-//   of channels, taking alternate k-blocks, so one warp's conversion and
-//   MMAs overlap its partner's shared-memory loads; nothing in the k-loop
-//   reads global memory;
+//   empty mbarriers, bounded waits); 2 NRG consumer warps, two per 16-row
+//   group of channels, taking alternate k-blocks, so one warp's conversion
+//   and MMAs overlap its partner's shared-memory loads; nothing in the
+//   k-loop reads global memory;
 //   cluster: ks CTAs splitting K, partial sums reduced through distributed
-//   shared memory (each CTA reduces and stores 64 / ks columns), so no
+//   shared memory (each CTA reduces and stores 16 NRG / ks columns), so no
 //   global scratch and a fixed summation order; launched with programmatic
 //   stream serialization (launch and prologue overlap the previous kernel).
 //   k-loop: lane (g, t) reads 32 weight bytes of rows g and 8 + g of its
@@ -1930,19 +1933,21 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 //   per step), the same permutation for A and B, which leaves the sum
 //   unchanged, and makes both operands' register pairs come straight from
 //   the conversions and the 16-byte loads.
-constexpr int GV_WARPS = 4;                        // 16-channel row groups per CTA
-constexpr int GV_CONSUMERS = 2 * GV_WARPS;         // two warps per row group, alternate k-blocks
-constexpr int GV_THREADS = 32 * (GV_CONSUMERS + 1);
-constexpr int GV_BN = 16 * GV_WARPS;  // 64 output channels per CTA
 constexpr int GV_BK = 128;
 constexpr int GV_STAGES = 8;  // k-blocks in flight per CTA (TMA ring)
-constexpr int GV_TILE = GV_BN * GV_BK;  // 64 weight rows x 128 codes, 8 KiB
+__host__ __device__ constexpr int gv_bn(int nrg) { return 16 * nrg; }          // output channels per CTA
+__host__ __device__ constexpr int gv_threads(int nrg) { return 32 * (2 * nrg + 1); }  // consumers + producer
+__host__ __device__ constexpr int gv_tile(int nrg) { return gv_bn(nrg) * GV_BK; }  // weight rows x 128 codes
 // x tile of a k-block: two 128-byte-wide boxes (values 0-63, 64-127) of 8 NT rows
 __host__ __device__ constexpr int gv_x_half(int nt) { return 8 * nt * 128; }
-__host__ __device__ constexpr int gv_stage(int nt) { return GV_TILE + 2 * gv_x_half(nt); }
-__host__ __device__ constexpr int gv_smem(int nt) {
-  return 1024 + GV_STAGES * gv_stage(nt) + 2 * 16 * GV_BN * 4 /*partials*/ + 2 * GV_STAGES * 8 /*barriers*/;
+__host__ __device__ constexpr int gv_stage(int nt, int nrg) { return gv_tile(nrg) + 2 * gv_x_half(nt); }
+__host__ __device__ constexpr int gv_smem(int nt, int nrg) {
+  return 1024 + GV_STAGES * gv_stage(nt, nrg) + 2 * 16 * gv_bn(nrg) * 4 /*partials*/ + 2 * GV_STAGES * 8 /*barriers*/;
 }
+static_assert(gv_stage(1, 7) % 1024 == 0 && gv_stage(2, 4) % 1024 == 0, "ring stages stay 1 KiB aligned");
+struct GvPlan {
+  int nrg, ks;  // 16-row groups of channels per CTA, CTAs splitting K
+};
 
 template <int WF, bool F16>
 __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o)[16]) {
@@ -1979,12 +1984,15 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int WF, bool F16, int NT>  // NT: 8-row tiles of x (1 for M <= 8, 2 for M <= 16)
-__global__ void __launch_bounds__(GV_THREADS, 2)
+// NT: 8-row tiles of x (1 for M <= 8, 2 for M <= 16); NRG: 16-row groups of channels per CTA (4: two
+// CTAs fit on an SM, 7: one)
+template <int WF, bool F16, int NT, int NRG>
+__global__ void __launch_bounds__(gv_threads(NRG), NRG == 4 ? 2 : 1)
 linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         int M, int N, int kslice, const Params p) {
   extern __shared__ uint8_t gv_raw[];
-  constexpr int XH = gv_x_half(NT), ST = gv_stage(NT);
+  constexpr int XH = gv_x_half(NT), ST = gv_stage(NT, NRG), GV_BN = gv_bn(NRG), GV_TILE = gv_tile(NRG);
+  constexpr int GV_CONSUMERS = 2 * NRG;
   const uint32_t raw_addr = smem_u32(gv_raw);
   const uint32_t ring = (raw_addr + 1023u) & ~1023u;  // GV_STAGES x [w tile | x half 0 | x half 1], 1 KiB aligned
   uint8_t *base = gv_raw + (ring - raw_addr);
@@ -2003,7 +2011,7 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
   if (threadIdx.x == 0) {
     for (int st = 0; st < GV_STAGES; st++) {
       mbar_init(full_bar(st), 1);
-      mbar_init(empty_bar(st), GV_WARPS);  // the four warps (one per row group) that read the stage
+      mbar_init(empty_bar(st), NRG);  // the warps (one per row group) that read the stage
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmap_w);
@@ -2016,7 +2024,7 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   float acc[NT][4] = {};
-  const int rg = warp & 3, par = warp >> 2;  // consumers: row group, k-block parity
+  const int rg = warp % NRG, par = warp / NRG;  // consumers: row group, k-block parity
   if (warp == GV_CONSUMERS) {
     // ---------------- producer: one lane streams the CTA's weight rows and the x rows, one k-block per stage
     if (lane == 0) {
@@ -2242,6 +2250,23 @@ int skinny_cluster_size(int dev, long long tiles, int num_kb, int smem) {
     }
   }
   return best_cs;
+}
+
+// CTA shape of the few-row kernel for an N x K weight matrix: 16 NRG channels
+// per CTA and K split over a cluster of ks CTAs. 64-channel CTAs (NRG = 4, two
+// fit on an SM) with the smallest split whose CTAs cover every SM once, except
+// where those CTAs would fill the SMs unevenly without a split (more CTAs
+// than SMs, fewer than two per SM: some SMs then hold two and set the time)
+// and 112-channel CTAs (NRG = 7) fit one per SM: then every SM converts at
+// most 7 row groups over K instead of 8 (14336 x 4096: 224 CTAs of 64 on 148
+// SMs against 128 of 112; measured 20.9 -> 19.8 us at 16 rows). Two 64-channel
+// CTAs per SM stream faster than one of either size, so other shapes keep them.
+GvPlan gv_plan(int64_t N, int64_t K, int sms) {
+  const int64_t nb4 = (N + gv_bn(4) - 1) / gv_bn(4), nb7 = (N + gv_bn(7) - 1) / gv_bn(7);
+  int ks = 1;
+  while (ks < 8 && K % (GV_BK * 2 * ks) == 0 && nb4 * ks < (int64_t)sms) ks *= 2;
+  if (ks == 1 && nb4 > sms && nb4 < 2 * (int64_t)sms && nb7 <= sms) return GvPlan{7, 1};
+  return GvPlan{4, ks};
 }
 
 }  // namespace gemm
@@ -2499,18 +2524,28 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
   }
   if (M <= 16 && K % GV_BK == 0 && K <= 0x7FFFFFFFLL - GV_BK && g_path != 3) {
     // very few rows: weights and x streamed by TMA, weights converted in registers for warp-level
-    // MMAs, K split over a cluster of ks CTAs: the smallest split whose CTAs cover every SM once
-    // (two CTAs fit on an SM, so the grid stays within about two waves), each K slice a multiple
-    // of the 128-value block
-    const int64_t nb = (N + GV_BN - 1) / GV_BN;
-    int ks = 1;
-    while (ks < 8 && K % (GV_BK * 2 * ks) == 0 && nb * ks < (int64_t)current_sm_count()) ks *= 2;
-    const int64_t kslice = K / ks;
+    // MMAs; CTAs of 64 or 112 channels, K split over a cluster of ks CTAs (gv_plan: each K slice a
+    // multiple of the 128-value block)
     const int nt = M > 8 ? 2 : 1;
-    const int64_t smem = gv_smem(nt);
+    const bool f16 = x_dtype == FP8B200_F16;
+    using GvKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, const Params);
+#define GV_K(WF, F16)                                                                                   \
+  linear_fp8w_gemv_kernel<WF, F16, 1, 4>, linear_fp8w_gemv_kernel<WF, F16, 1, 7>,                       \
+      linear_fp8w_gemv_kernel<WF, F16, 2, 4>, linear_fp8w_gemv_kernel<WF, F16, 2, 7>
+    static const GvKernel kernels[16] = {GV_K(FP8B200_E4M3, false), GV_K(FP8B200_E4M3, true),
+                                         GV_K(FP8B200_E5M2, false), GV_K(FP8B200_E5M2, true)};
+#undef GV_K
+    auto kindex = [&](int nrg) {
+      return (w_dtype == FP8B200_E4M3 ? 0 : 8) + (f16 ? 4 : 0) + (nt == 2 ? 2 : 0) + (nrg == 7 ? 1 : 0);
+    };
+    const GvPlan plan = gv_plan(N, K, current_sm_count());
+    const int nrg = plan.nrg, ks = plan.ks;
+    const int64_t nb = (N + gv_bn(nrg) - 1) / gv_bn(nrg);
+    const int64_t kslice = K / ks;
+    const int64_t smem = gv_smem(nt, nrg);
     if (nb <= 65535) {
       CUtensorMap mw, mx;
-      if (int rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, GV_BK, GV_BN,
+      if (int rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, GV_BK, (uint32_t)gv_bn(nrg),
                                CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
       // x: M rows of K 16-bit values; boxes of 64 values x 8 NT rows (rows past M read as zeros)
@@ -2527,18 +2562,11 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       p.timeout_ns = g_timeout_ns;
       p.epoch = next_epoch();
       p.debug_skip_first_load = g_debug_skip_first_load;
-      const bool f16 = x_dtype == FP8B200_F16;
-      using GvKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, const Params);
-      static const GvKernel kernels[8] = {
-          linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 1>, linear_fp8w_gemv_kernel<FP8B200_E4M3, false, 2>,
-          linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 1>,  linear_fp8w_gemv_kernel<FP8B200_E4M3, true, 2>,
-          linear_fp8w_gemv_kernel<FP8B200_E5M2, false, 1>, linear_fp8w_gemv_kernel<FP8B200_E5M2, false, 2>,
-          linear_fp8w_gemv_kernel<FP8B200_E5M2, true, 1>,  linear_fp8w_gemv_kernel<FP8B200_E5M2, true, 2>};
-      const int ki = (w_dtype == FP8B200_E4M3 ? 0 : 4) + (f16 ? 2 : 0) + (M > 8 ? 1 : 0);
+      const int ki = kindex(nrg);
       const GvKernel kern = kernels[ki];
       {  // dynamic shared-memory limit per kernel, only ever raised
         static std::mutex mu;
-        static int limit[8][64] = {};
+        static int limit[16][64] = {};
         std::lock_guard<std::mutex> lock(mu);
         if (dev < 64 && limit[ki][dev] < smem) {
           cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -2555,7 +2583,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
       attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.gridDim = dim3((unsigned)ks, (unsigned)nb, 1);
-      cfg.blockDim = dim3(GV_THREADS, 1, 1);
+      cfg.blockDim = dim3((unsigned)gv_threads(nrg), 1, 1);
       cfg.dynamicSmemBytes = (size_t)smem;
       cfg.stream = (cudaStream_t)stream;
       cfg.attrs = attr;

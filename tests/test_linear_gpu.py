@@ -300,3 +300,32 @@ def test_few_rows_bounded_wait_times_out_and_context_survives(nat):
     assert L.gemm_status() == 0
     r, S = reference(x.cpu(), w.cpu(), s.cpu())
     check(out, r, S, "after timeout")
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 9600, 256), (9, 11008, 512), (1, 14336, 128), (5, 9473, 384)])
+@pytest.mark.parametrize("wdt", [E4, E5])
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
+def test_few_rows_112_channel_ctas(nat, M, N, K, wdt, xdt):
+    """Shapes whose 64-channel CTAs would fill the SMs unevenly (more CTAs than SMs, fewer than two per
+    SM) run 112-channel CTAs, one per SM: per-channel scales, bias, a ragged last CTA (N = 9473)."""
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).to(xdt)
+    w = rand_w((N, K), wdt, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda(), bias.cuda(), out_dtype=torch.float32)
+    r, S = reference(x, w, s, bias.float())
+    check(out, r, S, f"112-channel CTAs {M}x{N}x{K} {wdt} {xdt}")
+
+
+@pytest.mark.parametrize("wdt", [E4, E5])
+def test_few_rows_112_channel_ctas_every_finite_code(nat, wdt):
+    """Every finite code in every k position of the 112-row weight tiles, picked out by one-hot rows."""
+    codes = torch.arange(256, dtype=torch.uint8)
+    finite = codes[torch.isfinite(codes.view(wdt).float())]
+    N, K = 9600, 128
+    w = finite.repeat(N * K // finite.numel() + 1)[: N * K].reshape(N, K).view(wdt)
+    eye = torch.eye(K, dtype=torch.bfloat16)
+    for k0 in range(0, K, 16):
+        out = nat.fp8_linear(eye[k0:k0 + 16].cuda(), w.cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32)
+        assert torch.equal(out.cpu(), w.float().T[k0:k0 + 16]), k0
