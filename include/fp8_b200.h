@@ -230,7 +230,7 @@ int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda,
  * per output channel (FP8B200_SCALE_ROWWISE); bias: N values or NULL.
  * The weights are converted to x's type (exact) and the products are
  * accumulated in float32 on the tensor cores; the scale and bias are applied
- * to the float32 sums. M <= 16 with K a multiple of 128: weights converted in
+ * to the float32 sums. M <= 64 with K a multiple of 128: weights converted in
  * registers for warp-level m16n8k16 MMAs, K split over a cluster; otherwise
  * converted in shared memory for tcgen05 kind::f16 MMAs.
  * Replaces the reference's dequantise-then-matmul path: fp8_scaled_mm_fast
@@ -287,7 +287,7 @@ int fp8b200_debug_gemm(int skip_first_load, unsigned long long wait_timeout_ns);
  * (tiles of 256 rows of A when M > 256), 4 = always CTA-pair 256x512 (or
  * 256x480 where the shape picks it; 256x256 when the output rows are not
  * 16-byte aligned, since the 256x512 kernel stores through a tensor map).
- * Path 3 also sends fp8b200_linear_fp8w calls with M <= 16 to its tcgen05
+ * Path 3 also sends fp8b200_linear_fp8w calls with M <= 64 to its tcgen05
  * small-M kernel instead of the warp-level MMA kernel.
  * Applies to launches from the calling host thread only; for tests and tuning.
  */

@@ -1904,13 +1904,13 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 }
 
 // ------------------------------------------------------------------ few-row float8-weight linear
-// For M <= 16 activation rows the float8-weight linear is a matrix-vector
-// product bound by the weight bytes: every weight is used by at most 16
+// For M <= 64 activation rows the float8-weight linear is bound by the
+// weight bytes and their conversion: every weight is used by at most 64
 // rows, so the tcgen05 path's shared-memory hand-off of converted weights
 // costs more than the math. This kernel converts weights in registers and
 // feeds them straight to the warp-level tensor-core instruction
 // mma.sync.m16n8k16 computing D^T = W x^T: 16 weight rows as the A operand,
-// 8 x rows as B (NT = 1 or 2 tiles, zero rows past M), float32 accumulators.
+// 8 x rows as B (NT = 1, 2, 4 or 8 tiles, zero rows past M), float32 accumulators.
 //   CTA: 16 NRG output channels (NRG = 4, or 7 where 64-channel CTAs would
 //   fill the SMs unevenly: 14336 channels are 224 CTAs of 64, two on 76 of
 //   the 148 SMs, or 128 CTAs of 112, one per SM; see gv_plan); a producer
@@ -1934,16 +1934,31 @@ int make_out_map(CUtensorMap *m, void *D, int64_t rows, int64_t cols, int64_t ld
 //   unchanged, and makes both operands' register pairs come straight from
 //   the conversions and the 16-byte loads.
 constexpr int GV_BK = 128;
-constexpr int GV_STAGES = 8;  // k-blocks in flight per CTA (TMA ring)
+// k-blocks in flight per CTA (TMA ring): fewer for 32 or 64 rows of x, whose larger x tiles would
+// otherwise keep two 64-channel CTAs off one SM (a deeper ring for the 112-channel CTAs, one per SM,
+// measured no faster: those shapes are bound by the conversion, the MMAs and the x reads)
+__host__ __device__ constexpr int gv_stages(int nt, int) { return nt <= 2 ? 8 : nt == 4 ? 6 : 4; }
 __host__ __device__ constexpr int gv_bn(int nrg) { return 16 * nrg; }          // output channels per CTA
 __host__ __device__ constexpr int gv_threads(int nrg) { return 32 * (2 * nrg + 1); }  // consumers + producer
 __host__ __device__ constexpr int gv_tile(int nrg) { return gv_bn(nrg) * GV_BK; }  // weight rows x 128 codes
 // x tile of a k-block: two 128-byte-wide boxes (values 0-63, 64-127) of 8 NT rows
 __host__ __device__ constexpr int gv_x_half(int nt) { return 8 * nt * 128; }
 __host__ __device__ constexpr int gv_stage(int nt, int nrg) { return gv_tile(nrg) + 2 * gv_x_half(nt); }
+// Partial sums [2 k-block parities][rows][channels]: beside the ring for NT <= 2 (16 rows), inside the
+// drained ring for NT > 2 (8 NT rows)
+__host__ __device__ constexpr int gv_part_rows(int nt) { return nt <= 2 ? 16 : 8 * nt; }
 __host__ __device__ constexpr int gv_smem(int nt, int nrg) {
-  return 1024 + GV_STAGES * gv_stage(nt, nrg) + 2 * 16 * gv_bn(nrg) * 4 /*partials*/ + 2 * GV_STAGES * 8 /*barriers*/;
+  return 1024 + gv_stages(nt, nrg) * gv_stage(nt, nrg) + (nt <= 2 ? 2 * 16 * gv_bn(nrg) * 4 : 0) /*partials*/ +
+         2 * gv_stages(nt, nrg) * 8 /*barriers*/;
 }
+static_assert(2 * gv_part_rows(8) * gv_bn(7) * 4 <= gv_stages(8, 7) * gv_stage(8, 7) &&
+                  2 * gv_part_rows(4) * gv_bn(7) * 4 <= gv_stages(4, 7) * gv_stage(4, 7) &&
+                  2 * gv_part_rows(8) * gv_bn(4) * 4 <= gv_stages(8, 4) * gv_stage(8, 4) &&
+                  2 * gv_part_rows(4) * gv_bn(4) * 4 <= gv_stages(4, 4) * gv_stage(4, 4),
+              "partial sums fit the drained ring");
+static_assert(gv_smem(8, 7) <= 232448 && gv_smem(4, 7) <= 232448 && 2 * (gv_smem(8, 4) + 1024) <= 233472 &&
+                  2 * (gv_smem(4, 4) + 1024) <= 233472 && 2 * (gv_smem(2, 4) + 1024) <= 233472,
+              "one 112-channel or two 64-channel CTAs per SM");
 static_assert(gv_stage(1, 7) % 1024 == 0 && gv_stage(2, 4) % 1024 == 0, "ring stages stay 1 KiB aligned");
 struct GvPlan {
   int nrg, ks;  // 16-row groups of channels per CTA, CTAs splitting K
@@ -1969,6 +1984,23 @@ __device__ __forceinline__ void gv_convert32(const uint4 (&raw)[2], uint32_t (&o
   }
 }
 
+// 16 codes (one 16-byte unit) -> 8 pairs; o[2i], o[2i+1] = codes 4i, 4i+1 and 4i+2, 4i+3.
+template <int WF, bool F16>
+__device__ __forceinline__ void gv_convert16(const uint4 &raw, uint32_t (&o)[8]) {
+  const uint32_t q[4] = {raw.x, raw.y, raw.z, raw.w};
+  if (fp8_unit_special<WF, F16>(q) == 0u) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) fp8x4_fast<WF, F16>(q[i], o[2 * i], o[2 * i + 1]);
+  } else {  // NaN / inf codes: conversion instructions
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const uint32_t lo = fp8x2_to_f16x2<WF>(q[i] & 0xFFFFu), hi = fp8x2_to_f16x2<WF>(q[i] >> 16);
+      o[2 * i] = F16 ? lo : f16x2_to_bf16x2(lo);
+      o[2 * i + 1] = F16 ? hi : f16x2_to_bf16x2(hi);
+    }
+  }
+}
+
 template <bool F16>
 __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -1984,20 +2016,20 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// NT: 8-row tiles of x (1 for M <= 8, 2 for M <= 16); NRG: 16-row groups of channels per CTA (4: two
-// CTAs fit on an SM, 7: one)
+// NT: 8-row tiles of x (1, 2, 4 or 8 for M <= 8, 16, 32, 64); NRG: 16-row groups of channels per CTA
+// (4: two CTAs fit on an SM, 7: one)
 template <int WF, bool F16, int NT, int NRG>
 __global__ void __launch_bounds__(gv_threads(NRG), NRG == 4 ? 2 : 1)
 linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         int M, int N, int kslice, const Params p) {
   extern __shared__ uint8_t gv_raw[];
   constexpr int XH = gv_x_half(NT), ST = gv_stage(NT, NRG), GV_BN = gv_bn(NRG), GV_TILE = gv_tile(NRG);
-  constexpr int GV_CONSUMERS = 2 * NRG;
+  constexpr int GV_CONSUMERS = 2 * NRG, GV_STAGES = gv_stages(NT, NRG), PROWS = gv_part_rows(NT);
   const uint32_t raw_addr = smem_u32(gv_raw);
   const uint32_t ring = (raw_addr + 1023u) & ~1023u;  // GV_STAGES x [w tile | x half 0 | x half 1], 1 KiB aligned
   uint8_t *base = gv_raw + (ring - raw_addr);
-  float *part = reinterpret_cast<float *>(base + GV_STAGES * ST);  // [2][16][GV_BN]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(part + 2 * 16 * GV_BN);
+  float *part = reinterpret_cast<float *>(NT <= 2 ? base + GV_STAGES * ST : base);  // [2][PROWS][GV_BN]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + GV_STAGES * ST + (NT <= 2 ? 2 * 16 * GV_BN * 4 : 0));
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int st) { return bar0 + 8u * st; };
   auto empty_bar = [&](int st) { return bar0 + 8u * (GV_STAGES + st); };
@@ -2065,36 +2097,74 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
           asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                        : "=r"(raw[h][c].x), "=r"(raw[h][c].y), "=r"(raw[h][c].z), "=r"(raw[h][c].w)
                        : "r"(tile + row_off[h] + unit_off[c]));
-      uint32_t wv[2][16];  // weight rows g and g + 8 converted: the A operand pairs
-      gv_convert32<WF, F16>(raw[0], wv[0]);
-      gv_convert32<WF, F16>(raw[1], wv[1]);
-      uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
-#pragma unroll
-      for (int u = 0; u < NT; u++)
-#pragma unroll
-        for (int v = 0; v < 4; v++)
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(xv[u][4 * v]), "=r"(xv[u][4 * v + 1]), "=r"(xv[u][4 * v + 2]), "=r"(xv[u][4 * v + 3])
-                       : "r"(tile + x_off + (uint32_t)(u * 1024) + (uint32_t)(((4 * (t & 1) + v) ^ g) * 16)));
-      // the stage's bytes are now in registers (the conversions consumed the weights, the MMAs below
-      // read only registers): only then may the producer's next TMA overwrite it; order these reads
-      // before that async-proxy write
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(st));  // this warp is done with the stage
-#pragma unroll
-      for (int j = 0; j < 8; j++)
+      if constexpr (NT <= 2) {
+        uint32_t wv[2][16];  // weight rows g and g + 8 converted: the A operand pairs
+        gv_convert32<WF, F16>(raw[0], wv[0]);
+        gv_convert32<WF, F16>(raw[1], wv[1]);
+        uint32_t xv[NT][16];  // x rows g (+ 8): 32 values each, the B operand pairs
 #pragma unroll
         for (int u = 0; u < NT; u++)
-          mma_16816<F16>(acc[u], wv[0][2 * j], wv[1][2 * j], wv[0][2 * j + 1], wv[1][2 * j + 1], xv[u][2 * j],
-                         xv[u][2 * j + 1]);
+#pragma unroll
+          for (int v = 0; v < 4; v++)
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(xv[u][4 * v]), "=r"(xv[u][4 * v + 1]), "=r"(xv[u][4 * v + 2]), "=r"(xv[u][4 * v + 3])
+                         : "r"(tile + x_off + (uint32_t)(u * 1024) + (uint32_t)(((4 * (t & 1) + v) ^ g) * 16)));
+        // the stage's bytes are now in registers (the conversions consumed the weights, the MMAs below
+        // read only registers): only then may the producer's next TMA overwrite it; order these reads
+        // before that async-proxy write
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(st));  // this warp is done with the stage
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+          for (int u = 0; u < NT; u++)
+            mma_16816<F16>(acc[u], wv[0][2 * j], wv[1][2 * j], wv[0][2 * j + 1], wv[1][2 * j + 1], xv[u][2 * j],
+                           xv[u][2 * j + 1]);
+      } else {
+        // 32 or 64 x rows: the weights converted 16 codes at a time (k-steps 4 hk .. 4 hk + 3), x read
+        // one 16-byte unit per row tile at a time (k-steps 4 hk + 2 kp, + 1), so that the registers
+        // hold one unit of every x tile instead of the whole block
+#pragma unroll
+        for (int hk = 0; hk < 2; hk++) {
+          uint32_t wv[2][8];  // weight rows g and g + 8, codes 16 hk .. 16 hk + 15 of the lane
+          gv_convert16<WF, F16>(raw[0][hk], wv[0]);
+          gv_convert16<WF, F16>(raw[1][hk], wv[1]);
+#pragma unroll
+          for (int kp = 0; kp < 2; kp++) {
+            uint32_t xq[NT][4];  // x rows 8u + g: values 16 (2 hk + kp) .. + 7 of the lane's 32
+#pragma unroll
+            for (int u = 0; u < NT; u++)
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(xq[u][0]), "=r"(xq[u][1]), "=r"(xq[u][2]), "=r"(xq[u][3])
+                           : "r"(tile + x_off + (uint32_t)(u * 1024) +
+                                 (uint32_t)(((4 * (t & 1) + 2 * hk + kp) ^ g) * 16)));
+            if (hk == 1 && kp == 1) {
+              // every read of the stage is issued: order them before the producer's next (async-proxy)
+              // write into the stage, then count this warp out of it
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              __syncwarp();
+              if (lane == 0) mbar_arrive(empty_bar(st));
+            }
+#pragma unroll
+            for (int k2 = 0; k2 < 2; k2++)
+#pragma unroll
+              for (int u = 0; u < NT; u++) {
+                const int i = 2 * kp + k2;
+                mma_16816<F16>(acc[u], wv[0][2 * i], wv[1][2 * i], wv[0][2 * i + 1], wv[1][2 * i + 1],
+                               xq[u][2 * k2], xq[u][2 * k2 + 1]);
+              }
+          }
+        }
+      }
     }
   }
 
+  if constexpr (NT > 2) __syncthreads();  // the ring is drained: the partial sums reuse it
   if (warp < GV_CONSUMERS) {
     // partial sums part[par][x row][channel] (rows < 8 NT, all written): acc[u] = D^T rows
     // (channels) g / g + 8, columns (x rows) 8u + 2t (+1)
-    float *pp = part + par * 16 * GV_BN;
+    float *pp = part + par * PROWS * GV_BN;
 #pragma unroll
     for (int u = 0; u < NT; u++) {
       const int ch = 16 * rg + g, xrow = 8 * u + 2 * t;
@@ -2106,7 +2176,7 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
   }
   __syncthreads();
   // the two parities' sums, in a fixed order, into part[0]
-  for (int i = threadIdx.x; i < 8 * NT * GV_BN; i += blockDim.x) part[i] += part[16 * GV_BN + i];
+  for (int i = threadIdx.x; i < 8 * NT * GV_BN; i += blockDim.x) part[i] += part[PROWS * GV_BN + i];
   __syncwarp();
   cluster_sync();  // every CTA's partial sums are complete
   // this CTA reduces and stores columns [rank * cw, (rank + 1) * cw) of the 64
@@ -2522,21 +2592,22 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
     attr_done[dev] = true;
   }
-  if (M <= 16 && K % GV_BK == 0 && K <= 0x7FFFFFFFLL - GV_BK && g_path != 3) {
+  if (M <= 64 && K % GV_BK == 0 && K <= 0x7FFFFFFFLL - GV_BK && g_path != 3) {
     // very few rows: weights and x streamed by TMA, weights converted in registers for warp-level
     // MMAs; CTAs of 64 or 112 channels, K split over a cluster of ks CTAs (gv_plan: each K slice a
     // multiple of the 128-value block)
-    const int nt = M > 8 ? 2 : 1;
+    const int nt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;  // 8-row tiles of x
     const bool f16 = x_dtype == FP8B200_F16;
     using GvKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, const Params);
-#define GV_K(WF, F16)                                                                                   \
-  linear_fp8w_gemv_kernel<WF, F16, 1, 4>, linear_fp8w_gemv_kernel<WF, F16, 1, 7>,                       \
-      linear_fp8w_gemv_kernel<WF, F16, 2, 4>, linear_fp8w_gemv_kernel<WF, F16, 2, 7>
-    static const GvKernel kernels[16] = {GV_K(FP8B200_E4M3, false), GV_K(FP8B200_E4M3, true),
-                                         GV_K(FP8B200_E5M2, false), GV_K(FP8B200_E5M2, true)};
+#define GV_K(WF, F16, NT) linear_fp8w_gemv_kernel<WF, F16, NT, 4>, linear_fp8w_gemv_kernel<WF, F16, NT, 7>
+#define GV_K4(WF, F16) GV_K(WF, F16, 1), GV_K(WF, F16, 2), GV_K(WF, F16, 4), GV_K(WF, F16, 8)
+    static const GvKernel kernels[32] = {GV_K4(FP8B200_E4M3, false), GV_K4(FP8B200_E4M3, true),
+                                         GV_K4(FP8B200_E5M2, false), GV_K4(FP8B200_E5M2, true)};
+#undef GV_K4
 #undef GV_K
     auto kindex = [&](int nrg) {
-      return (w_dtype == FP8B200_E4M3 ? 0 : 8) + (f16 ? 4 : 0) + (nt == 2 ? 2 : 0) + (nrg == 7 ? 1 : 0);
+      const int nti = nt == 1 ? 0 : nt == 2 ? 1 : nt == 4 ? 2 : 3;
+      return (w_dtype == FP8B200_E4M3 ? 0 : 16) + (f16 ? 8 : 0) + 2 * nti + (nrg == 7 ? 1 : 0);
     };
     const GvPlan plan = gv_plan(N, K, current_sm_count());
     const int nrg = plan.nrg, ks = plan.ks;
@@ -2566,7 +2637,7 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
       const GvKernel kern = kernels[ki];
       {  // dynamic shared-memory limit per kernel, only ever raised
         static std::mutex mu;
-        static int limit[16][64] = {};
+        static int limit[32][64] = {};
         std::lock_guard<std::mutex> lock(mu);
         if (dev < 64 && limit[ki][dev] < smem) {
           cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

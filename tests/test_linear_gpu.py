@@ -329,3 +329,60 @@ def test_few_rows_112_channel_ctas_every_finite_code(nat, wdt):
     for k0 in range(0, K, 16):
         out = nat.fp8_linear(eye[k0:k0 + 16].cuda(), w.cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32)
         assert torch.equal(out.cpu(), w.float().T[k0:k0 + 16]), k0
+
+
+# ---------------------------------------------------------------- 16 < M <= 64, K % 128 == 0: four or eight 8-row x tiles
+@pytest.mark.parametrize("M,N,K", [(17, 1000, 1408), (32, 14336, 4096), (33, 4096, 256), (48, 300, 256),
+                                   (64, 4096, 4096), (64, 9600, 512), (40, 65, 2048), (24, 4096, 14336)])
+def test_few_rows_up_to_64_shapes(nat, M, N, K):
+    g = torch.Generator().manual_seed(M * 5 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = rand_w((N, K), E4, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    r, S = reference(x, w, s)
+    check(out, r, S, f"up to 64 rows {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("M", [29, 64])
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("wdt", [E4, E5])
+@pytest.mark.parametrize("odt", [torch.float32, torch.bfloat16])
+def test_few_rows_up_to_64_dtypes_scales_bias(nat, M, xdt, wdt, odt):
+    N, K = 392, 640
+    g = torch.Generator().manual_seed(13 + M)
+    x = (torch.randn(M, K, generator=g) * 2).to(xdt)
+    w = rand_w((N, K), wdt, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    bias = (torch.randn(N, generator=g) * 5).to(torch.float16)
+    out = nat.fp8_linear(x.cuda(), w.cuda(), s.cuda(), bias.cuda(), out_dtype=odt)
+    r, S = reference(x, w, s, bias)
+    check(out, r, S, f"up to 64 rows {M} {xdt} {wdt} {odt}")
+
+
+@pytest.mark.parametrize("wdt", [E4, E5])
+@pytest.mark.parametrize("rows", [32, 64])
+def test_few_rows_up_to_64_every_finite_weight_code(nat, wdt, rows):
+    """Every finite code in every k position, picked out by `rows` one-hot x rows at a time."""
+    codes = torch.arange(256, dtype=torch.uint8)
+    finite = codes[torch.isfinite(codes.view(wdt).float())]
+    K = 128
+    w = finite.repeat(256 * K // finite.numel() + 1)[: 256 * K].reshape(256, K).view(wdt)
+    eye = torch.eye(K, dtype=torch.bfloat16)
+    for k0 in range(0, K, rows):
+        out = nat.fp8_linear(eye[k0:k0 + rows].cuda(), w.cuda(), torch.tensor(1.0).cuda(), out_dtype=torch.float32)
+        assert torch.equal(out.cpu(), w.float().T[k0:k0 + rows]), k0
+
+
+def test_few_rows_64_repeated_calls_are_stable(nat):
+    g = torch.Generator().manual_seed(8)
+    M, N, K = 64, 14336, 4096
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = rand_w((N, K), E4, g)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-3
+    r, S = reference(x, w, s)
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    outs = [nat.fp8_linear(xd, wd, sd) for _ in range(8)]
+    for i, o in enumerate(outs):
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16)), i
+    check(outs[0], r, S, "repeated 64-row calls")
