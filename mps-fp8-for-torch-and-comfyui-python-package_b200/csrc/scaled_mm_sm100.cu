@@ -2224,10 +2224,10 @@ uint32_t next_epoch() {
 // Resident 2-CTA clusters of the pair kernel (wide = false) or the wide
 // kernel (wide = true) on device `dev`.
 int pair_clusters(int dev, bool wide) {
-  static int cached[2][64] = {};
+  static std::atomic<int> cached[2][64];  // 0 = not yet queried; concurrent first calls store the same value
   if (dev < 0 || dev >= 64) return 1;
-  int &c = cached[wide ? 1 : 0][dev];
-  if (!c) {
+  std::atomic<int> &c = cached[wide ? 1 : 0][dev];
+  if (!c.load(std::memory_order_acquire)) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74, 1, 1);
     cfg.blockDim = dim3(wide ? W_THREADS : THREADS, 1, 1);
@@ -2236,9 +2236,9 @@ int pair_clusters(int dev, bool wide) {
     const cudaError_t e = wide ? cudaOccupancyMaxActiveClusters(&n, scaled_mm_wide_kernel<0>, &cfg)
                                : cudaOccupancyMaxActiveClusters(&n, scaled_mm_pair_kernel, &cfg);
     if (e != cudaSuccess || n < 1) n = current_sm_count() / 2;
-    c = n;
+    c.store(n, std::memory_order_release);
   }
-  return c;
+  return c.load(std::memory_order_acquire);
 }
 
 // Tile width of the wide kernel: 512 columns, or 480 (second MMA N = 224)
@@ -2381,8 +2381,8 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     return set_error(FP8B200_EINVAL, "scaled_mm: bias must be f32/bf16/f16");
   int dev;
   if (int rc = check_device(&dev)) return rc;
-  static bool attr_done[64] = {};
-  if (dev < 64 && !attr_done[dev]) {
+  static std::atomic<bool> attr_done[64];  // set-once flags; concurrent first calls both set the attribute
+  if (dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(scaled_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
@@ -2393,7 +2393,7 @@ extern "C" int fp8b200_scaled_mm(const void *A, int a_dtype, int64_t lda, const 
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(scaled_mm_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, W_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "scaled_mm: smem attribute: %s", cudaGetErrorString(e));
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
 
   const bool skinny = g_path == 3 || (g_path == 0 && M <= SK_MAX_MT);
@@ -2586,11 +2586,11 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
     return set_error(FP8B200_EINVAL, "linear_fp8w: bias must be f32/bf16/f16");
   int dev;
   if (int rc = check_device(&dev)) return rc;
-  static bool attr_done[64] = {};
-  if (dev < 64 && !attr_done[dev]) {
+  static std::atomic<bool> attr_done[64];  // set-once flags; concurrent first calls both set the attribute
+  if (dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(linear_fp8w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LW_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   if (M <= 64 && K % GV_BK == 0 && K <= 0x7FFFFFFFLL - GV_BK && g_path != 3) {
     // very few rows: weights and x streamed by TMA, weights converted in registers for warp-level
@@ -2672,12 +2672,12 @@ extern "C" int fp8b200_linear_fp8w(const void *x, int x_dtype, int64_t ldx, cons
   if (M <= SK_MAX_MT && !pair_mid) {
     // few rows: the small-M kernel with weights dequantised on load (128
     // weight rows per tile on the MMA's M, K split over a cluster)
-    static bool sk_attr[64] = {};
-    if (dev < 64 && !sk_attr[dev]) {
+    static std::atomic<bool> sk_attr[64];
+    if (dev < 64 && !sk_attr[dev].load(std::memory_order_acquire)) {
       cudaError_t e = cudaFuncSetAttribute(scaled_mm_skinny_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            SK_SMEM_MAX);
       if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "linear_fp8w: smem attribute: %s", cudaGetErrorString(e));
-      sk_attr[dev] = true;
+      sk_attr[dev].store(true, std::memory_order_release);
     }
     const int mt = (int)((M + 15) / 16 * 16);
     CUtensorMap mx, mw;
@@ -2793,12 +2793,12 @@ extern "C" int fp8b200_gemm_16bit(const void *A, const void *B, int dtype, int64
     return set_error(FP8B200_EINVAL, "gemm_16bit: bias must be f32/bf16/f16");
   int dev;
   if (int rc = check_device(&dev)) return rc;
-  static bool attr_done[64] = {};
-  if (dev < 64 && !attr_done[dev]) {
+  static std::atomic<bool> attr_done[64];  // set-once flags; concurrent first calls both set the attribute
+  if (dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(scaled_mm_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          W_SMEM_BYTES);
     if (e != cudaSuccess) return set_error(FP8B200_ELAUNCH, "gemm_16bit: smem attribute: %s", cudaGetErrorString(e));
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   CUtensorMap ma, mb, md;
   if (int rc = make_map_2d(&ma, A, CU_TENSOR_MAP_DATA_TYPE_UINT16, K, M, lda * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B))
