@@ -202,6 +202,15 @@ __device__ int g_bulk_status;
 // attribute.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Bring `bytes` of global memory at `src` into L2 ahead of their bulk load. Issued before
+// pdl_wait_prior by the bulk converters: a prefetch writes nothing, and L2 is where global
+// memory is coherent, so a line it fetches before the previous kernel's writes land is
+// updated by those writes, and the bulk loads after the wait read current data. It takes
+// the DRAM latency of a launch's first chunks off the time after the wait (~1.4 us of a
+// ~16 us 4096^2 decode).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 template <int KIND>
 __global__ void __launch_bounds__(kDecThreads)
@@ -218,9 +227,13 @@ decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < kStages; i++) {
+      const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
+      if (c < nch) bulk_prefetch_l2(src + c * C::kIn, C::kIn);
+    }
   }
   pdl_launch_dependents();
-  pdl_wait_prior();  // nothing in global memory is read or written before this
+  pdl_wait_prior();  // nothing in global memory is read or written before this (the L2 prefetch above excepted)
   const float s = load_scale(scale, mode);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
@@ -593,9 +606,13 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < kStages; i++) {
+      const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
+      if (c < nch) bulk_prefetch_l2(src + at(c) * C::kIn, C::kIn);
+    }
   }
   pdl_launch_dependents();
-  pdl_wait_prior();  // nothing in global memory is read or written before this
+  pdl_wait_prior();  // nothing in global memory is read or written before this (the L2 prefetch above excepted)
   const bool scaled = scale != nullptr || amax_bits != nullptr;
   const float s = amax_bits ? scale_from_amax(amax_bits, fmax, scale_out) : scale ? __ldg(scale) : 1.0f;
   if (threadIdx.x == 0) {
@@ -777,9 +794,13 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < kStages; i++) {
+      const int64_t c = blockIdx.x + (int64_t)i * gridDim.x;
+      if (c < nch) bulk_prefetch_l2(src + at(c) * C::kIn, C::kIn);
+    }
   }
   pdl_launch_dependents();
-  pdl_wait_prior();  // nothing in global memory is read or written before this
+  pdl_wait_prior();  // nothing in global memory is read or written before this (the L2 prefetch above excepted)
   const bool scaled = scale != nullptr || amax_bits != nullptr;
   const float s = amax_bits ? scale_from_amax(amax_bits, fmax, scale_out) : scale ? __ldg(scale) : 1.0f;
   if (threadIdx.x == 0) {
