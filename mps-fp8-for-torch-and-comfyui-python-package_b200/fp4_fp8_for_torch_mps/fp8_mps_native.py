@@ -295,9 +295,30 @@ def fp4_quantize(input):
 
 
 # ----------------------------------------------------------------- scaled GEMM
-# Rows of x from which fp8_linear decodes the weights once and runs the 16-bit
-# GEMM instead of dequantising them on load inside the GEMM.
-LINEAR_DECODE_ONCE_M = 1024
+# Above LINEAR_DECODE_ONCE_MIN_M - 1 rows of x, fp8_linear decodes the weights
+# once and runs the 16-bit GEMM instead of dequantising them on load inside the
+# GEMM whenever the dequant-on-load kernel's 256 x 256 output tiles outnumber
+# the device's CTA pairs (one pair per two SMs): that kernel is bound by each
+# SM's TMA intake, so a second wave of its tiles costs more than one pass over
+# the weights in a wider type. Measured on one B200 (us, dequant-on-load /
+# decode once): 384 x 14336 x 4096 93.9 / 77.6 (112 tiles), 1024 x 6144 x 4096
+# 93.9 / 60.2 (96 tiles); 1024 x 4096 x 4096 50.2 / 55.3 (64 tiles),
+# 768 x 6144 x 4096 51.3 / 59.4 (72 tiles).
+LINEAR_DECODE_ONCE_MIN_M = 257
+_SM_COUNT: dict[int, int] = {}
+
+
+def linear_decodes_once(M: int, N: int, device: torch.device) -> bool:
+    """Whether fp8_linear takes the decode-once path for M rows of x and N
+    output channels on `device` (see LINEAR_DECODE_ONCE_MIN_M)."""
+    if M < LINEAR_DECODE_ONCE_MIN_M:
+        return False
+    idx = torch.device(device).index
+    idx = torch.cuda.current_device() if idx is None else idx
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    tiles = -(-M // 256) * -(-N // 256)
+    return tiles > _SM_COUNT[idx] // 2
 
 
 def gemm_16bit(a: torch.Tensor, b_nk: torch.Tensor, scale_b: torch.Tensor, bias: torch.Tensor | None = None,
@@ -382,9 +403,9 @@ def fp8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor
             raise RuntimeError("fp8_linear: bias must hold N float values")
     M = x2.shape[0]
     out = torch.empty((M, N), dtype=odt, device=dev)
-    if M >= LINEAR_DECODE_ONCE_M and (N * out.element_size()) % 16 == 0:
-        # many rows: decode the weights once (exact; N*K values against M*N*K
-        # products) and run the 16-bit CTA-pair GEMM with the scale in its epilogue
+    if (N * out.element_size()) % 16 == 0 and linear_decodes_once(M, N, dev):
+        # more output tiles than CTA pairs: decode the weights once (exact; N*K values against
+        # M*N*K products) and run the 16-bit CTA-pair GEMM with the scale in its epilogue
         wd = decode_fp8(w.view(torch.uint8), weight.dtype, x.dtype)
         with torch.cuda.device(dev):
             L.check(L.lib().fp8b200_gemm_16bit(

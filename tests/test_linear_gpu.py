@@ -155,12 +155,15 @@ def test_mid_rows_wide_output(nat, M, N, K, wdt):
 
 
 # ---------------------------------------------------------------- many rows: decode once + 16-bit GEMM
-@pytest.mark.parametrize("M,N,K", [(1024, 512, 256), (2048, 1024, 512), (1500, 776, 333), (1100, 100, 64)])
+@pytest.mark.parametrize("M,N,K,once", [(1024, 6144, 256, True), (2048, 4864, 512, True), (1500, 5000, 333, True),
+                                        (300, 14336, 192, True), (1024, 512, 256, False), (1100, 100, 64, False),
+                                        (1500, 776, 333, False)])
 @pytest.mark.parametrize("wdt", [E4, E5])
-def test_many_rows_path(nat, M, N, K, wdt):
-    """M >= LINEAR_DECODE_ONCE_M: weights decoded once, 16-bit CTA-pair GEMM
-    (N = 100: output rows not 16-byte aligned, dequant-on-load kernel)."""
-    assert M >= nat.LINEAR_DECODE_ONCE_M
+def test_many_rows_path(nat, M, N, K, once, wdt):
+    """More than 256 rows: weights decoded once and the 16-bit CTA-pair GEMM when the
+    dequant-on-load kernel's 256 x 256 tiles outnumber the CTA pairs, else that kernel
+    (N = 100: output rows not 16-byte aligned, dequant-on-load kernel at any size)."""
+    assert nat.linear_decodes_once(M, N, torch.device("cuda")) == once
     g = torch.Generator().manual_seed(M + K)
     x = torch.randn(M, K, generator=g).to(torch.bfloat16)
     w = rand_w((N, K), wdt, g)
