@@ -113,10 +113,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait on phase `parity` of `bar`; false on timeout or if another
-// role already recorded a failure.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long timeout_ns, uint32_t epoch,
-                                       uint32_t site) {
-  if (mbar_try_wait(bar, parity)) return true;
+// role already recorded a failure. The first test is inlined at every call
+// site: a wait whose phase has already completed (the common case in a
+// pipeline that keeps up) costs one try_wait, not a function call; the
+// timed loop is out of line.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, unsigned long long timeout_ns, uint32_t epoch,
+                                            uint32_t site) {
   const uint64_t t0 = globaltimer();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -135,6 +137,11 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned l
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long timeout_ns, uint32_t epoch,
+                                          uint32_t site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, timeout_ns, epoch, site);
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
   asm volatile(
