@@ -193,6 +193,17 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
 // global->shared copies, complete in microseconds).
 constexpr long long kBulkSpinLimit = 1ll << 24;
 __device__ int g_bulk_status;
+// After a timed-out wait a CTA stops early, while bulk loads it issued for
+// later chunks may still be landing in its shared memory: its thread 0 holds
+// the CTA (and so its shared memory) for a bounded 200 us before it exits.
+__device__ __forceinline__ void drain_loads() {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  do {
+    __nanosleep(1000);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  } while (t - t0 < 200000ull);
+}
 
 // Programmatic dependent launch: the bulk converters let the next kernel in
 // the stream launch as soon as every CTA of this one has started, and wait
@@ -250,6 +261,7 @@ decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
   }
   const uint32_t *tab = lut + (threadIdx.x & 31u);
 
+  bool failed = false;
   for (int64_t i = 0;; i++) {
     const int64_t c = blockIdx.x + i * gridDim.x;
     if (c >= nch) break;
@@ -260,6 +272,7 @@ decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
       if (++n > kBulkSpinLimit) { timed_out = 1; break; }
     if (__syncthreads_or(timed_out)) {  // block-uniform exit; the host sees the status word
       if (threadIdx.x == 0) atomicExch(&g_bulk_status, 1);
+      failed = true;
       break;
     }
     // the store issued kStages chunks ago must have finished reading out[st]
@@ -281,6 +294,7 @@ decode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
     }
   }
   if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (failed && threadIdx.x == 0) drain_loads();  // loads issued before the timeout may still be landing
 
   // ragged tail (fewer than kIn input bytes), element-wise through the table
   if (blockIdx.x == gridDim.x - 1) {
@@ -622,6 +636,7 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
     }
   }
   __syncthreads();
+  bool failed = false;
   for (int64_t i = 0;; i++) {
     const int64_t c = blockIdx.x + i * gridDim.x;
     if (c >= nch) break;
@@ -632,6 +647,7 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
       if (++k > kBulkSpinLimit) { timed_out = 1; break; }
     if (__syncthreads_or(timed_out)) {
       if (threadIdx.x == 0) atomicExch(&g_bulk_status, 1);
+      failed = true;
       break;
     }
     if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStages - 1) : "memory");
@@ -655,6 +671,7 @@ encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, i
     }
   }
   if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (failed && threadIdx.x == 0) drain_loads();  // loads issued before the timeout may still be landing
   if (blockIdx.x == gridDim.x - 1)
     for (int64_t e = nch * kEncElems + threadIdx.x; e < n; e += kDecThreads)
       dst[e] = (uint8_t)encode_one<SRC, FMT>(load_raw<SRC>(src, e), scaled, s);
@@ -810,6 +827,7 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
     }
   }
   __syncthreads();
+  bool failed = false;
   for (int64_t i = 0;; i++) {
     const int64_t c = blockIdx.x + i * gridDim.x;
     if (c >= nch) break;
@@ -820,6 +838,7 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
       if (++k > kBulkSpinLimit) { timed_out = 1; break; }
     if (__syncthreads_or(timed_out)) {
       if (threadIdx.x == 0) atomicExch(&g_bulk_status, 1);
+      failed = true;
       break;
     }
     if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStages - 1) : "memory");
@@ -868,6 +887,7 @@ fp4_encode_bulk_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ ds
     }
   }
   if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (failed && threadIdx.x == 0) drain_loads();  // loads issued before the timeout may still be landing
   if (blockIdx.x == gridDim.x - 1)
     for (int64_t p = nch * (kEncElems / 2) + threadIdx.x; p < n / 2; p += kDecThreads) {
       float lo = load_elem<SRC>(src, 2 * p), hi = load_elem<SRC>(src, 2 * p + 1);

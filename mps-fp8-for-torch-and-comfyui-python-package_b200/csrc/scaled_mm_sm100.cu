@@ -112,6 +112,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// A role that gives up leaves its loop while copies and MMAs it or its CTA
+// issued earlier may still be landing in the CTA's shared and tensor memory;
+// the thread then holds the CTA (and so that memory) for a bounded 200 us
+// before the caller goes on to the kernel's teardown.
+__device__ __noinline__ void hold_after_failure() {
+  const uint64_t t0 = globaltimer();
+  while (globaltimer() - t0 < 200000ull) __nanosleep(1000);
+}
 // Bounded wait on phase `parity` of `bar`; false on timeout or if another
 // role already recorded a failure. The first test is inlined at every call
 // site: a wait whose phase has already completed (the common case in a
@@ -124,7 +132,10 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, unsig
     if (mbar_try_wait(bar, parity)) return true;
     if ((n & 31u) == 0) {
       unsigned long long s = *reinterpret_cast<volatile unsigned long long *>(&g_status);
-      if ((uint32_t)(s >> 32) == epoch) return false;  // another role of this launch gave up
+      if ((uint32_t)(s >> 32) == epoch) {  // another role of this launch gave up
+        hold_after_failure();
+        return false;
+      }
       if (globaltimer() - t0 > timeout_ns) {
         // record the first failure of this launch, replacing an older launch's record
         const unsigned long long mine = ((unsigned long long)epoch << 32) | 0x80000000ull | site;
@@ -133,6 +144,7 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, unsig
           if (prev == s) break;
           s = prev;
         }
+        hold_after_failure();
         return false;
       }
     }
