@@ -1651,12 +1651,11 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
   const uint32_t bar_base = smem_u32(bars);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };                                // x of both CTAs (leader)
   auto empty_bar = [&](int s) { return bar_base + 8u * (LW_LOADS + s); };                  // x slot read
-  auto conv_bar = [&](int c) { return bar_base + 8u * (2 * LW_LOADS + c); };               // both halves converted (leader)
-  auto cempty_bar = [&](int c) { return bar_base + 8u * (2 * LW_LOADS + LW_CONVS + c); };  // converted slot read
-  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * LW_LOADS + 2 * LW_CONVS + b); };
-  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * LW_LOADS + 2 * LW_CONVS + 2 + b); };
-  auto rfull_bar = [&](int s) { return bar_base + 8u * (2 * LW_LOADS + 2 * LW_CONVS + 4 + s); };  // raw weights (own)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * LW_LOADS + 2 * LW_CONVS + 4);
+  auto conv_bar = [&](int c) { return bar_base + 8u * (2 * LW_LOADS + c); };  // both halves converted (leader)
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * LW_LOADS + LW_CONVS + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * LW_LOADS + LW_CONVS + 2 + b); };
+  auto rfull_bar = [&](int s) { return bar_base + 8u * (2 * LW_LOADS + LW_CONVS + 4 + s); };  // raw weights (own)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * LW_LOADS + LW_CONVS + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1670,10 +1669,7 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
       mbar_init(empty_bar(s), 1);
       mbar_init(rfull_bar(s), 1);
     }
-    for (int c = 0; c < LW_CONVS; c++) {
-      mbar_init(conv_bar(c), 2 * LW_CONV_WARPS / LW_GROUPS);  // the warps of one group in each CTA
-      mbar_init(cempty_bar(c), 1);
-    }
+    for (int c = 0; c < LW_CONVS; c++) mbar_init(conv_bar(c), 2 * LW_CONV_WARPS / LW_GROUPS);  // a group's warps, both CTAs
     for (int b = 0; b < 2; b++) {
       mbar_init(tfull_bar(b), 1);
       mbar_init(tempty_bar(b), 8);  // four epilogue warps in each CTA
@@ -1738,8 +1734,8 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
           for (int k = 0; k < LW_BK / 16; k++)  // K = 16 per MMA: +32 bytes along the swizzled row
             umma_f16_pair(d_tmem, adesc + (uint64_t)((k * 32) >> 4), bdesc + (uint64_t)((k * 32) >> 4), p.idesc,
                           (kb > 0 || k > 0) ? 1u : 0u);
-          umma_commit_pair(empty_bar(stage));  // x slot free in both CTAs
-          umma_commit_pair(cempty_bar(cs));    // converted slot free in both CTAs
+          // x slot free in both CTAs; the converters also take this commit as "converted slot cs free"
+          umma_commit_pair(empty_bar(stage));
           if (++stage == LW_LOADS) { stage = 0; phase ^= 1u; }
           if (++cs == LW_CONVS) { cs = 0; cphase ^= 1u; }
         }
@@ -1763,11 +1759,18 @@ linear_fp8w_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_cons
       for (int kb = 0; kb < p.num_kb; kb++, it++) {
         if ((int)(it % LW_GROUPS) != group) continue;
         const int stage = (int)(it % LW_LOADS), cs = (int)(it % LW_CONVS);
-        const uint32_t phase = (it / LW_LOADS) & 1u, cphase = (it / LW_CONVS) & 1u;
+        const uint32_t phase = (it / LW_LOADS) & 1u;
         int got = 0;
-        if (lane == 0)
-          got = mbar_wait(rfull_bar(stage), phase, p.timeout_ns, p.epoch, 5) && mbar_wait(cempty_bar(cs), cphase ^ 1u, p.timeout_ns, p.epoch, 6)
-                    ? 1 : 0;
+        if (lane == 0) {
+          got = mbar_wait(rfull_bar(stage), phase, p.timeout_ns, p.epoch, 5) ? 1 : 0;
+          // converted slot cs was last read by the MMAs of k-block it - LW_CONVS, whose commit completes phase
+          // (it - LW_CONVS) / LW_LOADS of x slot (it - LW_CONVS) % LW_LOADS (this group's previous k-block
+          // waited for a later commit, so the phase before that one has completed: no early parity match)
+          if (got && it >= (uint32_t)LW_CONVS) {
+            const uint32_t prev = it - (uint32_t)LW_CONVS;
+            got = mbar_wait(empty_bar((int)(prev % LW_LOADS)), (prev / LW_LOADS) & 1u, p.timeout_ns, p.epoch, 6) ? 1 : 0;
+          }
+        }
         got = __shfl_sync(0xFFFFFFFFu, got, 0);
         if (!got) { ok = false; break; }
 #pragma unroll
