@@ -2132,9 +2132,9 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
                          : "=r"(xv[u][4 * v]), "=r"(xv[u][4 * v + 1]), "=r"(xv[u][4 * v + 2]), "=r"(xv[u][4 * v + 3])
                          : "r"(tile + x_off + (uint32_t)(u * 1024) + (uint32_t)(((4 * (t & 1) + v) ^ g) * 16)));
         // the stage's bytes are now in registers (the conversions consumed the weights, the MMAs below
-        // read only registers): only then may the producer's next TMA overwrite it; order these reads
-        // before that async-proxy write
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        // read only registers): only then may the producer's next TMA overwrite it. The arrival's
+        // release, which the producer acquires before it issues that TMA, orders these completed reads
+        // before the write (a buffer that is only read needs no proxy fence before its release)
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(st));  // this warp is done with the stage
 #pragma unroll
@@ -2162,9 +2162,9 @@ linear_fp8w_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid
                            : "r"(tile + x_off + (uint32_t)(u * 1024) +
                                  (uint32_t)(((4 * (t & 1) + 2 * hk + kp) ^ g) * 16)));
             if (hk == 1 && kp == 1) {
-              // every read of the stage is issued: order them before the producer's next (async-proxy)
-              // write into the stage, then count this warp out of it
-              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              // every read of the stage has returned its value (the conversion and these loads' values are
+              // used below only from registers): count this warp out of the stage; the arrival's release
+              // orders the reads before the producer's next TMA write into it
               __syncwarp();
               if (lane == 0) mbar_arrive(empty_bar(st));
             }
