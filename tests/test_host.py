@@ -252,3 +252,21 @@ def test_scaled_mm_argument_checks_reject(case):
     }
     with pytest.raises(RuntimeError, match=_REJECT_WHY[case]):
         check_scaled_mm_args(*args[case])
+
+
+@pytest.mark.parametrize("M,N,want", [
+    (256, 14336, False),    # at most 256 rows: never decoded once
+    (257, 14336, True),     # 2 x 56 = 112 tiles of 256 x 256 > 74 CTA pairs
+    (320, 14336, True),
+    (1024, 4096, False),    # 4 x 16 = 64 tiles: one wave of the dequant-on-load kernel
+    (768, 6144, False),     # 3 x 24 = 72 tiles
+    (1024, 6144, True),     # 4 x 24 = 96 tiles
+    (16384, 256, False),    # 64 x 1 = 64 tiles: one wave
+    (19200, 256, True),     # 75 x 1 = 75 tiles > 74
+])
+def test_linear_decode_once_rule(monkeypatch, M, N, want):
+    """fp8_linear's choice between dequant-on-load and decode-once + 16-bit GEMM, for a
+    148-SM device (74 CTA pairs), without touching a GPU."""
+    import fp4_fp8_for_torch_mps.fp8_mps_native as nat
+    monkeypatch.setattr(nat, "_SM_COUNT", {0: 148})
+    assert nat.linear_decodes_once(M, N, torch.device("cuda", 0)) == want
